@@ -1,0 +1,320 @@
+"""Benchmark of the causal linear-attention hot path (forward + backward).
+
+Workload (per GPU): B=8, H=8, N=8192, d_head=64, bfloat16 inputs with float32
+accumulation; Q, K, V, dO ~ N(0,1) from a seed; a key-padding mask with
+per-sequence valid lengths drawn uniform in [N/2, N]; gamma == 1 (the plain
+normaliser form phi(q)S/(phi(q)z), clamp 1e-5). One step = one forward and
+one backward scan over the batch. Inputs (268 MB) exceed the 126 MB L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs the full per-GPU
+workload on its own batch (batch x head sharding, no collective in the
+path): weak scaling; time = max over ranks of the device-timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "sub-quadratic-audio-transformer-engine_b200"))
+
+B, H, N, D = 8, 8, 8192, 64
+METRIC = "linear-attn fwd+bwd tokens/sec (B=8,H=8,N=8192,d=64 per GPU)"
+UNIT = "tokens/s"
+CONFIG = {"workload": "causal ELU+1 linear attention fwd+bwd, B=8 H=8 N=8192 d_head=64, "
+                      "key-padding mask lengths U[N/2,N], gamma=1",
+          "batch_per_gpu": B, "heads": H, "seq_len": N, "head_dim": D,
+          "l2": "inputs 268 MB > 126 MB L2 (no flush needed)"}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--path", default="auto", choices=["auto", "exact", "tensorcore"])
+    return p.parse_args()
+
+
+# --------------------------------------------------------------------------
+# Reference CPU arm: the reference's own C++ engine (built from its sources
+# into oracle/_ref), forward + backward on one (b,h) head-sequence per task.
+# --------------------------------------------------------------------------
+def _ref_task(args):
+    seed, n, d = args
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))
+    import _C  # the reference's pybind module (CPU build)
+
+    rng = np.random.default_rng(seed)
+    q, k, v, do = (rng.standard_normal((1, n, d)).astype(np.float32) for _ in range(4))
+    eng = _C.SubQEngine(64 * 1024 * 1024)
+    t0 = time.perf_counter()
+    eng.forward(q, k, v, 1.0)
+    eng.backward(do, q, k, v, 1.0)
+    return time.perf_counter() - t0
+
+
+def cpu_reference(tasks_per_core=1, cores=None):
+    """Times the reference CPU path on a bounded sample; returns (tokens/s, info)."""
+    import multiprocessing as mp
+
+    ref_so = [f for f in os.listdir(os.path.join(REPO, "oracle", "_ref")) if f.startswith("_C")] \
+        if os.path.isdir(os.path.join(REPO, "oracle", "_ref")) else []
+    if not ref_so:
+        return None, {"unavailable": "oracle/_ref was not built"}
+    cores = cores or os.cpu_count() or 1
+    ntask = cores * tasks_per_core
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        pool.map(_ref_task, [(1, 256, D)] * cores)  # warm the workers
+        t0 = time.perf_counter()
+        pool.map(_ref_task, [(100 + i, N, D) for i in range(ntask)])
+        wall = time.perf_counter() - t0
+    # one (b,h) sequence of N tokens is 1/H of a token's work (a token has H heads)
+    tokens = ntask * N / H
+    return tokens / wall, {"kind": "reference", "cores": cores,
+                           "sample": f"{ntask} head-sequences (N={N}, d={D}) through the reference C++ "
+                                     f"SubQEngine.forward+backward (float32, one process per core), "
+                                     f"scaled to tokens of {H} heads",
+                           "wall_s": round(wall, 3)}
+
+
+# --------------------------------------------------------------------------
+def clocks_sampler(dev_index):
+    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    try:
+        return subprocess.Popen(["nvidia-smi", "-i", str(dev_index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except OSError:
+        return None
+
+
+def clocks_summary(proc):
+    if proc is None:
+        return None
+    proc.terminate()
+    try:
+        out, _ = proc.communicate(timeout=5)
+    except subprocess.TimeoutExpired:
+        proc.kill()
+        out, _ = proc.communicate()
+    sms, mx, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in out.strip().splitlines():
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 9:
+            continue
+        try:
+            sms.append(float(f[1]))
+            mx = float(f[2])
+        except ValueError:
+            continue
+        for n_, val in zip(names, f[5:9]):
+            if val.lower() == "active":
+                reasons.add(n_)
+    if not sms:
+        return None
+    return {"sm_mhz": statistics.median(sms), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return pk["hbm_gbs"], pk["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        # each "step" is one bounded sample of the workload on all host cores
+        vals = []
+        info = {}
+        for _ in range(max(1, args.warmup // 3)):
+            cpu_reference(tasks_per_core=1)
+        for _ in range(args.steps if args.steps <= 3 else 3):
+            v, info = cpu_reference(tasks_per_core=1)
+            if v is None:
+                print(json.dumps({"impl": "reference", "unavailable": info["unavailable"]}))
+                return 0
+            vals.append(v)
+        val = statistics.median(vals)
+        line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+                "steps": len(vals), "warmup": args.warmup, "ms_per_step": B * N / val * 1e3 * world,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": CONFIG,
+                "cpu_baseline": {"value": val, "unit": UNIT, **info},
+                "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    # The CPU-baseline pool starts (spawn) before the first GPU call.
+    cpu_val, cpu_info = (None, None)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_val, cpu_info = cpu_reference(tasks_per_core=1)
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dev = torch.device("cuda", local_rank if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    from subq_audio import ops
+
+    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    q, k, v, do = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16) for _ in range(4))
+    lens = torch.randint(N // 2, N + 1, (B,), generator=g)
+    mask = torch.arange(N)[None, :] < lens[:, None]
+    qd, kd, vd, dod, md = (x.to(dev) for x in (q, k, v, do, mask))
+    stream = torch.cuda.current_stream(dev)
+
+    def step(qq, kk, vv, dd, mm):
+        o, _ = ops.scan_forward(qq, kk, vv, mask=mm, normalize=True, path=args.path)
+        n_f = ops.last_launches()
+        dq, dk, dv, _ = ops.scan_backward(qq, kk, vv, dd, mask=mm, normalize=True, path=args.path)
+        return (o, dq, dk, dv), n_f + ops.last_launches()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident timing ----
+    for _ in range(args.warmup):
+        step(qd, kd, vd, dod, md)
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    sampler = clocks_sampler(dev.index) if rank == 0 else None
+    time.sleep(0.3 if sampler else 0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    e0.record(stream)
+    for _ in range(args.steps):
+        _, n_l = step(qd, kd, vd, dod, md)
+        launches += n_l
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    clk = clocks_summary(sampler)
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    tokens = B * N * world
+    value = tokens / (ms_max / 1e3)
+
+    # ---- per-kernel launch timing (forward and backward separately) ----
+    fe = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    reps = max(3, min(args.steps, 10))
+    fwd_ms = bwd_ms = 0.0
+    for _ in range(reps):
+        fe[0].record(stream)
+        ops.scan_forward(qd, kd, vd, mask=md, normalize=True, path=args.path)
+        fe[1].record(stream)
+        ops.scan_backward(qd, kd, vd, dod, mask=md, normalize=True, path=args.path)
+        fe[2].record(stream)
+        torch.cuda.synchronize(dev)
+        fwd_ms += fe[0].elapsed_time(fe[1]) / reps
+        bwd_ms += fe[1].elapsed_time(fe[2]) / reps
+    path_used = ops.last_path()
+
+    # ---- end-to-end through the public API with host buffers ----
+    hq, hk, hv, hdo, hm = (x.pin_memory() for x in (q, k, v, do, mask))
+    outs_h = [torch.empty((B, H, N, D), dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hdo, hm))
+    d2h = sum(x.numel() * x.element_size() for x in outs_h)
+
+    def e2e_step():
+        dq_, dk_, dv_, dd_, dm_ = (x.to(dev, non_blocking=True) for x in (hq, hk, hv, hdo, hm))
+        res, _ = step(dq_, dk_, dv_, dd_, dm_)
+        for src, dst in zip(res, outs_h):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(max(2, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0.record(stream)
+    e2e_steps = max(3, args.steps // 2)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t2 = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_val = tokens / (float(t2.item()) / 1e3)
+
+    if rank == 0:
+        hbm, tflops, src = peaks()
+        valid = float(lens.sum())  # live tokens per head across the batch
+        # algorithmic bytes (bf16, d=64): backward reads q,k,v,dO of live tokens and writes dq,dk,dv of all
+        bwd_bytes = H * (valid * 4 * D * 2 + B * N * 3 * D * 2)
+        fwd_bytes = H * (valid * 3 * D * 2 + B * N * D * 2)
+        dom = "bwd" if bwd_ms >= fwd_ms else "fwd"
+        dom_bytes, dom_ms = (bwd_bytes, bwd_ms) if dom == "bwd" else (fwd_bytes, fwd_ms)
+        achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+        tr = profile_traffic().get(f"{path_used}_{dom}")
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": {**CONFIG, "kernel_path": path_used},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_source": src,
+                         "traffic": (tr * 1.0 if tr is not None else None),
+                         "algorithmic_bytes": dom_bytes, "launch_ms": dom_ms},
+            "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
+            "tc_frac": (12 * D * D * B * H * N) / (ms_max / 1e3) / (tflops * 1e12),
+            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "clocks": clk,
+        }
+        if cpu_val is not None:
+            line["cpu_baseline"] = {"value": cpu_val, "unit": UNIT, **cpu_info}
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,258 @@
+// The C ABI (include/kernels.hpp): argument validation, workspace sizing,
+// kernel-path selection and launch. No exception crosses this boundary.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "kernels.hpp"
+#include "scan_common.cuh"
+#include "scan_launch.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int g_last_path = SUBQ_PATH_AUTO;
+thread_local int g_last_launches = 0;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int fail_cuda(cudaError_t err, const char* where) {
+    return fail(SUBQ_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(err));
+}
+
+size_t elem_size(int dtype) { return dtype == SUBQ_FP64 ? 8 : dtype == SUBQ_FP32 ? 4 : 2; }
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// Common checks of a scan description; fills the scalar part of ScanParams.
+int check_desc(const subq_scan_desc& d, subq::ScanParams& p) {
+    if (d.batch < 0 || d.heads < 0 || d.seq_len < 0)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "negative batch, heads or seq_len");
+    if (d.head_dim <= 0 || d.value_dim <= 0)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "head_dim and value_dim must be positive");
+    if (d.batch > 65535 || d.heads > 65535 || d.seq_len > (int64_t)1 << 30)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "batch/heads above 65535 or seq_len above 2^30");
+    if (d.head_dim > 256 || d.value_dim > 256)
+        return fail(SUBQ_ERR_UNSUPPORTED, "head_dim and value_dim above 256 are not supported");
+    if (d.dtype != SUBQ_FP32 && d.dtype != SUBQ_FP16 && d.dtype != SUBQ_BF16 && d.dtype != SUBQ_FP64)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "unknown dtype");
+    if (d.decay_mode < SUBQ_DECAY_NONE || d.decay_mode > SUBQ_DECAY_PER_TOKEN)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "unknown decay_mode");
+    if ((d.decay_mode == SUBQ_DECAY_PER_HEAD || d.decay_mode == SUBQ_DECAY_PER_TOKEN) && !d.log_gamma)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "log_gamma pointer required by decay_mode");
+    if (d.path < SUBQ_PATH_AUTO || d.path > SUBQ_PATH_TENSORCORE)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "unknown kernel path");
+    if (!(d.clamp_min >= 0.f))
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "clamp_min must be >= 0");
+    memset(&p, 0, sizeof(p));
+    p.B = (int)d.batch; p.H = (int)d.heads; p.N = (int)d.seq_len;
+    p.d = (int)d.head_dim; p.e = (int)d.value_dim;
+    p.normalize = d.normalize ? 1 : 0;
+    p.scale = d.scale;
+    p.clamp_min = d.clamp_min;
+    p.decay_mode = d.decay_mode;
+    p.lg_scalar = d.log_gamma_scalar;
+    p.log_gamma = d.log_gamma;
+    p.mask = d.mask;
+    p.mask_sb = d.mask ? d.mask_stride_b : 0;
+    p.flush = d.flush_subnormal ? 1 : 0;
+    return SUBQ_OK;
+}
+
+// `empty`: the call touches no element (B, H or N is 0), so a null pointer is fine.
+int check_tensor(const subq_tensor4& t, const char* name, int dtype, bool empty) {
+    if (!t.data && !empty) return fail(SUBQ_ERR_INVALID_ARGUMENT, std::string(name) + " is null");
+    if (reinterpret_cast<uintptr_t>(t.data) % elem_size(dtype) != 0)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, std::string(name) + " is not aligned to its element size");
+    if (t.stride_b < 0 || t.stride_h < 0 || t.stride_n < 0)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, std::string(name) + " has a negative stride");
+    return SUBQ_OK;
+}
+
+bool use_tc(const subq::ScanParams& p, int dtype, int path) {
+    if (path == SUBQ_PATH_EXACT || dtype == SUBQ_FP64) return false;
+    return subq::tc_supported(p, dtype);
+}
+
+int fill_fwd(const subq_fwd_args* a, subq::ScanParams& p) {
+    if (!a) return fail(SUBQ_ERR_INVALID_ARGUMENT, "null argument block");
+    int rc = check_desc(a->desc, p);
+    if (rc) return rc;
+    const int dt = a->desc.dtype;
+    const bool empty = p.B == 0 || p.H == 0 || p.N == 0;
+    if ((rc = check_tensor(a->q, "q", dt, empty)) || (rc = check_tensor(a->k, "k", dt, empty)) ||
+        (rc = check_tensor(a->v, "v", dt, empty)) || (rc = check_tensor(a->o, "o", dt, empty)))
+        return rc;
+    p.q = a->q.data; p.q_sb = a->q.stride_b; p.q_sh = a->q.stride_h; p.q_sn = a->q.stride_n;
+    p.k = a->k.data; p.k_sb = a->k.stride_b; p.k_sh = a->k.stride_h; p.k_sn = a->k.stride_n;
+    p.v = a->v.data; p.v_sb = a->v.stride_b; p.v_sh = a->v.stride_h; p.v_sn = a->v.stride_n;
+    p.o = a->o.data; p.o_sb = a->o.stride_b; p.o_sh = a->o.stride_h; p.o_sn = a->o.stride_n;
+    p.S_in = a->state_in; p.z_in = a->norm_in;
+    p.S_out = a->state_out; p.z_out = a->norm_out;
+    return SUBQ_OK;
+}
+
+int fill_bwd(const subq_bwd_args* a, subq::ScanParams& p) {
+    if (!a) return fail(SUBQ_ERR_INVALID_ARGUMENT, "null argument block");
+    int rc = check_desc(a->desc, p);
+    if (rc) return rc;
+    const int dt = a->desc.dtype;
+    const bool empty = p.B == 0 || p.H == 0 || p.N == 0;
+    if ((rc = check_tensor(a->q, "q", dt, empty)) || (rc = check_tensor(a->k, "k", dt, empty)) ||
+        (rc = check_tensor(a->v, "v", dt, empty)) || (rc = check_tensor(a->dout, "dout", dt, empty)) ||
+        (rc = check_tensor(a->dq, "dq", dt, empty)) || (rc = check_tensor(a->dk, "dk", dt, empty)) ||
+        (rc = check_tensor(a->dv, "dv", dt, empty)))
+        return rc;
+    if (empty) return SUBQ_OK;
+    const void* ins[] = {a->q.data, a->k.data, a->v.data, a->dout.data};
+    const void* outs[] = {a->dq.data, a->dk.data, a->dv.data};
+    for (const void* in : ins)
+        for (const void* out : outs)
+            if (in == out)
+                return fail(SUBQ_ERR_ALIAS,
+                            "subquadratic_attention_backward: gradient outputs must not alias inputs");
+    if (a->dq.data == a->dk.data || a->dq.data == a->dv.data || a->dk.data == a->dv.data)
+        return fail(SUBQ_ERR_ALIAS, "gradient outputs must be distinct buffers");
+    p.q = a->q.data; p.q_sb = a->q.stride_b; p.q_sh = a->q.stride_h; p.q_sn = a->q.stride_n;
+    p.k = a->k.data; p.k_sb = a->k.stride_b; p.k_sh = a->k.stride_h; p.k_sn = a->k.stride_n;
+    p.v = a->v.data; p.v_sb = a->v.stride_b; p.v_sh = a->v.stride_h; p.v_sn = a->v.stride_n;
+    p.g = a->dout.data; p.g_sb = a->dout.stride_b; p.g_sh = a->dout.stride_h; p.g_sn = a->dout.stride_n;
+    p.o = a->dq.data; p.o_sb = a->dq.stride_b; p.o_sh = a->dq.stride_h; p.o_sn = a->dq.stride_n;
+    p.dk = a->dk.data; p.dk_sb = a->dk.stride_b; p.dk_sh = a->dk.stride_h; p.dk_sn = a->dk.stride_n;
+    p.dv = a->dv.data; p.dv_sb = a->dv.stride_b; p.dv_sh = a->dv.stride_h; p.dv_sn = a->dv.stride_n;
+    p.S_in = a->state_in; p.z_in = a->norm_in;
+    p.dlg = a->dlog_gamma;
+    return SUBQ_OK;
+}
+
+size_t exact_bwd_ws(const subq::ScanParams& p, int dtype) {
+    return align_up(elem_size(dtype == SUBQ_FP64 ? SUBQ_FP64 : SUBQ_FP32) * 3 * (size_t)p.B * p.H * (size_t)p.N);
+}
+
+int check_workspace(void* ws, size_t have, size_t need) {
+    if (need == 0) return SUBQ_OK;
+    if (!ws) return fail(SUBQ_ERR_WORKSPACE, "workspace required: " + std::to_string(need) + " bytes");
+    if (have < need)
+        return fail(SUBQ_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) +
+                                            " bytes, got " + std::to_string(have));
+    if (reinterpret_cast<uintptr_t>(ws) % kAlign != 0)
+        return fail(SUBQ_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    return SUBQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int subq_abi_version(void) { return SUBQ_ABI_VERSION; }
+
+const char* subq_last_error(void) { return g_last_error.c_str(); }
+
+int subq_last_path(void) { return g_last_path; }
+
+int subq_last_launches(void) { return g_last_launches; }
+
+size_t subq_fwd_workspace_bytes(const subq_fwd_args* a) {
+    subq::ScanParams p;
+    if (fill_fwd(a, p) != SUBQ_OK) return 0;
+    if (use_tc(p, a->desc.dtype, a->desc.path)) return subq::tc_fwd_workspace_bytes(p);
+    return 0;
+}
+
+size_t subq_bwd_workspace_bytes(const subq_bwd_args* a) {
+    subq::ScanParams p;
+    if (fill_bwd(a, p) != SUBQ_OK) return 0;
+    if (use_tc(p, a->desc.dtype, a->desc.path)) return subq::tc_bwd_workspace_bytes(p);
+    return exact_bwd_ws(p, a->desc.dtype);
+}
+
+int subq_fwd(const subq_fwd_args* a) {
+    subq::ScanParams p;
+    int rc = fill_fwd(a, p);
+    if (rc) return rc;
+    const bool tc = use_tc(p, a->desc.dtype, a->desc.path);
+    if (a->desc.path == SUBQ_PATH_TENSORCORE && !tc)
+        return fail(SUBQ_ERR_UNSUPPORTED, "tensor-core path needs bf16/fp16 with head_dim = value_dim = 64");
+    if (p.B == 0 || p.H == 0) {
+        g_last_path = tc ? SUBQ_PATH_TENSORCORE : SUBQ_PATH_EXACT;
+        g_last_launches = 0;
+        return SUBQ_OK;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(a->stream);
+    cudaError_t err;
+    int launches = 0;
+    if (tc) {
+        const size_t need = subq::tc_fwd_workspace_bytes(p);
+        if ((rc = check_workspace(a->workspace, a->workspace_bytes, need))) return rc;
+        p.ws = static_cast<float*>(a->workspace);
+        err = subq::launch_fwd_tc(p, a->desc.dtype, st, &launches);
+    } else {
+        err = subq::launch_fwd_exact(p, a->desc.dtype, st);
+        launches = 1;
+    }
+    if (err != cudaSuccess) return fail_cuda(err, "subq_fwd launch");
+    g_last_path = tc ? SUBQ_PATH_TENSORCORE : SUBQ_PATH_EXACT;
+    g_last_launches = launches;
+    return SUBQ_OK;
+}
+
+int subq_bwd(const subq_bwd_args* a) {
+    subq::ScanParams p;
+    int rc = fill_bwd(a, p);
+    if (rc) return rc;
+    const bool tc = use_tc(p, a->desc.dtype, a->desc.path);
+    if (a->desc.path == SUBQ_PATH_TENSORCORE && !tc)
+        return fail(SUBQ_ERR_UNSUPPORTED, "tensor-core path needs bf16/fp16 with head_dim = value_dim = 64");
+    if (!tc && subq::exact_bwd_smem_bytes(p.d, p.e, p.normalize, a->desc.dtype == SUBQ_FP64 ? 8 : 4) > 220 * 1024)
+        return fail(SUBQ_ERR_UNSUPPORTED, "backward state d x (e+1) does not fit in shared memory");
+    if (p.B == 0 || p.H == 0 || p.N == 0) {
+        g_last_path = tc ? SUBQ_PATH_TENSORCORE : SUBQ_PATH_EXACT;
+        g_last_launches = 0;
+        return SUBQ_OK;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(a->stream);
+    cudaError_t err;
+    int launches = 0;
+    const size_t need = tc ? subq::tc_bwd_workspace_bytes(p) : exact_bwd_ws(p, a->desc.dtype);
+    if ((rc = check_workspace(a->workspace, a->workspace_bytes, need))) return rc;
+    p.ws = static_cast<float*>(a->workspace);
+    if (tc) {
+        err = subq::launch_bwd_tc(p, a->desc.dtype, st, &launches);
+    } else {
+        err = subq::launch_bwd_exact(p, a->desc.dtype, st);
+        launches = 1;
+    }
+    if (err != cudaSuccess) return fail_cuda(err, "subq_bwd launch");
+    g_last_path = tc ? SUBQ_PATH_TENSORCORE : SUBQ_PATH_EXACT;
+    g_last_launches = launches;
+    return SUBQ_OK;
+}
+
+int subq_feature_map(void* x, int64_t n, int32_t dtype, void* stream) {
+    if (n < 0) return fail(SUBQ_ERR_INVALID_ARGUMENT, "negative element count");
+    if (n > 0 && !x) return fail(SUBQ_ERR_INVALID_ARGUMENT, "x is null");
+    if (dtype != SUBQ_FP32 && dtype != SUBQ_FP16 && dtype != SUBQ_BF16)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "subq_feature_map supports float32, float16 and bfloat16");
+    cudaError_t err = subq::launch_feature_map(x, n, dtype, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail_cuda(err, "subq_feature_map launch");
+    g_last_launches = n > 0 ? 1 : 0;
+    return SUBQ_OK;
+}
+
+int subq_device_info(int device, char* arch, size_t arch_len, size_t* memory_bytes, int* bf16_supported) {
+    cudaDeviceProp prop;
+    cudaError_t err = cudaGetDeviceProperties(&prop, device);
+    if (err != cudaSuccess) return fail_cuda(err, "cudaGetDeviceProperties");
+    if (arch && arch_len) snprintf(arch, arch_len, "SM %d.%d", prop.major, prop.minor);
+    if (memory_bytes) *memory_bytes = prop.totalGlobalMem;
+    if (bf16_supported) *bf16_supported = prop.major >= 8 ? 1 : 0;
+    return SUBQ_OK;
+}
+
+}  // extern "C"

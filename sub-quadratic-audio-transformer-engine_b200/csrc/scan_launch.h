@@ -1,0 +1,27 @@
+// Host-side launchers of the scan kernels (internal to libsubq_b200).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace subq {
+
+struct ScanParams;
+
+// Exact float32 path (scan_simt.cu).
+size_t exact_bwd_smem_bytes(int d, int e, int normalize, size_t acc_bytes);
+cudaError_t launch_fwd_exact(const ScanParams& p, int dtype, cudaStream_t st);
+cudaError_t launch_bwd_exact(const ScanParams& p, int dtype, cudaStream_t st);
+cudaError_t launch_feature_map(void* x, int64_t n, int dtype, cudaStream_t st);
+
+// Tensor-core path (scan_tc.cu).
+bool tc_supported(const ScanParams& p, int dtype);
+size_t tc_fwd_workspace_bytes(const ScanParams& p);
+size_t tc_bwd_workspace_bytes(const ScanParams& p);
+// Returns the number of kernel launches issued through *launches.
+cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches);
+cudaError_t launch_bwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches);
+// Device-side status word of the tensor-core kernels (bounded waits).
+cudaError_t tc_read_status(cudaStream_t st, int* status);
+
+}  // namespace subq

@@ -1,0 +1,378 @@
+"""Linear-attention autograd surface of subq_audio, on the B200 kernels.
+
+Same public names, signatures and semantics as the reference's
+python/subq_audio/autograd.py: ``feature_map``, ``feature_map_prime``,
+``chunkwise_flash_linear_attention`` (:379-438), ``SubQAttentionFunction``
+(:547-660), ``SubQLinearAttention`` (:663-772). The scan itself runs in the
+CUDA kernels of libsubq_b200.so; there is no torch fallback, and CPU tensors
+are staged through the GPU.
+
+Differences a caller can see:
+  * the carried state S (and S.Z) is float32 whatever the input dtype (the
+    reference keeps it in q.dtype, where a float16 Z overflows past ~65k
+    tokens);
+  * ``chunk_size`` is accepted for compatibility; the kernels choose their
+    own tiling, and results do not depend on it beyond float rounding.
+"""
+from __future__ import annotations
+
+import math
+from typing import Any, Optional, Tuple, Union
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+
+StateLike = Optional[Union[torch.Tensor, Tuple[torch.Tensor, ...]]]
+
+
+def feature_map(x: torch.Tensor) -> torch.Tensor:
+    """phi(x) = ELU(x) + 1 (positive feature map)."""
+    return F.elu(x) + 1.0
+
+
+def feature_map_prime(x: torch.Tensor) -> torch.Tensor:
+    """phi'(x) = 1 for x > 0 else exp(x)."""
+    return torch.where(x > 0.0, torch.ones_like(x), torch.exp(x))
+
+
+def rotate_half(x: torch.Tensor) -> torch.Tensor:
+    x1 = x[..., : x.shape[-1] // 2]
+    x2 = x[..., x.shape[-1] // 2:]
+    return torch.cat((-x2, x1), dim=-1)
+
+
+def apply_rotary_pos_emb(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                         unsqueeze_dim: int = 1) -> Tuple[torch.Tensor, torch.Tensor]:
+    if cos.ndim == 3 and q.ndim == 4:
+        cos = cos.unsqueeze(unsqueeze_dim)
+        sin = sin.unsqueeze(unsqueeze_dim)
+    return (q * cos) + (rotate_half(q) * sin), (k * cos) + (rotate_half(k) * sin)
+
+
+def _normalize_attention_mask(attention_mask: Optional[torch.Tensor], target_dtype: torch.dtype,
+                              target_len: int) -> Optional[torch.Tensor]:
+    """2-D/3-D/4-D bool/int/float mask -> active-token mask [B, 1, T, 1].
+
+    Rules of the reference (autograd.py:57-105): bool as is; float masks are
+    additive (< -1 means masked) or multiplicative (> 0 means live); a 4-D
+    mask marks a token live when it is a live query and a live key.
+    """
+    if attention_mask is None:
+        return None
+    m = attention_mask
+    if m.dtype == torch.bool:
+        valid = m.to(dtype=target_dtype)
+    elif torch.is_floating_point(m):
+        valid = ((m >= -1.0) if bool((m < -1.0).any()) else (m > 0.0)).to(dtype=target_dtype)
+    else:
+        valid = (m != 0).to(dtype=target_dtype)
+    if valid.ndim == 2:
+        return valid[:, None, :, None]
+    if valid.ndim == 3:
+        if valid.shape[1] == 1 and valid.shape[2] == target_len:
+            return valid.unsqueeze(-1)
+        if valid.shape[2] == 1 and valid.shape[1] == target_len:
+            return valid.unsqueeze(1)
+        red = (valid.sum(dim=-1, keepdim=True) > 0).to(dtype=target_dtype)
+        return red.unsqueeze(1) if red.shape[1] == target_len else red
+    if valid.ndim == 4:
+        if valid.shape[-2] != valid.shape[-1]:
+            raise ValueError(f"4D attention_mask must be square [B, 1|H, T, T]; got {tuple(valid.shape)}")
+        live_q = valid.sum(dim=-1) > 0
+        live_k = valid.sum(dim=-2) > 0
+        out = (live_q & live_k).to(dtype=target_dtype).unsqueeze(-1)
+        return out[:, :1] if out.shape[1] > 1 else out
+    return valid
+
+
+def _token_mask(valid_mask: Optional[torch.Tensor], B: int, T: int, device) -> Optional[torch.Tensor]:
+    """[B,1,T,1] active mask -> [B, T] uint8 for the kernels."""
+    if valid_mask is None:
+        return None
+    m = valid_mask.reshape(valid_mask.shape[0], -1)[:, :T] if valid_mask.ndim != 4 else valid_mask[:, 0, :, 0]
+    m = m.expand(B, T)
+    return (m != 0).to(device=device, dtype=torch.uint8).contiguous()
+
+
+def _log_gamma(decay_w: Any, B: int, H: int, T: int, device, dtype=torch.float32):
+    """``-softplus(-w)`` in the reference's broadcast layout (autograd.py:310-333).
+
+    Returns None for "no decay" (w is None), else a differentiable float32
+    tensor of shape [] / [H] / [B,H,T].
+    """
+    if decay_w is None:
+        return None
+    w = decay_w if isinstance(decay_w, torch.Tensor) else torch.tensor(decay_w, device=device)
+    w = w.to(device=device, dtype=dtype)
+    lg = -F.softplus(-w)
+    if w.ndim == 0:
+        return lg
+    if w.ndim == 1:
+        if w.shape[0] == H:
+            return lg
+        return lg.view(1, 1, -1).expand(B, H, T)
+    if w.ndim == 2:
+        if w.shape[1] == T:
+            return lg.view(B, 1, T).expand(B, H, T)
+        return lg.view(B, H, 1).expand(B, H, T)
+    if w.ndim == 3 and tuple(w.shape) == (B, H, T):
+        return lg
+    return lg.expand(B, H, T)
+
+
+def _split_state(past_state: StateLike):
+    if past_state is None:
+        return None
+    if isinstance(past_state, tuple):
+        S = past_state[0]
+        Z = past_state[1] if len(past_state) > 1 else None
+    else:
+        S = past_state
+        Z = getattr(past_state, "Z", None)
+    return (S, Z)
+
+
+class _CausalScan(torch.autograd.Function):
+    """One causal scan direction on the kernels; differentiable in q, k, v, log_gamma."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lg, mask_u8, state, want_state):
+        o, st = ops.scan_forward(q, k, v, log_gamma=lg, mask=mask_u8, normalize=True, state=state,
+                                 return_state=want_state)
+        ctx.save_for_backward(q, k, v, lg if isinstance(lg, torch.Tensor) else None, mask_u8)
+        ctx.lg_is_tensor = isinstance(lg, torch.Tensor)
+        ctx.state = state
+        if want_state:
+            ctx.mark_non_differentiable(st[0], st[1])
+            return o, st[0], st[1]
+        return o, None, None
+
+    @staticmethod
+    def backward(ctx, do, _dS=None, _dz=None):
+        q, k, v, lg, mask_u8 = ctx.saved_tensors
+        need_lg = ctx.lg_is_tensor and ctx.needs_input_grad[3]
+        dq, dk, dv, dlg = ops.scan_backward(q, k, v, do.contiguous(), log_gamma=lg, mask=mask_u8,
+                                            normalize=True, state=ctx.state, need_dlog_gamma=need_lg)
+        glg = None
+        if need_lg:
+            glg = dlg.to(lg.dtype)
+            if lg.dim() == 0:
+                glg = glg.sum()
+            elif lg.dim() == 1:
+                glg = glg.sum(dim=(0, 2))
+        return dq, dk, dv, glg, None, None, None
+
+
+def _to_device_inputs(q, k, v):
+    if q.is_cuda:
+        return q, k, v, None
+    if not torch.cuda.is_available():
+        raise RuntimeError("subq_audio needs a CUDA device: the scan runs only in its B200 kernels")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    return q.to(dev), k.to(dev), v.to(dev), q.device
+
+
+def _single_direction(q, k, v, decay_w, past_state, valid_mask, want_state):
+    B, H, T, D = q.shape
+    lg = _log_gamma(decay_w, B, H, T, q.device)
+    mask_u8 = _token_mask(valid_mask, B, T, q.device)
+    st = _split_state(past_state)
+    if st is not None:
+        S, Z = st
+        S = S.to(device=q.device, dtype=torch.float32)
+        Z = None if Z is None else Z.to(device=q.device, dtype=torch.float32).reshape(B, H, D)
+        st = (S, Z)
+    o, S_next, z_next = _CausalScan.apply(q, k, v, lg, mask_u8, st, want_state)
+    return o, S_next, z_next
+
+
+def chunkwise_flash_linear_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, decay_w: Any,
+                                     past_state: StateLike = None, chunk_size: int = 64,
+                                     attention_mask: Optional[torch.Tensor] = None,
+                                     is_causal: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Normalised ELU+1 linear attention (reference autograd.py:379-438).
+
+    ``q, k, v`` are [B,T,D] or [B,H,T,D]; ``decay_w`` is the decay logit
+    (gamma = sigmoid(w)) as a scalar, [H], [B,T], [B,H] or [B,H,T], or None
+    for gamma == 1. Returns ``(out, S_next)`` with ``S_next.Z`` attached.
+    """
+    is_3d = q.ndim == 3
+    if is_3d:
+        q, k, v = q.unsqueeze(1), k.unsqueeze(1), v.unsqueeze(1)
+    q, k, v, home = _to_device_inputs(q, k, v)
+    B, H, T, D = q.shape
+    valid_mask = _normalize_attention_mask(
+        attention_mask.to(q.device) if attention_mask is not None else None, q.dtype, T)
+    out, S_next, z_next = _single_direction(q, k, v, decay_w, past_state, valid_mask, True)
+    if not is_causal:
+        # Bidirectional: add the reversed-time scan and remove the double-counted
+        # diagonal (in normalised linear attention the self term is v).
+        flip = lambda x: torch.flip(x, dims=[2])  # noqa: E731
+        w_rev = torch.flip(decay_w, dims=[-1]) if isinstance(decay_w, torch.Tensor) and decay_w.ndim >= 2 else decay_w
+        vm_rev = torch.flip(valid_mask, dims=[2]) if valid_mask is not None else None
+        out_b, _, _ = _single_direction(flip(q), flip(k), flip(v), w_rev, None, vm_rev, False)
+        diag = v if valid_mask is None else v * valid_mask.expand_as(v)
+        out = out + flip(out_b) - diag
+        if valid_mask is not None:
+            out = out * valid_mask.expand_as(out)
+    S_next = S_next.to(q.device)
+    S_next.Z = z_next.unsqueeze(-1)
+    if is_3d:
+        out = out.squeeze(1)
+    if home is not None:
+        out = out.to(home)
+    return out.contiguous(), S_next
+
+
+def _reduce_dw(dlg: torch.Tensor, w: torch.Tensor, B: int, H: int, T: int) -> torch.Tensor:
+    """d loss / d w from the per-token d loss / d log(gamma) (reference autograd.py:526-542)."""
+    sg = torch.sigmoid(-w.to(torch.float32))
+    if w.ndim == 0:
+        return (dlg * sg).sum()
+    if w.ndim == 1:
+        if w.shape[0] == H:
+            return (dlg * sg.view(1, H, 1)).sum(dim=(0, 2))
+        return (dlg * sg.view(1, 1, -1)).sum(dim=(0, 1))
+    if w.ndim == 2:
+        if w.shape[1] == T:
+            return (dlg * sg.view(B, 1, T)).sum(dim=1)
+        return (dlg * sg.view(B, H, 1)).sum(dim=-1)
+    if w.ndim == 3:
+        return dlg * sg
+    return dlg.sum()
+
+
+def _direction_grads(q, k, v, w, do, valid_mask):
+    B, H, T, D = q.shape
+    lg = None if w is None else _log_gamma(w.detach(), B, H, T, q.device)
+    mask_u8 = _token_mask(valid_mask, B, T, q.device)
+    dq, dk, dv, dlg = ops.scan_backward(q, k, v, do.contiguous(), log_gamma=lg, mask=mask_u8, normalize=True,
+                                        need_dlog_gamma=w is not None)
+    dw = None if w is None else _reduce_dw(dlg, w, B, H, T)
+    return dq, dk, dv, dw
+
+
+class SubQAttentionFunction(torch.autograd.Function):
+    """Analytic autograd bridge (reference autograd.py:547-660).
+
+    ``apply(q, k, v, decay_w, chunk_size=64, attention_mask=None, is_causal=True)``.
+    Saves exactly (q, k, v, decay_w): the backward recomputes the forward
+    states in the kernels, so memory stays O(inputs).
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, decay_w, chunk_size: int = 64, attention_mask=None, is_causal: bool = True):
+        if q.shape != k.shape or q.shape != v.shape:
+            raise ValueError(f"Shape mismatch: Q:{q.shape}, K:{k.shape}, V:{v.shape}")
+        with torch.no_grad():
+            out, _ = chunkwise_flash_linear_attention(q, k, v, decay_w, chunk_size=chunk_size,
+                                                      attention_mask=attention_mask, is_causal=is_causal)
+        w_t = decay_w if isinstance(decay_w, torch.Tensor) else torch.tensor(decay_w, dtype=q.dtype, device=q.device)
+        ctx.save_for_backward(q, k, v, w_t)
+        ctx.is_3d = q.ndim == 3
+        ctx.is_causal = is_causal
+        ctx.decay_none = decay_w is None
+        T = q.shape[-2]
+        ctx.valid_mask = (_normalize_attention_mask(attention_mask, q.dtype, T)
+                          if attention_mask is not None else None)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, w = ctx.saved_tensors
+        home = None
+        if not q.is_cuda:
+            home = q.device
+        q4, k4, v4, g4 = (x.unsqueeze(1) if ctx.is_3d else x for x in (q, k, v, grad_output))
+        q4, k4, v4, _ = _to_device_inputs(q4, k4, v4)
+        g4 = g4.to(q4.device)
+        w_dev = None if ctx.decay_none else w.to(q4.device)
+        vm = ctx.valid_mask.to(q4.device) if ctx.valid_mask is not None else None
+        dQ, dK, dV, dw = _direction_grads(q4, k4, v4, w_dev, g4, vm)
+        if not ctx.is_causal:
+            flip = lambda x: torch.flip(x, dims=[2])  # noqa: E731
+            w_rev = (torch.flip(w_dev, dims=[-1]) if w_dev is not None and w_dev.ndim >= 2 else w_dev)
+            vm_rev = flip(vm) if vm is not None else None
+            dQb, dKb, dVb, dwb = _direction_grads(flip(q4), flip(k4), flip(v4), w_rev, flip(g4), vm_rev)
+            g_m = g4 if vm is None else g4 * vm.expand_as(g4)
+            dQ = dQ + flip(dQb)
+            dK = dK + flip(dKb)
+            dV = dV + flip(dVb) - g_m
+            if dw is not None:
+                dw = dw + (torch.flip(dwb, dims=[-1]) if w_dev.ndim >= 2 else dwb)
+        if ctx.is_3d:
+            dQ, dK, dV = dQ.squeeze(1), dK.squeeze(1), dV.squeeze(1)
+        dw_out = None if dw is None else dw.to(w.dtype).reshape(w.shape)
+        grads = [dQ.contiguous(), dK.contiguous(), dV.contiguous(), dw_out]
+        if home is not None:
+            grads = [g.to(home) if g is not None else None for g in grads]
+        return tuple(grads) + (None, None, None)
+
+
+class SubQLinearAttention(nn.Module):
+    """Linear-attention layer (reference autograd.py:663-772): q/k/v/out
+    projections, optional RoPE, GQA, learnable base decay with optional
+    data-dependent gating, per-head RMSNorm. The scan is the B200 kernel.
+    """
+
+    def __init__(self, hidden_size: int, num_heads: int = 1, num_key_value_heads: Optional[int] = None,
+                 decay_init: float = 0.99, bias: bool = False, use_data_dependent_gating: bool = True,
+                 is_causal: bool = True):
+        super().__init__()
+        self.hidden_size = hidden_size
+        self.num_heads = num_heads
+        self.num_key_value_heads = num_key_value_heads if num_key_value_heads is not None else num_heads
+        self.head_dim = hidden_size // num_heads
+        self.num_key_value_groups = self.num_heads // self.num_key_value_heads
+        self.use_data_dependent_gating = use_data_dependent_gating
+        self.is_causal = is_causal
+        if self.head_dim * num_heads != hidden_size:
+            raise ValueError(f"hidden_size {hidden_size} must be divisible by num_heads {num_heads}")
+        if self.num_heads % self.num_key_value_heads != 0:
+            raise ValueError(f"num_heads {num_heads} must be divisible by num_key_value_heads "
+                             f"{self.num_key_value_heads}")
+        self.q_proj = nn.Linear(hidden_size, hidden_size, bias=bias)
+        self.k_proj = nn.Linear(hidden_size, self.num_key_value_heads * self.head_dim, bias=bias)
+        self.v_proj = nn.Linear(hidden_size, self.num_key_value_heads * self.head_dim, bias=bias)
+        self.out_proj = nn.Linear(hidden_size, hidden_size, bias=bias)
+        self.head_norm = nn.RMSNorm(self.head_dim, eps=1e-5) if hasattr(nn, "RMSNorm") else None
+        d0 = min(max(decay_init, 1e-4), 1.0 - 1e-4)
+        self.raw_decay = nn.Parameter(torch.full((num_heads,), math.log(d0 / (1.0 - d0)), dtype=torch.float32))
+        self.gate_proj = nn.Linear(hidden_size, num_heads, bias=bias) if use_data_dependent_gating else None
+
+    @property
+    def decay_factor(self) -> torch.Tensor:
+        return torch.sigmoid(self.raw_decay)
+
+    def forward(self, hidden_states: torch.Tensor, past_state: StateLike = None,
+                attention_mask: Optional[torch.Tensor] = None, use_cache: bool = False,
+                position_embeddings: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, **kwargs: Any):
+        B, L, _ = hidden_states.shape
+        Q = self.q_proj(hidden_states).view(B, L, self.num_heads, self.head_dim).transpose(1, 2)
+        K = self.k_proj(hidden_states).view(B, L, self.num_key_value_heads, self.head_dim).transpose(1, 2)
+        V = self.v_proj(hidden_states).view(B, L, self.num_key_value_heads, self.head_dim).transpose(1, 2)
+        if position_embeddings is not None:
+            cos, sin = position_embeddings
+            Q, K = apply_rotary_pos_emb(Q, K, cos, sin)
+        if self.num_key_value_groups > 1:
+            K = K.repeat_interleave(self.num_key_value_groups, dim=1)
+            V = V.repeat_interleave(self.num_key_value_groups, dim=1)
+        if self.use_data_dependent_gating and self.gate_proj is not None:
+            gate = self.gate_proj(hidden_states).transpose(1, 2)
+            decay_w = self.raw_decay.view(1, self.num_heads, 1) + gate
+        else:
+            decay_w = self.raw_decay
+        out, next_state = chunkwise_flash_linear_attention(Q, K, V, decay_w, past_state=past_state,
+                                                           attention_mask=attention_mask, is_causal=self.is_causal)
+        if self.head_norm is not None:
+            out = self.head_norm(out)
+        else:
+            out = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + 1e-5)
+        out = out.transpose(1, 2).contiguous().view(B, L, self.hidden_size)
+        return self.out_proj(out), (next_state if use_cache else None)
+
+
+SubQuadraticAttention = SubQLinearAttention

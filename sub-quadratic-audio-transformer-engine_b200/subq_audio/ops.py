@@ -1,0 +1,202 @@
+"""Torch-facing launchers of the B200 scan kernels (through the C ABI).
+
+Tensors are [B, H, N, D] CUDA tensors (any strides with a contiguous last
+dimension). Computation is stream-ordered on torch's current stream; the
+only host work is argument packing. There is no CPU path: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple, Union
+
+import torch
+
+from . import _capi
+
+_DTYPES = {torch.float32: _capi.SUBQ_FP32, torch.float16: _capi.SUBQ_FP16, torch.bfloat16: _capi.SUBQ_BF16,
+           torch.float64: _capi.SUBQ_FP64}
+_PATHS = {"auto": _capi.SUBQ_PATH_AUTO, "exact": _capi.SUBQ_PATH_EXACT, "tensorcore": _capi.SUBQ_PATH_TENSORCORE}
+
+LogGamma = Union[None, float, torch.Tensor]
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda):
+            raise RuntimeError("subq_audio scan kernels run on CUDA tensors only (there is no CPU path)")
+
+
+def _t4(t: Optional[torch.Tensor]) -> _capi.Tensor4:
+    out = _capi.Tensor4()
+    if t is None:
+        return out
+    if t.dim() != 4:
+        raise ValueError(f"expected a [B, H, N, D] tensor, got shape {tuple(t.shape)}")
+    sb, sh, sn, sd = t.stride()
+    if sd != 1 and t.shape[-1] > 1:
+        raise ValueError("the last dimension must be contiguous")
+    out.data = t.data_ptr()
+    out.stride_b, out.stride_h, out.stride_n = sb, sh, sn
+    return out
+
+
+def _inner_contig(t: torch.Tensor) -> torch.Tensor:
+    return t if (t.shape[-1] <= 1 or t.stride(-1) == 1) else t.contiguous()
+
+
+def _desc(q: torch.Tensor, v: torch.Tensor, log_gamma: LogGamma, mask: Optional[torch.Tensor],
+          normalize: bool, scale: Optional[float], clamp_min: float, flush_subnormal: bool,
+          path: str, keep: list) -> _capi.ScanDesc:
+    B, H, N, d = q.shape
+    desc = _capi.ScanDesc()
+    desc.batch, desc.heads, desc.seq_len, desc.head_dim, desc.value_dim = B, H, N, d, v.shape[-1]
+    if q.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {q.dtype}; use float32, float16, bfloat16 or float64")
+    desc.dtype = _DTYPES[q.dtype]
+    desc.normalize = 1 if normalize else 0
+    desc.scale = float(scale) if scale is not None else (1.0 / math.sqrt(d) if normalize else 1.0)
+    desc.clamp_min = float(clamp_min)
+    desc.flush_subnormal = 1 if flush_subnormal else 0
+    desc.path = _PATHS[path]
+    if log_gamma is None:
+        desc.decay_mode = _capi.SUBQ_DECAY_NONE
+    elif isinstance(log_gamma, (float, int)):
+        desc.decay_mode = _capi.SUBQ_DECAY_SCALAR
+        desc.log_gamma_scalar = float(log_gamma)
+    else:
+        lg = log_gamma.detach()
+        if lg.device != q.device:
+            raise ValueError("log_gamma must be on the device of q")
+        lg = lg.to(torch.float32)
+        if lg.dim() == 0:
+            lg = lg.reshape(1).expand(H)
+        if lg.dim() == 1 and lg.shape[0] == H:
+            desc.decay_mode = _capi.SUBQ_DECAY_PER_HEAD
+        else:
+            lg = lg.expand(B, H, N)
+            desc.decay_mode = _capi.SUBQ_DECAY_PER_TOKEN
+        lg = lg.contiguous()
+        keep.append(lg)
+        desc.log_gamma = lg.data_ptr()
+    if mask is not None:
+        m = mask.detach()
+        if m.dim() != 2 or m.shape[0] != B or m.shape[1] != N:
+            raise ValueError(f"mask must be [B, N] = [{B}, {N}], got {tuple(m.shape)}")
+        if m.device != q.device:
+            raise ValueError("mask must be on the device of q")
+        if m.dtype != torch.uint8 or m.stride(1) != 1:
+            m = (m != 0).to(torch.uint8).contiguous()
+        keep.append(m)
+        desc.mask = m.data_ptr()
+        desc.mask_stride_b = m.stride(0)
+    return desc
+
+
+def _workspace(nbytes: int, device: torch.device, keep: list) -> Tuple[int, int]:
+    if nbytes == 0:
+        return 0, 0
+    buf = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+    keep.append(buf)
+    ptr = buf.data_ptr()
+    return (ptr + 255) // 256 * 256, nbytes
+
+
+def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma: LogGamma = None,
+                 mask: Optional[torch.Tensor] = None, normalize: bool = True, scale: Optional[float] = None,
+                 clamp_min: float = 1e-5, state: Optional[Tuple[torch.Tensor, Optional[torch.Tensor]]] = None,
+                 return_state: bool = False, flush_subnormal: bool = False, path: str = "auto",
+                 out: Optional[torch.Tensor] = None):
+    """Causal scan. Returns ``(o, (S, z) | None)``; S [B,H,d,e] and z [B,H,d] are float32."""
+    _require_cuda(q, k, v)
+    q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
+    if k.shape != q.shape or v.shape[:3] != q.shape[:3]:
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("q, k and v must share one dtype")
+    B, H, N, d = q.shape
+    e = v.shape[-1]
+    keep: list = []
+    with torch.cuda.device(q.device):
+        o = out if out is not None else torch.empty((B, H, N, e), dtype=q.dtype, device=q.device)
+        a = _capi.FwdArgs()
+        a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep)
+        a.q, a.k, a.v, a.o = _t4(q), _t4(k), _t4(v), _t4(o)
+        S_out = z_out = None
+        if state is not None:
+            S_in, z_in = state[0], (state[1] if len(state) > 1 else None)
+            S_in = S_in.detach().to(torch.float32).reshape(B, H, d, e).contiguous()
+            keep.append(S_in)
+            a.state_in = S_in.data_ptr()
+            if z_in is not None:
+                z_in = z_in.detach().to(torch.float32).reshape(B, H, d).contiguous()
+                keep.append(z_in)
+                a.norm_in = z_in.data_ptr()
+        if return_state:
+            S_out = torch.empty((B, H, d, e), dtype=torch.float32, device=q.device)
+            z_out = torch.zeros((B, H, d), dtype=torch.float32, device=q.device)
+            a.state_out = S_out.data_ptr()
+            if normalize:
+                a.norm_out = z_out.data_ptr()
+        a.stream = torch.cuda.current_stream(q.device).cuda_stream
+        a.workspace, a.workspace_bytes = _workspace(_capi.fwd_workspace_bytes(a), q.device, keep)
+        _capi.fwd(a)
+    return o, ((S_out, z_out) if return_state else None)
+
+
+def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch.Tensor, *,
+                  log_gamma: LogGamma = None, mask: Optional[torch.Tensor] = None, normalize: bool = True,
+                  scale: Optional[float] = None, clamp_min: float = 1e-5,
+                  state: Optional[Tuple[torch.Tensor, Optional[torch.Tensor]]] = None,
+                  need_dlog_gamma: bool = False, flush_subnormal: bool = False, path: str = "auto"):
+    """Gradients of ``scan_forward``. Returns ``(dq, dk, dv, dlog_gamma | None)``;
+    dlog_gamma is float32 [B,H,N] (d loss / d log gamma_t per token)."""
+    _require_cuda(q, k, v, dout)
+    q, k, v, dout = _inner_contig(q), _inner_contig(k), _inner_contig(v), _inner_contig(dout)
+    if dout.dtype != q.dtype:
+        dout = dout.to(q.dtype)
+    B, H, N, d = q.shape
+    e = v.shape[-1]
+    keep: list = []
+    with torch.cuda.device(q.device):
+        dq = torch.empty((B, H, N, d), dtype=q.dtype, device=q.device)
+        dk = torch.empty((B, H, N, d), dtype=q.dtype, device=q.device)
+        dv = torch.empty((B, H, N, e), dtype=q.dtype, device=q.device)
+        a = _capi.BwdArgs()
+        a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep)
+        a.q, a.k, a.v, a.dout = _t4(q), _t4(k), _t4(v), _t4(dout)
+        a.dq, a.dk, a.dv = _t4(dq), _t4(dk), _t4(dv)
+        if state is not None:
+            S_in = state[0].detach().to(torch.float32).reshape(B, H, d, e).contiguous()
+            keep.append(S_in)
+            a.state_in = S_in.data_ptr()
+            if len(state) > 1 and state[1] is not None:
+                z_in = state[1].detach().to(torch.float32).reshape(B, H, d).contiguous()
+                keep.append(z_in)
+                a.norm_in = z_in.data_ptr()
+        dlg = None
+        if need_dlog_gamma:
+            dlg = torch.empty((B, H, N), dtype=torch.float32, device=q.device)
+            a.dlog_gamma = dlg.data_ptr()
+        a.stream = torch.cuda.current_stream(q.device).cuda_stream
+        a.workspace, a.workspace_bytes = _workspace(_capi.bwd_workspace_bytes(a), q.device, keep)
+        _capi.bwd(a)
+    return dq, dk, dv, dlg
+
+
+def feature_map_(x: torch.Tensor) -> torch.Tensor:
+    """In-place phi(x) = ELU(x) + 1 on a contiguous CUDA tensor (run_feature_map)."""
+    _require_cuda(x)
+    if not x.is_contiguous():
+        raise ValueError("feature_map_ needs a contiguous tensor")
+    with torch.cuda.device(x.device):
+        _capi.check(_capi.load().subq_feature_map(x.data_ptr(), x.numel(), _DTYPES[x.dtype],
+                                                   torch.cuda.current_stream(x.device).cuda_stream))
+    return x
+
+
+def last_path() -> str:
+    return {0: "auto", 1: "exact", 2: "tensorcore"}.get(_capi.last_path(), "?")
+
+
+def last_launches() -> int:
+    return _capi.last_launches()

@@ -1,0 +1,186 @@
+"""Parity of the CUDA scan (through the C ABI) with the float64 oracle.
+
+Metric: max |x - ref| / max |ref| over the tensor (the north-star metric).
+Tolerances: 1e-4 for float32, 1e-10 for float64 (exact path), 2e-2 for
+bfloat16/float16 (tensor-core path and exact path on 16-bit inputs); the
+oracle runs on the 16-bit-rounded inputs in float64.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from subq_audio import ops
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-4, torch.float64: 1e-10, torch.bfloat16: 2e-2, torch.float16: 2e-2}
+
+
+def rel_err(got, ref):
+    got = got.detach().double().cpu().numpy() if isinstance(got, torch.Tensor) else np.asarray(got)
+    den = np.abs(ref).max()
+    return float(np.abs(got - ref).max() / (den if den > 0 else 1.0))
+
+
+def make_case(B, H, N, d, e, dtype, seed, decay="none", mask=False, state=False, normalize=True, scale_in=1.0):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(B, H, N, d, generator=g) * scale_in).to(dtype)
+    k = (torch.randn(B, H, N, d, generator=g) * scale_in).to(dtype)
+    v = torch.randn(B, H, N, e, generator=g).to(dtype)
+    do = torch.randn(B, H, N, e, generator=g).to(dtype)
+    lg = None
+    if decay == "scalar":
+        lg = math.log(0.97)
+    elif decay == "head":
+        lg = -torch.nn.functional.softplus(-torch.linspace(1.0, 5.0, H))
+    elif decay == "token":
+        lg = -torch.nn.functional.softplus(-(torch.randn(B, H, N, generator=g) + 3.0))
+    m = None
+    if mask:
+        lens = torch.randint(max(1, N // 2), N + 1, (B,), generator=g)
+        lens[0] = N
+        m = (torch.arange(N)[None, :] < lens[:, None])
+    st = None
+    if state:
+        S0 = torch.randn(B, H, d, e, generator=g) * 0.5
+        z0 = torch.rand(B, H, d, generator=g) * 2.0 if normalize else None
+        st = (S0, z0)
+    return q, k, v, do, lg, m, st
+
+
+def oracle_inputs(q, k, v, do, lg, m, st, B, H, N):
+    f = lambda t: t.double().numpy()  # noqa: E731
+    # log(gamma) crosses the C ABI as float32; the oracle sees the same rounded value.
+    if lg is None:
+        lg_np = None
+    elif isinstance(lg, float):
+        lg_np = np.full((B, H, N), float(np.float32(lg)))
+    elif lg.dim() == 1:
+        lg_np = np.broadcast_to(lg.float().double().numpy()[None, :, None], (B, H, N))
+    else:
+        lg_np = lg.float().double().numpy()
+    m_np = None if m is None else np.broadcast_to(m.double().numpy()[:, None, :], (B, H, N))
+    S0 = None if st is None else st[0].double().numpy()
+    z0 = None if (st is None or st[1] is None) else st[1].double().numpy()
+    return f(q), f(k), f(v), f(do), lg_np, m_np, S0, z0
+
+
+def to_dev(x):
+    if x is None or isinstance(x, float):
+        return x
+    if isinstance(x, tuple):
+        return tuple(to_dev(t) for t in x)
+    return x.cuda()
+
+
+CASES = [
+    # B, H, N, d, e, dtype, decay, mask, state, normalize, path
+    (1, 1, 7, 4, 4, torch.float32, "scalar", False, False, False, "exact"),
+    (2, 1, 130, 16, 16, torch.float32, "scalar", False, False, False, "exact"),
+    (1, 1, 65, 8, 8, torch.float32, "none", False, True, False, "exact"),
+    (2, 3, 100, 16, 16, torch.float32, "head", False, False, True, "exact"),
+    (2, 2, 80, 16, 16, torch.float32, "token", True, False, True, "exact"),
+    (1, 2, 150, 32, 48, torch.float32, "none", True, True, True, "exact"),
+    (1, 1, 300, 64, 64, torch.float32, "none", True, False, True, "exact"),
+    (1, 1, 96, 128, 128, torch.float32, "scalar", False, False, True, "exact"),
+    (2, 2, 67, 8, 8, torch.float64, "token", True, True, True, "exact"),
+    (1, 2, 64, 64, 64, torch.float64, "scalar", False, False, False, "exact"),
+    (2, 2, 200, 64, 64, torch.bfloat16, "none", True, False, True, "exact"),
+    (1, 2, 129, 64, 64, torch.float16, "head", False, True, True, "exact"),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
+def test_forward_backward_matches_oracle(case):
+    B, H, N, d, e, dtype, decay, mask, state, normalize, path = case
+    q, k, v, do, lg, m, st = make_case(B, H, N, d, e, dtype, seed=17 + N + d, decay=decay, mask=mask,
+                                       state=state, normalize=normalize)
+    qn, kn, vn, don, lgn, mn, S0, z0 = oracle_inputs(q, k, v, do, lg, m, st, B, H, N)
+    scale = 1.0 / math.sqrt(d) if normalize else 1.0
+    ref_o, ref_S, ref_z, _ = oracle.forward(qn, kn, vn, log_gamma=lgn, mask=mn, normalize=normalize,
+                                            scale=scale, S0=S0, z0=z0)
+    o, (S, z) = ops.scan_forward(to_dev(q), to_dev(k), to_dev(v), log_gamma=to_dev(lg), mask=to_dev(m),
+                                 normalize=normalize, state=to_dev(st), return_state=True, path=path)
+    tol = TOL[dtype]
+    assert ops.last_path() == path
+    assert rel_err(o, ref_o) < tol
+    # The carried state is always float32.
+    assert rel_err(S, ref_S) < max(tol, 1e-5)
+    if normalize:
+        assert rel_err(z, ref_z) < max(tol, 1e-5)
+
+    rq, rk, rv, rdlg = oracle.backward(qn, kn, vn, don, log_gamma=lgn, mask=mn, normalize=normalize,
+                                       scale=scale, S0=S0, z0=z0)
+    dq, dk, dv, dlg = ops.scan_backward(to_dev(q), to_dev(k), to_dev(v), to_dev(do), log_gamma=to_dev(lg),
+                                        mask=to_dev(m), normalize=normalize, state=to_dev(st),
+                                        need_dlog_gamma=True, path=path)
+    assert rel_err(dq, rq) < tol, "dq"
+    assert rel_err(dk, rk) < tol, "dk"
+    assert rel_err(dv, rv) < tol, "dv"
+    assert rel_err(dlg, rdlg) < max(tol, 2e-4), "dlog_gamma"
+
+
+def test_strided_bnhd_layout_matches_contiguous():
+    """q/k/v consumed straight from a [B, N, H, D] projection layout via strides."""
+    B, N, H, D = 2, 96, 3, 16
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(B, N, 3, H, D, generator=g).cuda()
+    q, k, v = (x[:, :, i].transpose(1, 2) for i in range(3))  # [B,H,N,D] non-contiguous views
+    o_strided, _ = ops.scan_forward(q, k, v, log_gamma=math.log(0.9))
+    o_contig, _ = ops.scan_forward(q.contiguous(), k.contiguous(), v.contiguous(), log_gamma=math.log(0.9))
+    assert torch.equal(o_strided, o_contig)
+
+
+def test_streaming_state_equals_single_pass():
+    B, H, N, D = 1, 2, 512, 32
+    q, k, v, _, _, _, _ = make_case(B, H, N, D, D, torch.float32, seed=3)
+    q, k, v = q.cuda(), k.cuda(), v.cuda()
+    full, (S_full, z_full) = ops.scan_forward(q, k, v, return_state=True)
+    parts, st = [], None
+    for s in range(0, N, 128):
+        o, st = ops.scan_forward(q[:, :, s:s + 128], k[:, :, s:s + 128], v[:, :, s:s + 128], state=st,
+                                 return_state=True)
+        parts.append(o)
+    streamed = torch.cat(parts, dim=2)
+    assert (streamed - full).abs().max().item() <= 1e-5 * full.abs().max().item()
+    assert (st[0] - S_full).abs().max().item() <= 1e-5 * S_full.abs().max().item()
+
+
+def test_empty_and_single_token_sequences():
+    q = torch.randn(2, 1, 0, 8, device="cuda")
+    o, st = ops.scan_forward(q, q, q, return_state=True)
+    assert o.shape == (2, 1, 0, 8)
+    assert torch.count_nonzero(st[0]) == 0
+    q1 = torch.randn(1, 1, 1, 8, device="cuda")
+    o1, _ = ops.scan_forward(q1, q1, q1, normalize=False)
+    phi = lambda x: torch.where(x > 0, x + 1, torch.exp(x))  # noqa: E731
+    ref = (phi(q1[0, 0, 0]) @ phi(q1[0, 0, 0])) * q1[0, 0, 0]
+    assert torch.allclose(o1[0, 0, 0], ref, rtol=1e-5, atol=1e-6)
+
+
+def test_fully_masked_sequence_outputs_zero():
+    q = torch.randn(1, 2, 40, 16, device="cuda")
+    m = torch.zeros(1, 40, dtype=torch.bool, device="cuda")
+    o, _ = ops.scan_forward(q, q, q, mask=m)
+    assert torch.count_nonzero(o) == 0
+    dq, dk, dv, _ = ops.scan_backward(q, q, q, torch.ones_like(q), mask=m)
+    assert torch.count_nonzero(dq) == torch.count_nonzero(dk) == torch.count_nonzero(dv) == 0
+
+
+def test_nan_inputs_propagate_without_fault():
+    q = torch.full((1, 1, 64, 16), float("nan"), device="cuda")
+    k = torch.full_like(q, float("inf"))
+    v = torch.full_like(q, -float("inf"))
+    o, _ = ops.scan_forward(q, k, v, normalize=False)
+    torch.cuda.synchronize()
+    assert torch.isnan(o).any()
+
+
+def test_feature_map_known_answers():
+    x = torch.tensor([-1.0, 2.0, 0.0, -2.0], device="cuda")
+    ops.feature_map_(x)
+    ref = torch.tensor([0.367879, 3.0, 1.0, 0.135335], device="cuda")
+    assert torch.allclose(x, ref, atol=1e-4)
