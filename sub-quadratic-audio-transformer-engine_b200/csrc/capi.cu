@@ -80,6 +80,10 @@ bool use_tc(const subq::ScanParams& p, int dtype, int path) {
     return subq::tc_supported(p, dtype);
 }
 
+bool use_tc_bwd(const subq::ScanParams& p, int dtype, int path) {
+    return use_tc(p, dtype, path) && subq::tc_bwd_supported(p, dtype);
+}
+
 int fill_fwd(const subq_fwd_args* a, subq::ScanParams& p) {
     if (!a) return fail(SUBQ_ERR_INVALID_ARGUMENT, "null argument block");
     int rc = check_desc(a->desc, p);
@@ -168,7 +172,7 @@ size_t subq_fwd_workspace_bytes(const subq_fwd_args* a) {
 size_t subq_bwd_workspace_bytes(const subq_bwd_args* a) {
     subq::ScanParams p;
     if (fill_bwd(a, p) != SUBQ_OK) return 0;
-    if (use_tc(p, a->desc.dtype, a->desc.path)) return subq::tc_bwd_workspace_bytes(p);
+    if (use_tc_bwd(p, a->desc.dtype, a->desc.path)) return subq::tc_bwd_workspace_bytes(p);
     return exact_bwd_ws(p, a->desc.dtype);
 }
 
@@ -206,7 +210,7 @@ int subq_bwd(const subq_bwd_args* a) {
     subq::ScanParams p;
     int rc = fill_bwd(a, p);
     if (rc) return rc;
-    const bool tc = use_tc(p, a->desc.dtype, a->desc.path);
+    const bool tc = use_tc_bwd(p, a->desc.dtype, a->desc.path);
     if (a->desc.path == SUBQ_PATH_TENSORCORE && !tc)
         return fail(SUBQ_ERR_UNSUPPORTED, "tensor-core path needs bf16/fp16 with head_dim = value_dim = 64");
     if (!tc && subq::exact_bwd_smem_bytes(p.d, p.e, p.normalize, a->desc.dtype == SUBQ_FP64 ? 8 : 4) > 220 * 1024)

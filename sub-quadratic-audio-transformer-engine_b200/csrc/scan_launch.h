@@ -16,6 +16,7 @@ cudaError_t launch_feature_map(void* x, int64_t n, int dtype, cudaStream_t st);
 
 // Tensor-core path (scan_tc.cu).
 bool tc_supported(const ScanParams& p, int dtype);
+bool tc_bwd_supported(const ScanParams& p, int dtype);
 size_t tc_fwd_workspace_bytes(const ScanParams& p);
 size_t tc_bwd_workspace_bytes(const ScanParams& p);
 // Returns the number of kernel launches issued through *launches.

@@ -123,6 +123,50 @@ def test_forward_backward_matches_oracle(case):
     assert rel_err(dlg, rdlg) < max(tol, 2e-4), "dlog_gamma"
 
 
+TC_CASES = [
+    # B, H, N, dtype, mask, state, normalize
+    (1, 1, 1, torch.bfloat16, False, False, True),
+    (1, 1, 100, torch.bfloat16, False, False, True),
+    (1, 2, 128, torch.bfloat16, True, False, True),
+    (2, 2, 1000, torch.bfloat16, True, True, True),
+    (1, 1, 4096, torch.bfloat16, False, False, True),
+    (2, 1, 777, torch.float16, True, True, True),
+    (1, 3, 300, torch.bfloat16, False, True, False),
+    (8, 8, 512, torch.bfloat16, True, False, True),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES, ids=[f"tc{i}" for i in range(len(TC_CASES))])
+def test_tensorcore_forward_matches_oracle(case):
+    B, H, N, dtype, mask, state, normalize = case
+    d = e = 64
+    q, k, v, do, lg, m, st = make_case(B, H, N, d, e, dtype, seed=101 + N + H, mask=mask, state=state,
+                                       normalize=normalize, scale_in=1.0)
+    qn, kn, vn, don, lgn, mn, S0, z0 = oracle_inputs(q, k, v, do, lg, m, st, B, H, N)
+    scale = 1.0 / math.sqrt(d) if normalize else 1.0
+    ref_o, ref_S, ref_z, _ = oracle.forward(qn, kn, vn, log_gamma=lgn, mask=mn, normalize=normalize,
+                                            scale=scale, S0=S0, z0=z0)
+    o, (S, z) = ops.scan_forward(to_dev(q), to_dev(k), to_dev(v), mask=to_dev(m), normalize=normalize,
+                                 state=to_dev(st), return_state=True, path="tensorcore")
+    torch.cuda.synchronize()
+    assert ops.last_path() == "tensorcore"
+    assert rel_err(o, ref_o) < 2e-2
+    assert rel_err(S, ref_S) < 2e-2
+    if normalize:
+        assert rel_err(z, ref_z) < 2e-2
+
+
+def test_tensorcore_forward_matches_exact_path():
+    B, H, N = 2, 4, 2048
+    q, k, v, _, _, m, _ = make_case(B, H, N, 64, 64, torch.bfloat16, seed=9, mask=True)
+    q, k, v, m = q.cuda(), k.cuda(), v.cuda(), m.cuda()
+    o_tc, st_tc = ops.scan_forward(q, k, v, mask=m, return_state=True, path="tensorcore")
+    o_ex, st_ex = ops.scan_forward(q, k, v, mask=m, return_state=True, path="exact")
+    ref = o_ex.double()
+    assert ((o_tc.double() - ref).abs().max() / ref.abs().max()).item() < 2e-2
+    assert ((st_tc[0] - st_ex[0]).abs().max() / st_ex[0].abs().max()).item() < 1e-2
+
+
 def test_strided_bnhd_layout_matches_contiguous():
     """q/k/v consumed straight from a [B, N, H, D] projection layout via strides."""
     B, N, H, D = 2, 96, 3, 16
