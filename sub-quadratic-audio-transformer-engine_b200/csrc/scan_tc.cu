@@ -452,6 +452,601 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const __grid_consta
     if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
+// ===================================================================
+// Backward. One cluster of G CTAs per (batch, head) sequence; CTA g owns
+// segment g. With q~ = scale phi(q), k~ = m phi(k), Zc_t = max(Z_t, clamp):
+//   o^_t = m_t dO_t / Zc_t,   c_t = -(m_t dO_t . num_t) / Zc_t^2   (quotient rule)
+//   dA   = (O^ V^T + c m^T) * [tau <= t]                 (per chunk, 128 x 128)
+//   dQ~  = dA K~ + O^ S_c^T + c z_c^T                    (S_c, z_c: prefix state)
+//   dK~  = dA^T Q~ + V dS_c^T + m dz_c^T                 (dS_c, dz_c: suffix adjoint)
+//   dV   = (P * [tau <= t])^T O^ + K~ dS_c
+//   dS_c-1 = dS_c + Q~^T O^,  dz_c-1 = dz_c + Q~^T c
+// then dq = dQ~ scale phi'(q), dk = dK~ phi'(k) m, dv = dV m, with
+// phi'(x) = min(phi(x), 1). Phases:
+//   A  segment sums of K~^T V and colsum K~ (g < G-1) -> DSMEM -> S_c, z_c prefix
+//   B  chunks ascending: recompute num and Z, build O^ and c, emit dq, store
+//      (Zc_t, c_t) per token in the workspace, accumulate the segment's
+//      Q~^T O^ and Q~^T c
+//   -> DSMEM -> dS, dz suffix of the segment
+//   C  chunks descending: rebuild O^ from dO and (Zc, c), emit dk and dv.
+// Reference: python/subq_audio/autograd.py:441-544 (quotient rule :497-499,
+// adjoint scan :172-289) and src/kernels/attention_backward.cpp:165-229.
+// ===================================================================
+struct BwdSmem {
+    static constexpr uint32_t stage = 4 * kTile;  // q, k, v, dO
+    static constexpr uint32_t q = 0, k = kTile, v = 2 * kTile, g = 3 * kTile;
+    static constexpr uint32_t p = kStages * stage;     // P, 2 blocks (also the exchange buffer)
+    static constexpr uint32_t da = p + 2 * kTile;      // dA, 2 blocks
+    static constexpr uint32_t ob = da + 2 * kTile;     // O^ tile [t][e]
+    static constexpr uint32_t sb = ob + kTile;         // bf16 S_c (phase B) / dS_c (phase C)
+    static constexpr uint32_t zc = sb + kD * kD * 2;   // z_c (B) / dz_c (C), fp32 [64]
+    static constexpr uint32_t zp = zc + kD * 4;        // partial column sums [2][64]
+    static constexpr uint32_t cb = zp + 2 * kD * 4;    // c_t [128]
+    static constexpr uint32_t mb = cb + kC * 4;        // m_t [128]
+    static constexpr uint32_t bars = mb + kC * 4;
+    static constexpr uint32_t tslot = bars + 8 * (kStages + 1);
+    static constexpr uint32_t total = tslot + 16;
+};
+static_assert(BwdSmem::p % 1024 == 0 && BwdSmem::da % 1024 == 0 && BwdSmem::ob % 1024 == 0 &&
+                  BwdSmem::sb % 1024 == 0,
+              "tiles must be 1024-byte aligned");
+
+// TMEM columns: P [0,128), dA [128,256), X1 [256,320), X2 [320,384),
+// S [384,448) and dS [448,512) (both M = 64 layout).
+constexpr uint32_t kBwdTmemCols = 512;
+constexpr uint32_t kBP = 0, kBdA = 128, kBX1 = 256, kBX2 = 320, kBS = 384, kBdS = 448;
+
+struct TcBwdParams {
+    CUtensorMap tm_q, tm_k, tm_v, tm_g, tm_dq, tm_dk, tm_dv;
+    ScanParams p;
+    int G;
+    int cps;
+};
+
+// Weighted column sums of a swizzled 128 x 64 tile: zp[half][col] = sum_r tile[r][col] * w[r].
+template <bool kFp16>
+__device__ __forceinline__ void tile_colsum_w(const uint8_t* tile, const float* w, float* zp, int tid) {
+    using E = Elem<kFp16>;
+    const int col = tid & 63, half = tid >> 6;
+    float acc = 0.f;
+    for (int r = half * 64; r < half * 64 + 64; ++r) {
+        const typename E::T* e = reinterpret_cast<const typename E::T*>(tile + tc::sw128_off(r, col));
+        acc = fmaf((float)(*e), w[r], acc);
+    }
+    zp[half * 64 + col] = acc;
+}
+
+// Reads the 64 values of row r of a swizzled tile into fp32.
+template <bool kFp16>
+__device__ __forceinline__ void load_row(const uint8_t* tile, int r, float* out) {
+    using E = Elem<kFp16>;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        uint4 raw = *reinterpret_cast<const uint4*>(tile + tc::sw128_chunk(r, j));
+        const typename E::T2* h = reinterpret_cast<const typename E::T2*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float2 f2 = E::to2(h[i]);
+            out[8 * j + 2 * i] = f2.x;
+            out[8 * j + 2 * i + 1] = f2.y;
+        }
+    }
+}
+
+template <bool kFp16, bool kNorm>
+__global__ void __launch_bounds__(kThreads, 1) bwd_tc_kernel(const __grid_constant__ TcBwdParams P) {
+    const ScanParams& p = P.p;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    cg::cluster_group cluster = cg::this_cluster();
+
+    const int g = (int)cluster.block_rank();
+    const int bh = blockIdx.y;
+    const int b = bh / p.H, h = bh - b * p.H;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nC = (p.N + kC - 1) / kC;
+    const int c_begin = min(nC, g * P.cps);
+    const int c_end = min(nC, c_begin + P.cps);
+    const int n = c_end - c_begin;
+
+    uint64_t* tma_bar = reinterpret_cast<uint64_t*>(sm + BwdSmem::bars);
+    uint64_t* mma_bar = tma_bar + kStages;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + BwdSmem::tslot);
+    float* zc = reinterpret_cast<float*>(sm + BwdSmem::zc);
+    float* zp = reinterpret_cast<float*>(sm + BwdSmem::zp);
+    float* cb = reinterpret_cast<float*>(sm + BwdSmem::cb);
+    float* mb = reinterpret_cast<float*>(sm + BwdSmem::mb);
+    uint8_t* Pt = sm + BwdSmem::p;
+    uint8_t* dAt = sm + BwdSmem::da;
+    uint8_t* Ot = sm + BwdSmem::ob;
+    uint8_t* Sb = sm + BwdSmem::sb;
+    float2* wsz = reinterpret_cast<float2*>(p.ws) + (int64_t)bh * p.N;  // (Zc_t, c_t) per token
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) tc::mbar_init(&tma_bar[s], 1);
+        tc::mbar_init(mma_bar, 1);
+        tc::fence_mbar_init();
+    }
+    if (warp == 0) tc::tmem_alloc(tslot, kBwdTmemCols);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t tP = tmem + kBP, tdA = tmem + kBdA, tX1 = tmem + kBX1, tX2 = tmem + kBX2;
+    const uint32_t tS = tmem + kBS, tdS = tmem + kBdS;
+    const uint32_t sbase = tc::smem_u32(sm);
+
+    bool ok = true;
+    uint32_t tma_phase[kStages] = {0, 0};
+    int pending[kStages] = {0, 0};
+    uint32_t mma_phase = 0;
+
+    constexpr uint32_t id128_KK = tc::idesc_f16<kFp16>(128, 128, false, false);
+    constexpr uint32_t id64_KM = tc::idesc_f16<kFp16>(128, 64, false, true);
+    constexpr uint32_t id64_KK = tc::idesc_f16<kFp16>(128, 64, false, false);
+    constexpr uint32_t id64_MM = tc::idesc_f16<kFp16>(128, 64, true, true);
+    constexpr uint32_t idS_MM = tc::idesc_f16<kFp16>(64, 64, true, true);
+
+    auto stage_addr = [&](int s, uint32_t which) { return sbase + s * BwdSmem::stage + which; };
+    auto stage_ptr = [&](int s, uint32_t which) { return sm + s * BwdSmem::stage + which; };
+    auto issue = [&](int chunk, int s, bool full) {
+        const int t0 = chunk * kC;
+        pending[s] = 1;
+        tc::mbar_arrive_expect_tx(&tma_bar[s], (full ? 4u : 2u) * kTile);
+        if (full) {
+            tc::tma_load_4d(stage_ptr(s, BwdSmem::q), &P.tm_q, 0, t0, h, b, &tma_bar[s]);
+            tc::tma_load_4d(stage_ptr(s, BwdSmem::g), &P.tm_g, 0, t0, h, b, &tma_bar[s]);
+        }
+        tc::tma_load_4d(stage_ptr(s, BwdSmem::k), &P.tm_k, 0, t0, h, b, &tma_bar[s]);
+        tc::tma_load_4d(stage_ptr(s, BwdSmem::v), &P.tm_v, 0, t0, h, b, &tma_bar[s]);
+    };
+    auto row_mask = [&](int chunk, int r) -> float {
+        const int t = chunk * kC + r;
+        if (t >= p.N) return 0.f;
+        return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
+    };
+    auto wait_mma = [&]() {
+        ok = __syncthreads_and(wait_bar(mma_bar, mma_phase)) && ok;
+        mma_phase ^= 1u;
+        tc::tc_fence_after();
+    };
+    auto sync_for_mma = [&]() {
+        tc::fence_proxy_async();
+        tc::tc_fence_before();
+        __syncthreads();
+    };
+    // acc (+)= X^T Y over 128 tokens: X, Y are [128][64] tiles read MN-major (M=64 layout).
+    auto mma_xty = [&](uint32_t dst, uint32_t xa, uint32_t ya, bool first) {
+        for (int kk = 0; kk < 8; ++kk)
+            tc::mma_f16(dst, tc::sdesc_sw128(xa + kk * 2048, kTile, 1024), tc::sdesc_sw128(ya + kk * 2048, kTile, 1024),
+                        idS_MM, (first && kk == 0) ? 0u : 1u);
+    };
+    // Causal-masked 128 x 128 tile from TMEM to bf16 shared memory (two 64-column blocks),
+    // optionally adding c_t m_tau and returning the row sum.
+    auto tile_out = [&](uint32_t tsrc, uint8_t* dst, bool add_cm, float ct) -> float {
+        float rs = 0.f;
+        for (int blk = 0; blk < 4; ++blk) {
+            float v[32];
+            tc::tmem_ld32(tsrc + lane_off + blk * 32, v);
+#pragma unroll
+            for (int u = 0; u < 32; ++u) {
+                const int tau = blk * 32 + u;
+                float x = add_cm ? fmaf(ct, mb[tau], v[u]) : v[u];
+                x = (tau <= tid) ? x : 0.f;
+                rs += x;
+                v[u] = x;
+            }
+            uint8_t* pb = dst + (blk >> 1) * kTile;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) store_chunk<kFp16>(pb, tid, (blk & 1) * 4 + q4, v + 8 * q4);
+        }
+        return rs;
+    };
+    // M = 64 state (TMEM) -> bf16 shared-memory copy (row = state row).
+    auto refresh_state_copy = [&](uint32_t tsrc) {
+        float srow[64];
+        tc::tmem_ld32(tsrc + lane_off + 0, srow);
+        tc::tmem_ld32(tsrc + lane_off + 32, srow + 32);
+        if (lane < 16) {
+            const int r = warp * 16 + lane;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) store_chunk<kFp16>(Sb, r, j, srow + 8 * j);
+        }
+    };
+    // Writes a 64 x 64 fp32 state into TMEM (M = 64 layout) and its bf16 copy.
+    auto load_state = [&](uint32_t tdst, float* row) {
+        if (lane < 16) {
+            const int r = warp * 16 + lane;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) store_chunk<kFp16>(Sb, r, j, row + 8 * j);
+        }
+        tc::tmem_st32(tdst + lane_off + 0, row);
+        tc::tmem_st32(tdst + lane_off + 32, row + 32);
+    };
+
+    float* Xs = reinterpret_cast<float*>(Pt);
+    float* Xz = reinterpret_cast<float*>(Pt + kD * kD * 4);
+
+    // ------------------------------------------------------------ phase A
+    if (g < P.G - 1) {
+        float zacc = 0.f;
+        if (tid == 0 && n > 0) issue(c_begin, 0, false);
+        for (int i = 0; i < n && ok; ++i) {
+            const int c = c_begin + i, s = i % kStages;
+            if (tid == 0 && i + 1 < n) issue(c + 1, (i + 1) % kStages, false);
+            ok = __syncthreads_and(wait_bar(&tma_bar[s], tma_phase[s]));
+            tma_phase[s] ^= 1u;
+            pending[s] = 0;
+            if (!ok) break;
+            uint8_t* kt = stage_ptr(s, BwdSmem::k);
+            const float m = row_mask(c, tid);
+            row_transform<kFp16>(kt, tid, [&](int, float* v) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = phi_fast(v[u]) * m;
+            });
+            sync_for_mma();
+            if (tid == 0) {
+                tc::tc_fence_after();
+                mma_xty(tS, stage_addr(s, BwdSmem::k), stage_addr(s, BwdSmem::v), i == 0);
+                tc::mma_commit(mma_bar);
+            }
+            if (kNorm) {
+                tile_colsum<kFp16>(kt, zp, tid);
+                zacc += zp[tid];
+            }
+            wait_mma();
+        }
+        float row[64];
+        if (n > 0 && ok) {
+            tc::tmem_ld32(tS + lane_off + 0, row);
+            tc::tmem_ld32(tS + lane_off + 32, row + 32);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) row[j] = 0.f;
+        }
+        if (lane < 16) {
+            const int r = warp * 16 + lane;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) Xs[r * 64 + j] = row[j];
+        }
+        zp[tid] = zacc;
+        __syncthreads();
+        if (tid < 64) Xz[tid] = kNorm ? zp[tid] + zp[tid + 64] : 0.f;
+    }
+    tc::tc_fence_before();
+    cluster.sync();
+    tc::tc_fence_after();
+    {
+        float row[64];
+        const int r = warp * 16 + lane;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) row[j] = 0.f;
+        if (lane < 16) {
+            if (p.S_in)
+                for (int j = 0; j < 64; ++j) row[j] = p.S_in[((int64_t)bh * kD + r) * kD + j];
+            for (int src = 0; src < g; ++src) {
+                const float* rx = cluster.map_shared_rank(Xs, src);
+                for (int j = 0; j < 64; ++j) row[j] += rx[r * 64 + j];
+            }
+        }
+        load_state(tS, row);
+        if (kNorm && tid < 64) {
+            float z = p.z_in ? p.z_in[(int64_t)bh * kD + tid] : 0.f;
+            for (int src = 0; src < g; ++src) z += cluster.map_shared_rank(Xz, src)[tid];
+            zc[tid] = z;
+        }
+    }
+    tc::fence_proxy_async();
+    tc::tc_fence_before();
+    cluster.sync();
+    tc::tc_fence_after();
+
+    // ------------------------------------------------------------ phase B
+    float dzacc = 0.f;  // this thread's column partial of Q~^T c over the segment
+    if (tid == 0 && n > 0) issue(c_begin, 0, true);
+    for (int i = 0; i < n && ok; ++i) {
+        const int c = c_begin + i, s = i % kStages;
+        if (tid == 0 && i + 1 < n) {
+            tc::bulk_wait_read0();
+            issue(c + 1, (i + 1) % kStages, true);
+        }
+        ok = __syncthreads_and(wait_bar(&tma_bar[s], tma_phase[s]));
+        tma_phase[s] ^= 1u;
+        pending[s] = 0;
+        if (!ok) break;
+        uint8_t* qt = stage_ptr(s, BwdSmem::q);
+        uint8_t* kt = stage_ptr(s, BwdSmem::k);
+        const float m = row_mask(c, tid);
+        mb[tid] = m;
+        float zq = 0.f;
+        row_transform<kFp16>(qt, tid, [&](int j, float* v) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                v[u] = phi_fast(v[u]) * p.scale;
+                if (kNorm) zq = fmaf(v[u], zc[8 * j + u], zq);
+            }
+        });
+        row_transform<kFp16>(kt, tid, [&](int, float* v) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = phi_fast(v[u]) * m;
+        });
+        sync_for_mma();
+        const uint32_t qa = stage_addr(s, BwdSmem::q), ka = stage_addr(s, BwdSmem::k);
+        const uint32_t va = stage_addr(s, BwdSmem::v);
+        if (tid == 0) {
+            tc::tc_fence_after();
+            for (int kk = 0; kk < 4; ++kk)  // P = Q~ K~^T
+                tc::mma_f16(tP, tc::sdesc_sw128(qa + kk * 32, 16, 1024), tc::sdesc_sw128(ka + kk * 32, 16, 1024),
+                            id128_KK, kk > 0);
+            for (int kk = 0; kk < 4; ++kk)  // num = Q~ S_c
+                tc::mma_f16(tX1, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
+                            tc::sdesc_sw128(sbase + BwdSmem::sb + kk * 2048, 8192, 1024), id64_KM, kk > 0);
+            tc::mma_commit(mma_bar);
+        }
+        wait_mma();
+        if (!ok) break;
+        const float Zt = tile_out(tP, Pt, false, 0.f) + zq;
+        sync_for_mma();
+        if (tid == 0) {
+            tc::tc_fence_after();
+            for (int kk = 0; kk < 8; ++kk) {  // num += P V
+                const uint32_t pa = sbase + BwdSmem::p + (kk >> 2) * kTile + (kk & 3) * 32;
+                tc::mma_f16(tX1, tc::sdesc_sw128(pa, 16, 1024), tc::sdesc_sw128(va + kk * 2048, kTile, 1024), id64_KM,
+                            1u);
+            }
+            tc::mma_commit(mma_bar);
+        }
+        wait_mma();
+        if (!ok) break;
+        // O^ and c (quotient rule); (Zc, c) go to the workspace for phase C.
+        float ct = 0.f;
+        {
+            float num[64], go[64];
+            tc::tmem_ld32(tX1 + lane_off + 0, num);
+            tc::tmem_ld32(tX1 + lane_off + 32, num + 32);
+            load_row<kFp16>(stage_ptr(s, BwdSmem::g), tid, go);
+            const float zcl = kNorm ? fmaxf(Zt, p.clamp_min) : 1.f;
+            const float inv = m / zcl;
+            float dot = 0.f;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                dot = fmaf(go[j] * m, num[j], dot);
+                go[j] *= inv;
+            }
+            ct = kNorm ? -dot / (zcl * zcl) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) store_chunk<kFp16>(Ot, tid, j, go + 8 * j);
+            if (c * kC + tid < p.N) wsz[c * kC + tid] = make_float2(zcl, ct);
+        }
+        cb[tid] = ct;
+        sync_for_mma();
+        if (tid == 0) {
+            tc::tc_fence_after();
+            for (int kk = 0; kk < 4; ++kk)  // dA = O^ V^T
+                tc::mma_f16(tdA, tc::sdesc_sw128(sbase + BwdSmem::ob + kk * 32, 16, 1024),
+                            tc::sdesc_sw128(va + kk * 32, 16, 1024), id128_KK, kk > 0);
+            mma_xty(tdS, qa, sbase + BwdSmem::ob, i == 0);  // segment sum of Q~^T O^
+            mma_xty(tS, ka, va, false);                      // S_c+1 = S_c + K~^T V
+            tc::mma_commit(mma_bar);
+        }
+        if (kNorm) tile_colsum_w<kFp16>(qt, cb, zp, tid);  // this chunk's Q~^T c
+        wait_mma();
+        if (!ok) break;
+        tile_out(tdA, dAt, kNorm, ct);
+        sync_for_mma();
+        if (tid == 0) {
+            tc::tc_fence_after();
+            for (int kk = 0; kk < 8; ++kk) {  // dQ~ = dA K~
+                const uint32_t aa = sbase + BwdSmem::da + (kk >> 2) * kTile + (kk & 3) * 32;
+                tc::mma_f16(tX2, tc::sdesc_sw128(aa, 16, 1024), tc::sdesc_sw128(ka + kk * 2048, kTile, 1024), id64_KM,
+                            kk > 0);
+            }
+            for (int kk = 0; kk < 4; ++kk)  // dQ~ += O^ S_c^T
+                tc::mma_f16(tX2, tc::sdesc_sw128(sbase + BwdSmem::ob + kk * 32, 16, 1024),
+                            tc::sdesc_sw128(sbase + BwdSmem::sb + kk * 32, 16, 1024), id64_KK, 1u);
+            tc::mma_commit(mma_bar);
+        }
+        wait_mma();
+        if (!ok) break;
+        {
+            float dq[64], qr[64];
+            tc::tmem_ld32(tX2 + lane_off + 0, dq);
+            tc::tmem_ld32(tX2 + lane_off + 32, dq + 32);
+            load_row<kFp16>(qt, tid, qr);
+            const float inv_scale = 1.f / p.scale;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                float x = kNorm ? fmaf(ct, zc[j], dq[j]) : dq[j];
+                x *= p.scale * fminf(qr[j] * inv_scale, 1.f) * m;
+                dq[j] = x;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) store_chunk<kFp16>(qt, tid, j, dq + 8 * j);
+        }
+        if (kNorm) dzacc += zp[tid];
+        __syncthreads();
+        // z_c+1 = z_c + colsum(K~): recompute the K~ column sums (zp was reused above).
+        if (kNorm) {
+            tile_colsum<kFp16>(kt, zp, tid);
+            __syncthreads();
+            if (tid < 64) zc[tid] += zp[tid] + zp[tid + 64];
+        }
+        refresh_state_copy(tS);
+        sync_for_mma();
+        if (tid == 0) {
+            tc::tma_store_4d(&P.tm_dq, qt, 0, c * kC, h, b);
+            tc::bulk_commit();
+        }
+    }
+
+    // --------------------------------------------- suffix exchange (dS, dz)
+    {
+        float row[64];
+        if (n > 0 && ok) {
+            tc::tmem_ld32(tdS + lane_off + 0, row);
+            tc::tmem_ld32(tdS + lane_off + 32, row + 32);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) row[j] = 0.f;
+        }
+        if (tid == 0) tc::bulk_wait_read0();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (lane < 16) {
+            const int r = warp * 16 + lane;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) Xs[r * 64 + j] = row[j];
+        }
+        zp[tid] = dzacc;
+        __syncthreads();
+        if (tid < 64) Xz[tid] = kNorm ? zp[tid] + zp[tid + 64] : 0.f;
+    }
+    cluster.sync();
+    tc::tc_fence_after();
+    {
+        float row[64];
+        const int r = warp * 16 + lane;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) row[j] = 0.f;
+        if (lane < 16) {
+            for (int src = g + 1; src < P.G; ++src) {
+                const float* rx = cluster.map_shared_rank(Xs, src);
+                for (int j = 0; j < 64; ++j) row[j] += rx[r * 64 + j];
+            }
+        }
+        float dz = 0.f;
+        if (kNorm && tid < 64)
+            for (int src = g + 1; src < P.G; ++src) dz += cluster.map_shared_rank(Xz, src)[tid];
+        tc::tc_fence_before();
+        cluster.sync();  // remote reads finished before the buffers are reused
+        tc::tc_fence_after();
+        load_state(tdS, row);
+        if (tid < 64) zc[tid] = dz;
+    }
+    tc::fence_proxy_async();
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+
+    // ------------------------------------------------------------ phase C
+    if (tid == 0 && n > 0) issue(c_end - 1, 0, true);
+    for (int i = 0; i < n && ok; ++i) {
+        const int c = c_end - 1 - i, s = i % kStages;
+        if (tid == 0 && i + 1 < n) {
+            tc::bulk_wait_read0();
+            issue(c - 1, (i + 1) % kStages, true);
+        }
+        ok = __syncthreads_and(wait_bar(&tma_bar[s], tma_phase[s]));
+        tma_phase[s] ^= 1u;
+        pending[s] = 0;
+        if (!ok) break;
+        uint8_t* qt = stage_ptr(s, BwdSmem::q);
+        uint8_t* kt = stage_ptr(s, BwdSmem::k);
+        uint8_t* vt = stage_ptr(s, BwdSmem::v);
+        const float m = row_mask(c, tid);
+        mb[tid] = m;
+        float2 zcc = make_float2(1.f, 0.f);
+        if (c * kC + tid < p.N) zcc = wsz[c * kC + tid];
+        const float ct = zcc.y;
+        cb[tid] = ct;
+        row_transform<kFp16>(qt, tid, [&](int, float* v) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = phi_fast(v[u]) * p.scale;
+        });
+        row_transform<kFp16>(kt, tid, [&](int, float* v) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = phi_fast(v[u]) * m;
+        });
+        {
+            float go[64];
+            load_row<kFp16>(stage_ptr(s, BwdSmem::g), tid, go);
+            const float inv = m / zcc.x;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) go[j] *= inv;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) store_chunk<kFp16>(Ot, tid, j, go + 8 * j);
+        }
+        sync_for_mma();
+        const uint32_t qa = stage_addr(s, BwdSmem::q), ka = stage_addr(s, BwdSmem::k);
+        const uint32_t va = stage_addr(s, BwdSmem::v);
+        if (tid == 0) {
+            tc::tc_fence_after();
+            for (int kk = 0; kk < 4; ++kk) {
+                tc::mma_f16(tP, tc::sdesc_sw128(qa + kk * 32, 16, 1024), tc::sdesc_sw128(ka + kk * 32, 16, 1024),
+                            id128_KK, kk > 0);
+                tc::mma_f16(tdA, tc::sdesc_sw128(sbase + BwdSmem::ob + kk * 32, 16, 1024),
+                            tc::sdesc_sw128(va + kk * 32, 16, 1024), id128_KK, kk > 0);
+            }
+            tc::mma_commit(mma_bar);
+        }
+        wait_mma();
+        if (!ok) break;
+        tile_out(tP, Pt, false, 0.f);
+        tile_out(tdA, dAt, kNorm, ct);
+        sync_for_mma();
+        if (tid == 0) {
+            tc::tc_fence_after();
+            for (int kk = 0; kk < 8; ++kk) {  // dK~ = dA^T Q~ ; dV = P^T O^  (A read MN-major, M = 128)
+                tc::mma_f16(tX1, tc::sdesc_sw128(sbase + BwdSmem::da + kk * 2048, kTile, 1024),
+                            tc::sdesc_sw128(qa + kk * 2048, kTile, 1024), id64_MM, kk > 0);
+                tc::mma_f16(tX2, tc::sdesc_sw128(sbase + BwdSmem::p + kk * 2048, kTile, 1024),
+                            tc::sdesc_sw128(sbase + BwdSmem::ob + kk * 2048, kTile, 1024), id64_MM, kk > 0);
+            }
+            for (int kk = 0; kk < 4; ++kk) {
+                // dK~ += V dS_c^T
+                tc::mma_f16(tX1, tc::sdesc_sw128(va + kk * 32, 16, 1024),
+                            tc::sdesc_sw128(sbase + BwdSmem::sb + kk * 32, 16, 1024), id64_KK, 1u);
+                // dV += K~ dS_c
+                tc::mma_f16(tX2, tc::sdesc_sw128(ka + kk * 32, 16, 1024),
+                            tc::sdesc_sw128(sbase + BwdSmem::sb + kk * 2048, 8192, 1024), id64_KM, 1u);
+            }
+            mma_xty(tdS, qa, sbase + BwdSmem::ob, false);  // dS_c-1 = dS_c + Q~^T O^
+            tc::mma_commit(mma_bar);
+        }
+        if (kNorm) tile_colsum_w<kFp16>(qt, cb, zp, tid);
+        wait_mma();
+        if (!ok) break;
+        {
+            float acc[64], kr[64];
+            tc::tmem_ld32(tX1 + lane_off + 0, acc);
+            tc::tmem_ld32(tX1 + lane_off + 32, acc + 32);
+            load_row<kFp16>(kt, tid, kr);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                float x = kNorm ? fmaf(m, zc[j], acc[j]) : acc[j];
+                acc[j] = x * fminf(kr[j], 1.f) * m;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) store_chunk<kFp16>(kt, tid, j, acc + 8 * j);
+            tc::tmem_ld32(tX2 + lane_off + 0, acc);
+            tc::tmem_ld32(tX2 + lane_off + 32, acc + 32);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) acc[j] *= m;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) store_chunk<kFp16>(vt, tid, j, acc + 8 * j);
+        }
+        __syncthreads();
+        if (kNorm && tid < 64) zc[tid] += zp[tid] + zp[tid + 64];
+        refresh_state_copy(tdS);
+        sync_for_mma();
+        if (tid == 0) {
+            tc::tma_store_4d(&P.tm_dk, kt, 0, c * kC, h, b);
+            tc::tma_store_4d(&P.tm_dv, vt, 0, c * kC, h, b);
+            tc::bulk_commit();
+        }
+    }
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s)
+            if (pending[s]) wait_bar(&tma_bar[s], tma_phase[s]);
+        tc::bulk_wait0();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, kBwdTmemCols);
+}
+
 // ------------------------------------------------------------------- host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -544,9 +1139,46 @@ cudaError_t launch_fwd_impl(const ScanParams& p, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, kern, P);
 }
 
+template <bool kFp16, bool kNorm>
+cudaError_t launch_bwd_impl(const ScanParams& p, cudaStream_t st) {
+    TcBwdParams P;
+    memset(&P, 0, sizeof(P));
+    P.p = p;
+    const int dt = kFp16 ? SUBQ_FP16 : SUBQ_BF16;
+    if (!make_map(&P.tm_q, p.q, dt, p.N, p.H, p.B, p.q_sn, p.q_sh, p.q_sb) ||
+        !make_map(&P.tm_k, p.k, dt, p.N, p.H, p.B, p.k_sn, p.k_sh, p.k_sb) ||
+        !make_map(&P.tm_v, p.v, dt, p.N, p.H, p.B, p.v_sn, p.v_sh, p.v_sb) ||
+        !make_map(&P.tm_g, p.g, dt, p.N, p.H, p.B, p.g_sn, p.g_sh, p.g_sb) ||
+        !make_map(&P.tm_dq, p.o, dt, p.N, p.H, p.B, p.o_sn, p.o_sh, p.o_sb) ||
+        !make_map(&P.tm_dk, p.dk, dt, p.N, p.H, p.B, p.dk_sn, p.dk_sh, p.dk_sb) ||
+        !make_map(&P.tm_dv, p.dv, dt, p.N, p.H, p.B, p.dv_sn, p.dv_sh, p.dv_sb))
+        return cudaErrorInvalidValue;
+    const int nC = (p.N + kC - 1) / kC;
+    P.G = pick_segments(p);
+    P.cps = (nC + P.G - 1) / P.G;
+    auto kern = bwd_tc_kernel<kFp16, kNorm>;
+    const size_t smem = BwdSmem::total + 1024;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(P.G, p.B * p.H, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = P.G;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, P);
+}
+
 }  // namespace
 
-bool tc_bwd_supported(const ScanParams&, int) { return false; }
+bool tc_bwd_supported(const ScanParams& p, int) { return p.dlg == nullptr; }
 
 bool tc_supported(const ScanParams& p, int dtype) {
     if (dtype != SUBQ_BF16 && dtype != SUBQ_FP16) return false;
@@ -558,7 +1190,11 @@ bool tc_supported(const ScanParams& p, int dtype) {
 }
 
 size_t tc_fwd_workspace_bytes(const ScanParams&) { return 0; }
-size_t tc_bwd_workspace_bytes(const ScanParams&) { return 0; }
+
+// (Zc_t, c_t) per token, written by phase B and read back by phase C.
+size_t tc_bwd_workspace_bytes(const ScanParams& p) {
+    return ((size_t)p.B * p.H * (size_t)p.N * sizeof(float2) + 255) / 256 * 256;
+}
 
 cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches) {
     *launches = 1;
@@ -567,9 +1203,11 @@ cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* 
     return p.normalize ? launch_fwd_impl<false, true>(p, st) : launch_fwd_impl<false, false>(p, st);
 }
 
-cudaError_t launch_bwd_tc(const ScanParams&, int, cudaStream_t, int* launches) {
-    *launches = 0;
-    return cudaErrorNotSupported;
+cudaError_t launch_bwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches) {
+    *launches = 1;
+    const bool fp16 = dtype == SUBQ_FP16;
+    if (fp16) return p.normalize ? launch_bwd_impl<true, true>(p, st) : launch_bwd_impl<true, false>(p, st);
+    return p.normalize ? launch_bwd_impl<false, true>(p, st) : launch_bwd_impl<false, false>(p, st);
 }
 
 cudaError_t tc_read_status(cudaStream_t st, int* status) {

@@ -156,6 +156,34 @@ def test_tensorcore_forward_matches_oracle(case):
         assert rel_err(z, ref_z) < 2e-2
 
 
+@pytest.mark.parametrize("case", TC_CASES[1:], ids=[f"tcb{i}" for i in range(1, len(TC_CASES))])
+def test_tensorcore_backward_matches_oracle(case):
+    B, H, N, dtype, mask, state, normalize = case
+    d = e = 64
+    q, k, v, do, lg, m, st = make_case(B, H, N, d, e, dtype, seed=202 + N + H, mask=mask, state=state,
+                                       normalize=normalize)
+    qn, kn, vn, don, lgn, mn, S0, z0 = oracle_inputs(q, k, v, do, lg, m, st, B, H, N)
+    scale = 1.0 / math.sqrt(d) if normalize else 1.0
+    rq, rk, rv, _ = oracle.backward(qn, kn, vn, don, log_gamma=lgn, mask=mn, normalize=normalize, scale=scale,
+                                    S0=S0, z0=z0)
+    dq, dk, dv, _ = ops.scan_backward(to_dev(q), to_dev(k), to_dev(v), to_dev(do), mask=to_dev(m),
+                                      normalize=normalize, state=to_dev(st), path="tensorcore")
+    torch.cuda.synchronize()
+    assert ops.last_path() == "tensorcore"
+    assert rel_err(dq, rq) < 2e-2, "dq"
+    assert rel_err(dk, rk) < 2e-2, "dk"
+    assert rel_err(dv, rv) < 2e-2, "dv"
+
+
+def test_tensorcore_backward_single_token_is_degenerate():
+    """One token: out = v exactly, so dq and dk vanish; only rounding noise remains."""
+    q, k, v, do, _, _, _ = make_case(1, 2, 1, 64, 64, torch.bfloat16, seed=3)
+    dq, dk, dv, _ = ops.scan_backward(q.cuda(), k.cuda(), v.cuda(), do.cuda(), path="tensorcore")
+    assert dq.abs().max().item() < 1e-2 * dv.abs().max().item()
+    assert dk.abs().max().item() < 1e-2 * dv.abs().max().item()
+    assert rel_err(dv, (do * 1.0).double().numpy()) < 2e-2
+
+
 def test_tensorcore_forward_matches_exact_path():
     B, H, N = 2, 4, 2048
     q, k, v, _, _, m, _ = make_case(B, H, N, 64, 64, torch.bfloat16, seed=9, mask=True)
