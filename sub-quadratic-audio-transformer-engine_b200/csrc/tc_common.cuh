@@ -1,0 +1,162 @@
+// Shared pieces of the tensor-core scan kernels (forward and backward):
+// tile geometry, 16-bit element helpers, the feature map, bounded waits,
+// swizzled-tile row helpers and the host-side launch plumbing.
+#pragma once
+
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <string.h>
+
+#include "scan_common.cuh"
+#include "scan_launch.h"
+#include "tc_ptx.cuh"
+
+namespace subq {
+namespace tcs {
+
+constexpr int kC = 128;                  // tokens per chunk (MMA M)
+constexpr int kD = 64;                   // head_dim = value_dim on this path
+constexpr int kThreads = 256;            // 8 warps: row = 32 * (warp % 4) + lane, column half = warp / 4
+constexpr uint32_t kTile = kC * kD * 2;  // one 128 x 64 16-bit tile, 128-byte swizzle (16 KB)
+constexpr uint32_t kMTile = kC * 16 * 2; // one 128 x 16 16-bit tile, 32-byte swizzle (4 KB)
+constexpr uint32_t kSpinLimit = 1u << 25;
+
+template <bool kFp16>
+struct Elem;
+template <>
+struct Elem<false> {
+    using T = __nv_bfloat16;
+    using T2 = __nv_bfloat162;
+    static __device__ __forceinline__ float2 to2(T2 x) { return __bfloat1622float2(x); }
+    static __device__ __forceinline__ T2 from2(float a, float b) { return __floats2bfloat162_rn(a, b); }
+};
+template <>
+struct Elem<true> {
+    using T = __half;
+    using T2 = __half2;
+    static __device__ __forceinline__ float2 to2(T2 x) { return __half22float2(x); }
+    static __device__ __forceinline__ T2 from2(float a, float b) { return __floats2half2_rn(a, b); }
+};
+
+// phi(x) = ELU(x) + 1 with the fast exponential intrinsic on non-positive inputs.
+__device__ __forceinline__ float phi_fast(float x) { return x > 0.f ? x + 1.f : __expf(x); }
+
+// Bounded mbarrier wait; on expiry records SUBQ_ERR_TIMEOUT in *status (the
+// library's device status word) and returns false.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (tc::mbar_try_wait(bar, parity)) return true;
+    atomicCAS(status, 0, (int)SUBQ_ERR_TIMEOUT);
+    return false;
+}
+
+// f(j, v[8]) over the 16-byte chunks j in [j0, j0 + nj) of row r of a 128-byte
+// swizzled tile, in place.
+template <bool kFp16, typename F>
+__device__ __forceinline__ void chunks_transform(uint8_t* tile, int r, int j0, int nj, F&& f) {
+    using E = Elem<kFp16>;
+#pragma unroll
+    for (int jj = 0; jj < nj; ++jj) {
+        const int j = j0 + jj;
+        uint4* ptr = reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, j));
+        uint4 raw = *ptr;
+        typename E::T2* h = reinterpret_cast<typename E::T2*>(&raw);
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f2 = E::to2(h[i]);
+            v[2 * i] = f2.x;
+            v[2 * i + 1] = f2.y;
+        }
+        f(j, v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = E::from2(v[2 * i], v[2 * i + 1]);
+        *ptr = raw;
+    }
+}
+
+template <bool kFp16>
+__device__ __forceinline__ void store_chunk(uint8_t* tile, int r, int j, const float* v) {
+    using E = Elem<kFp16>;
+    uint4 raw;
+    typename E::T2* h = reinterpret_cast<typename E::T2*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = E::from2(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, j)) = raw;
+}
+
+template <bool kFp16>
+__device__ __forceinline__ void load_chunks(const uint8_t* tile, int r, int j0, int nj, float* out) {
+    using E = Elem<kFp16>;
+#pragma unroll
+    for (int jj = 0; jj < nj; ++jj) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(tile + tc::sw128_chunk(r, j0 + jj));
+        const typename E::T2* h = reinterpret_cast<const typename E::T2*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f2 = E::to2(h[i]);
+            out[8 * jj + 2 * i] = f2.x;
+            out[8 * jj + 2 * i + 1] = f2.y;
+        }
+    }
+}
+
+__device__ __forceinline__ void zero_chunks(uint8_t* tile, int r, int j0, int nj) {
+#pragma unroll
+    for (int jj = 0; jj < nj; ++jj) *reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, j0 + jj)) = make_uint4(0, 0, 0, 0);
+}
+
+// Row r of a 128 x 16 tile with a 32-byte swizzle (16-byte chunk j of row r
+// lands at chunk j ^ ((r >> 2) & 1)): value x in column 0, zeros elsewhere.
+template <bool kFp16>
+__device__ __forceinline__ void mtile_row(uint8_t* tile, int r, float x) {
+    using E = Elem<kFp16>;
+    uint4 c0 = make_uint4(0, 0, 0, 0);
+    typename E::T2* h = reinterpret_cast<typename E::T2*>(&c0);
+    h[0] = E::from2(x, 0.f);
+    const int sw = (r >> 2) & 1;
+    *reinterpret_cast<uint4*>(tile + r * 32 + (sw << 4)) = c0;
+    *reinterpret_cast<uint4*>(tile + r * 32 + ((sw ^ 1) << 4)) = make_uint4(0, 0, 0, 0);
+}
+
+// Row r of the same 128 x 16 tile with values x0, x1 in columns 0 and 1.
+template <bool kFp16>
+__device__ __forceinline__ void mtile_row2(uint8_t* tile, int r, float x0, float x1) {
+    using E = Elem<kFp16>;
+    uint4 c0 = make_uint4(0, 0, 0, 0);
+    typename E::T2* h = reinterpret_cast<typename E::T2*>(&c0);
+    h[0] = E::from2(x0, x1);
+    const int sw = (r >> 2) & 1;
+    *reinterpret_cast<uint4*>(tile + r * 32 + (sw << 4)) = c0;
+    *reinterpret_cast<uint4*>(tile + r * 32 + ((sw ^ 1) << 4)) = make_uint4(0, 0, 0, 0);
+}
+
+// 32-byte-swizzled MN-major operand (N = 16): SBO = 256 B between 8-row groups.
+__device__ __forceinline__ uint64_t sdesc_sw32(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((512u >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((256u >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)6 << 61;
+    return d;
+}
+
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    return __uint_as_float(r);
+}
+
+// Launch plumbing (scan_tc.cu).
+struct Maps;
+bool make_map(CUtensorMap* m, const void* base, int dtype, int N, int H, int B, int64_t sn, int64_t sh, int64_t sb);
+int pick_segments(const ScanParams& p);
+int* status_ptr();  // device address of the status word (current device)
+cudaError_t launch_cluster(const void* kern, int G, int BH, size_t smem, cudaStream_t st, void** args);
+
+}  // namespace tcs
+}  // namespace subq
