@@ -139,6 +139,12 @@ size_t subq_bwd_workspace_bytes(const subq_bwd_args* args);
 /* In-place phi(x) = ELU(x) + 1 over n contiguous elements (run_feature_map). */
 int subq_feature_map(void* x, int64_t n, int32_t dtype, void* stream);
 
+/* Synchronises `stream`, then reads and clears the device status word of the
+ * current device: SUBQ_OK, or SUBQ_ERR_TIMEOUT when a bounded device-side wait
+ * of a tensor-core kernel gave up since the last query (its outputs are then
+ * not valid). Returns SUBQ_ERR_CUDA if the synchronisation itself fails. */
+int subq_device_status(void* stream, int* status);
+
 /* Kernel path the last successful subq_fwd / subq_bwd of this thread ran. */
 int subq_last_path(void);
 

@@ -160,6 +160,15 @@ const char* subq_last_error(void) { return g_last_error.c_str(); }
 
 int subq_last_path(void) { return g_last_path; }
 
+int subq_device_status(void* stream, int* status) {
+    if (!status) return fail(SUBQ_ERR_INVALID_ARGUMENT, "status is null");
+    int v = 0;
+    cudaError_t err = subq::tc_read_status(static_cast<cudaStream_t>(stream), &v);
+    if (err != cudaSuccess) return fail_cuda(err, "subq_device_status");
+    *status = v;
+    return SUBQ_OK;
+}
+
 int subq_last_launches(void) { return g_last_launches; }
 
 size_t subq_fwd_workspace_bytes(const subq_fwd_args* a) {

@@ -89,13 +89,13 @@ int pick_segments(const ScanParams& p) {
     return G;
 }
 
-cudaError_t launch_cluster(const void* kern, int G, int BH, size_t smem, cudaStream_t st, void** args) {
+cudaError_t launch_cluster(const void* kern, int G, int BH, int threads, size_t smem, cudaStream_t st, void** args) {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(G, BH, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

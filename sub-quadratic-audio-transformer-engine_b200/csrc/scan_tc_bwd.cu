@@ -632,7 +632,7 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     P.cps = (nC + P.G - 1) / P.G;
     const void* kern = reinterpret_cast<const void*>(&bwd_kernel<kFp16, kNorm>);
     void* args[] = {&P};
-    return launch_cluster(kern, P.G, p.B * p.H, BwdLayout::total + 1024, st, args);
+    return launch_cluster(kern, P.G, p.B * p.H, kThreads, BwdLayout::total + 1024, st, args);
 }
 
 }  // namespace

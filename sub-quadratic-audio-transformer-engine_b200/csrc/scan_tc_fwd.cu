@@ -1,23 +1,28 @@
-// Tensor-core forward scan (d = e = 64, bf16/fp16 inputs, fp32 accumulation).
+// Tensor-core forward scan (d = e = 64, bf16/fp16 inputs, fp32 accumulation),
+// warp-specialised and pipelined across chunks.
 //
 // One cluster of G CTAs per (batch, head) sequence; CTA g owns segment g
 // (a run of 128-token chunks). Per chunk (t, tau index the chunk's tokens):
-//   P       = phi~(Q) phi~(K)^T                 tcgen05 128x128x64   -> TMEM
-//   P      <- P [tau <= t];  Z_t = sum_tau P + phi~(q_t) . z_c         (registers)
-//   O       = phi~(Q) S_c + P V                 tcgen05 128x64x64 + 128x64x128
-//   S_c+1   = S_c + phi~(K)^T V                 tcgen05 64x64x128, TMEM-resident fp32
-//   z_c+1   = z_c + phi~(K)^T m                 tcgen05 64x16x128 against a mask column
-//   out_t   = O_t / max(Z_t, clamp)  (normalised)  or  O_t
-// with phi~(q) = scale phi(q), phi~(k) = m phi(k) (masked keys drop out of P,
-// S and z). The bf16 copy of S in shared memory is the next chunk's operand.
+//   P      = phi~(Q) phi~(K)^T                   tcgen05 128x128x64 -> TMEM P[b]
+//   P     <- P [tau <= t];  r_t = sum_tau P            (compute warps)
+//   [O|Zi] = phi~(Q) [S_c | z_c]                 tcgen05 128x80x64  -> TMEM O'[b]
+//   O     += P V                                 tcgen05 128x64x128
+//   [S|z] += phi~(K)^T [V | 1]                   tcgen05 64x80x128, TMEM-resident fp32
+//   out_t  = O_t / max(r_t + Zi_t, clamp)  (normalised)  or  O_t
+// with phi~(q) = scale phi(q) and phi~(k) = m phi(k): masked keys drop out of
+// P, S and z (z = phi~(K)^T 1). The normaliser rides along as an extra 16
+// output columns of the state MMAs; bf16 [S_c | z_c] in shared memory is the
+// next chunk's operand.
 //
-// Segment prefix: CTA g first sums phi~(K)^T V and phi~(K)^T m over its own
-// segment (phase 1), publishes them in shared memory, and after a cluster
-// barrier adds those of CTAs 0..g-1 (read over DSMEM) to the incoming state;
-// phase 2 re-reads K and V, mostly from L2.
+// Roles (448 threads): warps 0-7 compute (TMEM lane = 32 (warp % 4) + lane,
+// column half = warp / 4); warps 8-11 transform (feature map in shared
+// memory); warp 12 TMA producer; warp 13 MMA issuer. P and O' are
+// double-buffered in TMEM: while the tensor core runs chunk c's O and state
+// MMAs, the compute warps mask P of chunk c+1.
 //
-// Threads: 256. TMEM lane / chunk row = 32 * (warp % 4) + lane; the two warps
-// of a TMEM quadrant split each row's columns (half = warp / 4).
+// Segment prefix: CTA g first sums phi~(K)^T [V | 1] over its own segment
+// (phase 1), publishes the sums in shared memory, and after a cluster barrier
+// adds those of CTAs 0..g-1 (read over DSMEM) to the incoming state.
 //
 // Reference algorithm: python/subq_audio/autograd.py:108-169 (chunked scan),
 // :292-376 (normaliser, clamp, mask); recurrence of
@@ -31,26 +36,46 @@ namespace tcs {
 namespace {
 
 constexpr int kStages = 3;
+constexpr int kFwdThreads = 448;
+constexpr int kComputeThreads = 256, kTransformThreads = 128;
+constexpr int kBarCompute = 1, kBarTransform = 2;  // named barrier ids
+constexpr int kWarpProducer = 12, kWarpMma = 13;
+constexpr int kNX = 80;  // state / output MMA width: 64 value columns + 16 normaliser columns
 
-struct FwdLayout {
+struct L {
     static constexpr uint32_t stage = 3 * kTile;  // q, k, v
     static constexpr uint32_t q = 0, k = kTile, v = 2 * kTile;
-    static constexpr uint32_t p = kStages * stage;  // P (two 64-column blocks); exchange buffer between phases
-    static constexpr uint32_t sb = p + 2 * kTile;   // bf16 S_c (MN-major B operand)
-    static constexpr uint32_t mt = sb + kD * kD * 2;  // mask column tile (128 x 16, 32-byte swizzle)
-    static constexpr uint32_t zc = mt + kMTile;     // z_c fp32 [64]
-    static constexpr uint32_t zq = zc + 256;        // partial phi~(q).z_c [2][128]
-    static constexpr uint32_t rs = zq + 1024;       // partial row sums of P [2][128]
-    static constexpr uint32_t bars = rs + 1024;     // tma[kStages], mma
-    static constexpr uint32_t tslot = bars + 8 * (kStages + 1);
+    static constexpr uint32_t ones = kStages * stage;  // 128 x 64 atom, column 0 = 1 (the "| 1" of [V | 1])
+    static constexpr uint32_t sb = ones + kTile;       // bf16 [S_c | z_c]: two 64 x 64 atoms (MN-major B)
+    static constexpr uint32_t os = sb + 2 * kD * kD * 2;  // output staging
+    static constexpr uint32_t xs = os + kTile;         // segment-sum exchange: [64][64] + [64] fp32
+    static constexpr uint32_t rs = xs + kD * kD * 4 + 1024;  // partial row sums [2 buf][2 half][128]
+    static constexpr uint32_t bars = rs + 2048;
+    static constexpr uint32_t tslot = bars + 8 * 24;
     static constexpr uint32_t total = tslot + 16;
 };
-static_assert(FwdLayout::p % 1024 == 0 && FwdLayout::sb % 1024 == 0 && FwdLayout::mt % 1024 == 0, "alignment");
-static_assert(FwdLayout::total + 1024 <= 232448, "shared memory");
+static_assert(L::stage % 1024 == 0 && L::ones % 1024 == 0 && L::sb % 1024 == 0 && L::os % 1024 == 0,
+              "alignment");
+static_assert(L::total + 1024 <= 232448, "shared memory");
 
-// TMEM (fp32 columns): P [0,128), O [128,192), S [192,256) (M=64), z' [256,288) (M=64, column 0 = z).
+enum {
+    B_FULL = 0,                    // [kStages] TMA -> transform
+    B_TDONE = B_FULL + kStages,    // [kStages] transform -> MMA
+    B_EMPTY = B_TDONE + kStages,   // [kStages] MMA -> producer
+    B_PFULL = B_EMPTY + kStages,   // [2] MMA -> compute (P ready)
+    B_PSDONE = B_PFULL + 2,        // [2] compute -> MMA (P consumed, bf16 P written)
+    B_OFULL = B_PSDONE + 2,        // [2] MMA -> compute (O' ready)
+    B_ODONE = B_OFULL + 2,         // [2] compute -> MMA (O' consumed)
+    B_SFULL = B_ODONE + 2,         // MMA -> compute (state updated)
+    B_SBDONE = B_SFULL + 1,        // compute -> MMA (state read, bf16 copy written)
+    B_COUNT = B_SBDONE + 1
+};
+static_assert(B_COUNT <= 24, "barrier slots");
+
+// TMEM (512 fp32 columns): P0 [0,128) P1 [128,256) O'0 [256,336) O'1 [336,416)
+// S' [416,496) (M = 64 layout; column 64 of S' is z, column 64 of O' is Zi).
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t cP = 0, cO = 128, cS = 192, cZ = 256;
+constexpr uint32_t cP = 0, cO = 256, cS = 416;
 
 struct FwdParams {
     CUtensorMap tm_q, tm_k, tm_v, tm_o;
@@ -61,7 +86,7 @@ struct FwdParams {
 };
 
 template <bool kFp16, bool kNorm>
-__global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant__ FwdParams P) {
+__global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdParams P) {
     const ScanParams& p = P.p;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -71,137 +96,148 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     const int bh = blockIdx.y;
     const int b = bh / p.H, h = bh - b * p.H;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quad = warp & 3, hf = warp >> 2;
-    const int row = quad * 32 + lane;   // chunk row == TMEM lane
-    const int srow = quad * 16 + lane;  // state row held by lanes < 16 (M = 64 layout)
     const int nC = (p.N + kC - 1) / kC;
     const int c_begin = min(nC, g * P.cps);
     const int n = min(nC, c_begin + P.cps) - c_begin;
+    const int n1 = (g < P.G - 1) ? n : 0;  // phase-1 chunks
 
-    uint64_t* tma_bar = reinterpret_cast<uint64_t*>(sm + FwdLayout::bars);
-    uint64_t* mma_bar = tma_bar + kStages;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + FwdLayout::tslot);
-    float* zc = reinterpret_cast<float*>(sm + FwdLayout::zc);
-    float* zqs = reinterpret_cast<float*>(sm + FwdLayout::zq);
-    float* rss = reinterpret_cast<float*>(sm + FwdLayout::rs);
-    uint8_t* Pt = sm + FwdLayout::p;
-    uint8_t* Sb = sm + FwdLayout::sb;
-    uint8_t* Mt = sm + FwdLayout::mt;
-    float* Xs = reinterpret_cast<float*>(Pt);                // [64][64] segment sum phi~(K)^T V
-    float* Xz = reinterpret_cast<float*>(Pt + kD * kD * 4);  // [64] segment sum phi~(K)^T m
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::bars);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L::tslot);
+    float* rsm = reinterpret_cast<float*>(sm + L::rs);
+    float* Xs = reinterpret_cast<float*>(sm + L::xs);                // [64][64] segment sum phi~(K)^T V
+    float* Xz = reinterpret_cast<float*>(sm + L::xs + kD * kD * 4);  // [64] segment sum phi~(K)^T 1
+    const uint32_t sbase = tc::smem_u32(sm);
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) tc::mbar_init(&tma_bar[s], 1);
-        tc::mbar_init(mma_bar, 1);
+        for (int i = 0; i < B_COUNT; ++i) tc::mbar_init(&bars[i], 1);
         tc::fence_mbar_init();
-        tc::prefetch_tmap(&P.tm_q);
-        tc::prefetch_tmap(&P.tm_k);
-        tc::prefetch_tmap(&P.tm_v);
-        tc::prefetch_tmap(&P.tm_o);
     }
-    if (warp == 0) tc::tmem_alloc(tslot, kTmemCols);
+    if (warp == kWarpMma) tc::tmem_alloc(tslot, kTmemCols);
+    if (warp >= 8 && warp < 12) {  // the constant ones column (chunks 0-1 of each row; others never read)
+        const int r = tid - 256;
+        float one[8] = {1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        store_chunk<kFp16>(sm + L::ones, r, 0, one);
+        zero_chunks(sm + L::ones, r, 1, 1);
+        tc::fence_proxy_async();
+    }
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tslot;
-    const uint32_t loff = (uint32_t)(quad * 32) << 16;
-    const uint32_t tP = tmem + cP, tO = tmem + cO, tS = tmem + cS, tZ = tmem + cZ;
-    const uint32_t sbase = tc::smem_u32(sm);
-
-    bool ok = true;
-    uint32_t tma_phase[kStages];
-    int pending[kStages];
-    for (int s = 0; s < kStages; ++s) {
-        tma_phase[s] = 0;
-        pending[s] = 0;
-    }
-    uint32_t mma_phase = 0;
 
     constexpr uint32_t idP = tc::idesc_f16<kFp16>(128, 128, false, false);
-    constexpr uint32_t idO = tc::idesc_f16<kFp16>(128, 64, false, true);
-    constexpr uint32_t idS = tc::idesc_f16<kFp16>(64, 64, true, true);
-    constexpr uint32_t idZ = tc::idesc_f16<kFp16>(64, 16, true, true);
+    constexpr uint32_t idOX = tc::idesc_f16<kFp16>(128, kNX, false, true);  // phi~(Q) [S | z]
+    constexpr uint32_t idO = tc::idesc_f16<kFp16>(128, 64, false, true);    // P V
+    constexpr uint32_t idSX = tc::idesc_f16<kFp16>(64, kNX, true, true);    // phi~(K)^T [V | 1]
 
-    auto issue = [&](int chunk, int s, bool with_q) {
-        const int t0 = chunk * kC;
-        pending[s] = 1;
-        uint8_t* base = sm + s * FwdLayout::stage;
-        tc::mbar_arrive_expect_tx(&tma_bar[s], (with_q ? 3u : 2u) * kTile);
-        if (with_q) tc::tma_load_4d(base + FwdLayout::q, &P.tm_q, 0, t0, h, b, &tma_bar[s]);
-        tc::tma_load_4d(base + FwdLayout::k, &P.tm_k, 0, t0, h, b, &tma_bar[s]);
-        tc::tma_load_4d(base + FwdLayout::v, &P.tm_v, 0, t0, h, b, &tma_bar[s]);
-    };
-    auto row_mask = [&](int chunk) -> float {
-        const int t = chunk * kC + row;
+    auto row_mask_at = [&](int chunk, int r) -> float {
+        const int t = chunk * kC + r;
         if (t >= p.N) return 0.f;
         return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
     };
-    auto wait_tma = [&](int s) {
-        ok = __syncthreads_and(wait_bar(&tma_bar[s], tma_phase[s], P.status)) && ok;
-        tma_phase[s] ^= 1u;
-        pending[s] = 0;
-    };
-    auto wait_mma = [&]() {
-        ok = __syncthreads_and(wait_bar(mma_bar, mma_phase, P.status)) && ok;
-        mma_phase ^= 1u;
-        tc::tc_fence_after();
-    };
-    auto publish = [&]() {  // generic-proxy smem writes -> MMA, TMEM reads done -> next MMA
-        tc::fence_proxy_async();
-        tc::tc_fence_before();
-        __syncthreads();
-    };
-    // S (+)= phi~(K)^T V and z' (+)= phi~(K)^T m over one chunk.
+    // [S|z] (+)= phi~(K)^T [V | 1] over the chunk in stage s (8 K-steps of 16 tokens).
     auto mma_state = [&](int s, bool first) {
-        const uint32_t ka = sbase + s * FwdLayout::stage + FwdLayout::k;
-        const uint32_t va = sbase + s * FwdLayout::stage + FwdLayout::v;
-        const uint32_t ma = sbase + FwdLayout::mt;
-        for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = tc::sdesc_sw128(ka + kk * 2048, kTile, 1024);
-            tc::mma_f16(tS, ad, tc::sdesc_sw128(va + kk * 2048, kTile, 1024), idS, (first && kk == 0) ? 0u : 1u);
-            if (kNorm) tc::mma_f16(tZ, ad, sdesc_sw32(ma + kk * 512), idZ, (first && kk == 0) ? 0u : 1u);
+        const uint32_t ka = sbase + s * L::stage + L::k, va = sbase + s * L::stage + L::v;
+        const uint32_t lbo = L::ones - (s * L::stage + L::v);  // V atom -> ones atom
+        const uint32_t n80 = kNorm ? idSX : tc::idesc_f16<kFp16>(64, 64, true, true);
+        for (int kk = 0; kk < 8; ++kk)
+            tc::mma_f16(tmem + cS, tc::sdesc_sw128(ka + kk * 2048, kTile, 1024),
+                        tc::sdesc_sw128(va + kk * 2048, lbo, 1024), n80, (first && kk == 0) ? 0u : 1u);
+    };
+
+    bool ok = true;
+
+    auto produce = [&](int jlo, int jhi) {
+        for (int j = jlo; j < jhi && ok; ++j) {
+            const bool ph2 = j >= n1;
+            const int chunk = c_begin + (ph2 ? j - n1 : j);
+            const int s = j % kStages, u = j / kStages;
+            if (u >= 1) ok = wait_bar(&bars[B_EMPTY + s], (u - 1) & 1, P.status);
+            if (!ok) break;
+            uint8_t* base = sm + s * L::stage;
+            tc::mbar_arrive_expect_tx(&bars[B_FULL + s], (ph2 ? 3u : 2u) * kTile);
+            if (ph2) tc::tma_load_4d(base + L::q, &P.tm_q, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + L::k, &P.tm_k, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + L::v, &P.tm_v, 0, chunk * kC, h, b, &bars[B_FULL + s]);
         }
     };
-    auto transform_k = [&](uint8_t* kt, float m) {
-        chunks_transform<kFp16>(kt, row, hf * 4, 4, [&](int, float* v) {
+    auto transform = [&](int jlo, int jhi) {
+        const int r = tid - 256;
+        for (int j = jlo; j < jhi && ok; ++j) {
+            const bool ph2 = j >= n1;
+            const int chunk = c_begin + (ph2 ? j - n1 : j);
+            const int s = j % kStages, u = j / kStages;
+            ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
+            if (!ok) break;
+            uint8_t* base = sm + s * L::stage;
+            const float m = row_mask_at(chunk, r);
+            if (ph2) {
+                chunks_transform<kFp16>(base + L::q, r, 0, 8, [&](int, float* v) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = phi_fast(v[u]) * m;
-        });
-        if (kNorm && hf == 0) mtile_row<kFp16>(Mt, row, m);
+                    for (int x = 0; x < 8; ++x) v[x] = phi_fast(v[x]) * p.scale;
+                });
+            }
+            chunks_transform<kFp16>(base + L::k, r, 0, 8, [&](int, float* v) {
+#pragma unroll
+                for (int x = 0; x < 8; ++x) v[x] = phi_fast(v[x]) * m;
+            });
+            tc::fence_proxy_async();
+            tc::bar_sync(kBarTransform, kTransformThreads);
+            if (r == 0) tc::mbar_arrive(&bars[B_TDONE + s]);
+        }
     };
 
     // ------------------------------------------------------------ phase 1
-    if (g < P.G - 1) {
-        if (tid == 0)
-            for (int j = 0; j < kStages - 1 && j < n; ++j) issue(c_begin + j, j, false);
-        for (int i = 0; i < n && ok; ++i) {
-            const int s = i % kStages;
-            if (tid == 0 && i + kStages - 1 < n) issue(c_begin + i + kStages - 1, (i + kStages - 1) % kStages, false);
-            wait_tma(s);
-            if (!ok) break;
-            transform_k(sm + s * FwdLayout::stage + FwdLayout::k, row_mask(c_begin + i));
-            publish();
-            if (tid == 0) {
+    if (warp == kWarpProducer) {
+        if (lane == 0) {
+            tc::prefetch_tmap(&P.tm_q);
+            tc::prefetch_tmap(&P.tm_k);
+            tc::prefetch_tmap(&P.tm_v);
+            tc::prefetch_tmap(&P.tm_o);
+            produce(0, n1 + min(n, kStages));  // later phase-2 stages are freed only after the barriers
+        }
+        __syncwarp();
+    } else if (warp >= 8 && warp < 12) {
+        transform(0, n1);
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            for (int j = 0; j < n1 && ok; ++j) {
+                const int s = j % kStages, u = j / kStages;
+                ok = wait_bar(&bars[B_TDONE + s], u & 1, P.status);
+                if (!ok) break;
                 tc::tc_fence_after();
-                mma_state(s, i == 0);
-                tc::mma_commit(mma_bar);
+                mma_state(s, j == 0);
+                tc::mma_commit(&bars[B_EMPTY + s]);
             }
-            wait_mma();
+            if (n1 > 0 && ok) tc::mma_commit(&bars[B_SFULL]);
         }
-        float v[32];
-        if (n > 0 && ok) {
-            tc::tmem_ld32(tS + loff + hf * 32, v);
-        } else {
+        __syncwarp();
+    }
+    uint32_t sfull_count = 0;
+    if (warp < 8) {
+        const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
+        const uint32_t loff = (uint32_t)(quad * 32) << 16;
+        if (n1 > 0) {
+            ok = tc::bar_and(kBarCompute, kComputeThreads, wait_bar(&bars[B_SFULL], 0, P.status)) && ok;
+            sfull_count = 1;
+            tc::tc_fence_after();
+        }
+        if (g < P.G - 1) {
+            float v[32];
+            if (n1 > 0 && ok) {
+                tc::tmem_ld32(tmem + cS + loff + hf * 32, v);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
-        }
-        if (lane < 16) {
+                for (int x = 0; x < 32; ++x) v[x] = 0.f;
+            }
+            if (lane < 16) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) Xs[srow * 64 + hf * 32 + j] = v[j];
-        }
-        if (hf == 0) {
-            const float zv = (kNorm && n > 0 && ok) ? tmem_ld1(tZ + loff) : 0.f;
-            if (lane < 16) Xz[srow] = zv;
+                for (int x = 0; x < 32; ++x) Xs[srow * 64 + hf * 32 + x] = v[x];
+            }
+            if (hf == 0) {
+                const float zv = (kNorm && n1 > 0 && ok) ? tmem_ld1(tmem + cS + loff + 64) : 0.f;
+                if (lane < 16) Xz[srow] = zv;
+            }
         }
     }
     tc::tc_fence_before();
@@ -209,168 +245,221 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     tc::tc_fence_after();
 
     // ------------------------------------------------------ segment prefix
-    {
+    if (warp < 8) {
+        const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
+        const uint32_t loff = (uint32_t)(quad * 32) << 16;
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        for (int x = 0; x < 32; ++x) v[x] = 0.f;
         if (lane < 16) {
             if (p.S_in) {
                 const float* src = p.S_in + ((int64_t)bh * kD + srow) * kD + hf * 32;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = src[j];
+                for (int x = 0; x < 32; ++x) v[x] = src[x];
             }
             for (int r = 0; r < g; ++r) {
                 const float* rx = cluster.map_shared_rank(Xs, r) + srow * 64 + hf * 32;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] += rx[j];
+                for (int x = 0; x < 32; ++x) v[x] += rx[x];
             }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(Sb, srow, hf * 4 + j, v + 8 * j);
+            for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + L::sb, srow, hf * 4 + x, v + 8 * x);
         }
-        tc::tmem_st32(tS + loff + hf * 32, v);
-        if (kNorm && tid < 64) {
-            float z = p.z_in ? p.z_in[(int64_t)bh * kD + tid] : 0.f;
-            for (int r = 0; r < g; ++r) z += cluster.map_shared_rank(Xz, r)[tid];
-            zc[tid] = z;
-        }
-    }
-    __syncthreads();
-    if (kNorm && hf == 0) {  // z' column 0 <- z_c (the accumulator of the mask-column MMA)
-        float v[32];
+        tc::tmem_st32(tmem + cS + loff + hf * 32, v);
+        if (hf == 0) {
+            float z = 0.f;
+            if (kNorm && lane < 16) {
+                z = p.z_in ? p.z_in[(int64_t)bh * kD + srow] : 0.f;
+                for (int r = 0; r < g; ++r) z += cluster.map_shared_rank(Xz, r)[srow];
+            }
+            if (lane < 16) {
+                float zc8[8] = {z, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                store_chunk<kFp16>(sm + L::sb + kD * kD * 2, srow, 0, zc8);
+                zero_chunks(sm + L::sb + kD * kD * 2, srow, 1, 1);
+            }
+            float w[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
-        if (lane < 16) v[0] = zc[srow];
-        tc::tmem_st32(tZ + loff, v);
+            for (int x = 0; x < 32; ++x) w[x] = 0.f;
+            w[0] = (lane < 16) ? z : 0.f;
+            tc::tmem_st32(tmem + cS + loff + 64, w);
+        }
+        tc::fence_proxy_async();
     }
-    tc::fence_proxy_async();
     tc::tc_fence_before();
-    cluster.sync();  // every remote read of the exchange buffers is done
+    cluster.sync();  // remote reads done; prefix state published
     tc::tc_fence_after();
 
-    // ------------------------------------------------------------ phase 2
-    if (tid == 0)
-        for (int j = 0; j < kStages - 1 && j < n; ++j) issue(c_begin + j, j, true);
-    for (int i = 0; i < n && ok; ++i) {
-        const int c = c_begin + i, s = i % kStages;
-        if (tid == 0 && i + kStages - 1 < n) {
-            tc::bulk_wait_read0();  // outputs staged in that stage's Q tile have been read
-            issue(c + kStages - 1, (i + kStages - 1) % kStages, true);
-        }
-        wait_tma(s);
-        if (!ok) break;
-        uint8_t* qt = sm + s * FwdLayout::stage + FwdLayout::q;
-        uint8_t* kt = sm + s * FwdLayout::stage + FwdLayout::k;
-        const uint32_t qa = sbase + s * FwdLayout::stage + FwdLayout::q;
-        const uint32_t ka = sbase + s * FwdLayout::stage + FwdLayout::k;
-        const uint32_t va = sbase + s * FwdLayout::stage + FwdLayout::v;
-        const float m = row_mask(c);
-        float zq = 0.f;
-        chunks_transform<kFp16>(qt, row, hf * 4, 4, [&](int j, float* v) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                v[u] = phi_fast(v[u]) * p.scale;
-                if (kNorm) zq = fmaf(v[u], zc[8 * j + u], zq);
+    // ============================================================ phase 2
+    if (warp == kWarpProducer) {
+        if (lane == 0) produce(n1 + min(n, kStages), n1 + n);
+        __syncwarp();
+    } else if (warp >= 8 && warp < 12) {
+        transform(n1, n1 + n);
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            auto issue_p = [&](int i) -> bool {  // P[i % 2] = phi~(Q) phi~(K)^T
+                const int j = n1 + i, s = j % kStages, u = j / kStages, bf = i & 1;
+                if (!wait_bar(&bars[B_TDONE + s], u & 1, P.status)) return false;
+                if (i >= 2 && !wait_bar(&bars[B_PSDONE + bf], ((i >> 1) - 1) & 1, P.status)) return false;
+                tc::tc_fence_after();
+                const uint32_t qa = sbase + s * L::stage + L::q, ka = sbase + s * L::stage + L::k;
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16(tmem + cP + bf * 128, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(ka + kk * 32, 16, 1024), idP, kk > 0);
+                tc::mma_commit(&bars[B_PFULL + bf]);
+                return true;
+            };
+            if (n > 0) ok = issue_p(0);
+            for (int i = 0; i < n && ok; ++i) {
+                const int j = n1 + i, s = j % kStages, bf = i & 1, pu = i >> 1;
+                if (i + 1 < n) ok = issue_p(i + 1);
+                if (ok) ok = wait_bar(&bars[B_PSDONE + bf], pu & 1, P.status);
+                if (ok && i >= 2) ok = wait_bar(&bars[B_ODONE + bf], (pu - 1) & 1, P.status);
+                if (ok && i >= 1) ok = wait_bar(&bars[B_SBDONE], (i - 1) & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                const uint32_t qa = sbase + s * L::stage + L::q, va = sbase + s * L::stage + L::v;
+                const uint32_t tOb = tmem + cO + bf * kNX;
+                for (int kk = 0; kk < 4; ++kk)  // [O | Zi] = phi~(Q) [S_c | z_c]
+                    tc::mma_f16(tOb, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(sbase + L::sb + kk * 2048, kD * kD * 2, 1024),
+                                kNorm ? idOX : idO, kk > 0);
+                for (int kk = 0; kk < 8; ++kk)  // O += P V, bf16 P read from TMEM (8 columns per 16 tokens)
+                    tc::mma_f16_ts(tOb, tmem + cP + bf * 128 + kk * 8, tc::sdesc_sw128(va + kk * 2048, kTile, 1024),
+                                   idO, 1u);
+                tc::mma_commit(&bars[B_OFULL + bf]);
+                mma_state(s, false);  // [S|z]_c+1
+                tc::mma_commit(&bars[B_SFULL]);
+                tc::mma_commit(&bars[B_EMPTY + s]);
             }
-        });
-        if (kNorm) zqs[hf * 128 + row] = zq;
-        transform_k(kt, m);
-        publish();
-        if (tid == 0) {
-            tc::tc_fence_after();
-            for (int kk = 0; kk < 4; ++kk)  // P = phi~(Q) phi~(K)^T
-                tc::mma_f16(tP, tc::sdesc_sw128(qa + kk * 32, 16, 1024), tc::sdesc_sw128(ka + kk * 32, 16, 1024), idP,
-                            kk > 0);
-            for (int kk = 0; kk < 4; ++kk)  // O = phi~(Q) S_c
-                tc::mma_f16(tO, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
-                            tc::sdesc_sw128(sbase + FwdLayout::sb + kk * 2048, 8192, 1024), idO, kk > 0);
-            tc::mma_commit(mma_bar);
         }
-        wait_mma();
-        if (!ok) break;
-        // P columns [64 hf, 64 hf + 64): causal mask on the diagonal block only; the
-        // block right of the diagonal (rows < 64, half 1) is all zero.
-        {
-            uint8_t* pb = Pt + hf * kTile;
+        __syncwarp();
+    } else if (warp < 8) {
+        const int quad = warp & 3, hf = warp >> 2;
+        const int row = quad * 32 + lane, srow = quad * 16 + lane;
+        const uint32_t loff = (uint32_t)(quad * 32) << 16;
+        // P of chunk i: causal mask on the diagonal block, row sums, and the bf16
+        // copy packed back into the first 64 TMEM columns of P[b] (the A operand
+        // of O += P V).
+        auto mask_p = [&](int i) -> bool {
+            const int bf = i & 1;
+            if (!tc::bar_and(kBarCompute, kComputeThreads, wait_bar(&bars[B_PFULL + bf], (i >> 1) & 1, P.status)))
+                return false;
+            tc::tc_fence_after();
+            using E = Elem<kFp16>;
+            uint32_t packed[32];
             float rs = 0.f;
             if (hf == 1 && quad < 2) {
-                zero_chunks(pb, row, 0, 8);
+#pragma unroll
+                for (int x = 0; x < 32; ++x) packed[x] = 0u;
             } else {
                 const bool diag = (hf == (quad >> 1));
+                float v[64];
+                tc::tmem_ld32(tmem + cP + bf * 128 + loff + hf * 64, v);
+                tc::tmem_ld32(tmem + cP + bf * 128 + loff + hf * 64 + 32, v + 32);
 #pragma unroll
-                for (int half32 = 0; half32 < 2; ++half32) {
-                    float v[32];
-                    tc::tmem_ld32(tP + loff + hf * 64 + half32 * 32, v);
+                for (int x = 0; x < 64; ++x) {
+                    if (diag && (hf * 64 + x) > row) v[x] = 0.f;
+                    rs += v[x];
+                }
 #pragma unroll
-                    for (int u = 0; u < 32; ++u) {
-                        const int tau = hf * 64 + half32 * 32 + u;
-                        if (diag && tau > row) v[u] = 0.f;
-                        rs += v[u];
-                    }
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) store_chunk<kFp16>(pb, row, half32 * 4 + q4, v + 8 * q4);
+                for (int x = 0; x < 32; ++x) {
+                    typename E::T2 h2 = E::from2(v[2 * x], v[2 * x + 1]);
+                    packed[x] = *reinterpret_cast<uint32_t*>(&h2);
                 }
             }
-            if (kNorm) rss[hf * 128 + row] = rs;
-        }
-        publish();
-        if (tid == 0) {
+            if (kNorm) rsm[(bf * 2 + hf) * 128 + row] = rs;
+            tc::tc_fence_before();
+            tc::bar_sync(kBarCompute, kComputeThreads);  // every fp32 read of P[b] is done
             tc::tc_fence_after();
-            for (int kk = 0; kk < 8; ++kk) {  // O += P V
-                const uint32_t pa = sbase + FwdLayout::p + (kk >> 2) * kTile + (kk & 3) * 32;
-                tc::mma_f16(tO, tc::sdesc_sw128(pa, 16, 1024), tc::sdesc_sw128(va + kk * 2048, kTile, 1024), idO, 1u);
+            tc::tmem_st32_raw(tmem + cP + bf * 128 + loff + hf * 32, packed);
+            tc::tc_fence_before();
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) tc::mbar_arrive(&bars[B_PSDONE + bf]);
+            return true;
+        };
+        if (n > 0) ok = mask_p(0);
+        for (int i = 0; i < n && ok; ++i) {
+            const int c = c_begin + i, bf = i & 1, pu = i >> 1;
+            if (i + 1 < n) {
+                ok = mask_p(i + 1);
+                if (!ok) break;
             }
-            mma_state(s, false);  // S_c+1, z_c+1
-            tc::mma_commit(mma_bar);
-        }
-        wait_mma();
-        if (!ok) break;
-        {
+            // state refresh: bf16 [S | z]_c+1 for the next chunk's operand
+            ok = tc::bar_and(kBarCompute, kComputeThreads,
+                             wait_bar(&bars[B_SFULL], sfull_count & 1, P.status)) && ok;
+            ++sfull_count;
+            if (!ok) break;
+            tc::tc_fence_after();
+            {
+                float v[32];
+                tc::tmem_ld32(tmem + cS + loff + hf * 32, v);
+                if (lane < 16) {
+#pragma unroll
+                    for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + L::sb, srow, hf * 4 + x, v + 8 * x);
+                }
+                if (kNorm && hf == 0) {
+                    const float zv = tmem_ld1(tmem + cS + loff + 64);
+                    if (lane < 16) {
+                        float zc8[8] = {zv, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                        store_chunk<kFp16>(sm + L::sb + kD * kD * 2, srow, 0, zc8);
+                    }
+                }
+            }
+            tc::fence_proxy_async();
+            tc::tc_fence_before();
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) tc::mbar_arrive(&bars[B_SBDONE]);
+            // output of chunk i
+            ok = tc::bar_and(kBarCompute, kComputeThreads, wait_bar(&bars[B_OFULL + bf], pu & 1, P.status)) && ok;
+            if (!ok) break;
+            tc::tc_fence_after();
             float o[32];
-            tc::tmem_ld32(tO + loff + hf * 32, o);
-            float inv = m;
-            if (kNorm) inv = m / fmaxf(rss[row] + rss[128 + row] + zqs[row] + zqs[128 + row], p.clamp_min);
+            tc::tmem_ld32(tmem + cO + bf * kNX + loff + hf * 32, o);
+            float zi = 0.f;
+            if (kNorm) zi = tmem_ld1(tmem + cO + bf * kNX + loff + 64);
+            tc::tc_fence_before();
+            if (tid == 0) tc::bulk_wait_read0();  // the previous chunk's output has left the staging tile
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) tc::mbar_arrive(&bars[B_ODONE + bf]);  // every thread has read O'[bf]
+            {
+                const float m = row_mask_at(c, row);
+                float inv = m;
+                if (kNorm) {
+                    const float z = rsm[(bf * 2) * 128 + row] + rsm[(bf * 2 + 1) * 128 + row] + zi;
+                    inv = m / fmaxf(z, p.clamp_min);
+                }
 #pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] *= inv;
+                for (int x = 0; x < 32; ++x) o[x] *= inv;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(qt, row, hf * 4 + j, o + 8 * j);
+                for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + L::os, row, hf * 4 + x, o + 8 * x);
+            }
+            tc::fence_proxy_async();
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) {
+                tc::tma_store_4d(&P.tm_o, sm + L::os, 0, c * kC, h, b);
+                tc::bulk_commit();
+            }
         }
-        {
+        if (g == P.G - 1 && ok) {  // final state of the whole sequence
             float v[32];
-            tc::tmem_ld32(tS + loff + hf * 32, v);
-            if (lane < 16) {
+            tc::tmem_ld32(tmem + cS + loff + hf * 32, v);
+            if (lane < 16 && p.S_out) {
+                float* dst = p.S_out + ((int64_t)bh * kD + srow) * kD + hf * 32;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) store_chunk<kFp16>(Sb, srow, hf * 4 + j, v + 8 * j);
+                for (int x = 0; x < 32; ++x) dst[x] = v[x];
             }
-            if (kNorm && hf == 0) {
-                const float zv = tmem_ld1(tZ + loff);
-                if (lane < 16) zc[srow] = zv;
+            if (p.z_out && hf == 0) {
+                const float zv = kNorm ? tmem_ld1(tmem + cS + loff + 64) : 0.f;
+                if (lane < 16) p.z_out[(int64_t)bh * kD + srow] = zv;
             }
         }
-        publish();
-        if (tid == 0) {
-            tc::tma_store_4d(&P.tm_o, qt, 0, c * kC, h, b);
-            tc::bulk_commit();
-        }
+        if (tid == 0) tc::bulk_wait0();
     }
 
-    if (g == P.G - 1 && ok) {
-        float v[32];
-        tc::tmem_ld32(tS + loff + hf * 32, v);
-        if (lane < 16 && p.S_out) {
-            float* dst = p.S_out + ((int64_t)bh * kD + srow) * kD + hf * 32;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) dst[j] = v[j];
-        }
-        if (p.z_out && tid < 64) p.z_out[(int64_t)bh * kD + tid] = kNorm ? zc[tid] : 0.f;
-    }
-    if (tid == 0) {
-        for (int s = 0; s < kStages; ++s)
-            if (pending[s]) wait_bar(&tma_bar[s], tma_phase[s], P.status);
-        tc::bulk_wait0();
-    }
     tc::tc_fence_before();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
+    if (warp == kWarpMma) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
 template <bool kFp16, bool kNorm>
@@ -391,7 +480,7 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     P.cps = (nC + P.G - 1) / P.G;
     const void* kern = reinterpret_cast<const void*>(&fwd_kernel<kFp16, kNorm>);
     void* args[] = {&P};
-    return launch_cluster(kern, P.G, p.B * p.H, FwdLayout::total + 1024, st, args);
+    return launch_cluster(kern, P.G, p.B * p.H, kFwdThreads, L::total + 1024, st, args);
 }
 
 }  // namespace

@@ -21,7 +21,7 @@ constexpr int kD = 64;                   // head_dim = value_dim on this path
 constexpr int kThreads = 256;            // 8 warps: row = 32 * (warp % 4) + lane, column half = warp / 4
 constexpr uint32_t kTile = kC * kD * 2;  // one 128 x 64 16-bit tile, 128-byte swizzle (16 KB)
 constexpr uint32_t kMTile = kC * 16 * 2; // one 128 x 16 16-bit tile, 32-byte swizzle (4 KB)
-constexpr uint32_t kSpinLimit = 1u << 25;
+constexpr uint32_t kSpinLimit = 1u << 22;
 
 template <bool kFp16>
 struct Elem;
@@ -156,7 +156,7 @@ struct Maps;
 bool make_map(CUtensorMap* m, const void* base, int dtype, int N, int H, int B, int64_t sn, int64_t sh, int64_t sb);
 int pick_segments(const ScanParams& p);
 int* status_ptr();  // device address of the status word (current device)
-cudaError_t launch_cluster(const void* kern, int G, int BH, size_t smem, cudaStream_t st, void** args);
+cudaError_t launch_cluster(const void* kern, int G, int BH, int threads, size_t smem, cudaStream_t st, void** args);
 
 }  // namespace tcs
 }  // namespace subq

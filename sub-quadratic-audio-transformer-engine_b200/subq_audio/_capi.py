@@ -29,7 +29,7 @@ SUBQ_PATH_AUTO, SUBQ_PATH_EXACT, SUBQ_PATH_TENSORCORE = 0, 1, 2
 EXPORTED = (
     "subq_fwd", "subq_bwd", "subq_fwd_workspace_bytes", "subq_bwd_workspace_bytes",
     "subq_feature_map", "subq_last_path", "subq_last_launches", "subq_last_error",
-    "subq_abi_version", "subq_device_info",
+    "subq_abi_version", "subq_device_info", "subq_device_status",
 )
 
 
@@ -112,6 +112,8 @@ def load() -> ctypes.CDLL:
             lib.subq_device_info.argtypes = [ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t,
                                              ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_int)]
             lib.subq_device_info.restype = ctypes.c_int
+            lib.subq_device_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
+            lib.subq_device_status.restype = ctypes.c_int
             _lib = lib
     return _lib
 
@@ -138,6 +140,13 @@ def fwd_workspace_bytes(args: FwdArgs) -> int:
 
 def bwd_workspace_bytes(args: BwdArgs) -> int:
     return int(load().subq_bwd_workspace_bytes(ctypes.byref(args)))
+
+
+def device_status(stream: int = 0) -> int:
+    """Synchronises `stream` and returns (and clears) the device status word."""
+    st = ctypes.c_int(0)
+    check(load().subq_device_status(ctypes.c_void_p(stream), ctypes.byref(st)))
+    return int(st.value)
 
 
 def last_path() -> int:
