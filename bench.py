@@ -66,7 +66,12 @@ def _ref_task(args):
     return time.perf_counter() - t0
 
 
-def cpu_reference(tasks_per_core=1, cores=None):
+# One head-sequence (N=8192) takes about 0.3 s through the reference engine on
+# one core; 32 per core keeps a sample near 10 s of wall time.
+CPU_TASKS_PER_CORE = 32
+
+
+def cpu_reference(tasks_per_core=CPU_TASKS_PER_CORE, cores=None):
     """Times the reference CPU path on a bounded sample; returns (tokens/s, info)."""
     import multiprocessing as mp
 
@@ -162,9 +167,9 @@ def main():
         vals = []
         info = {}
         for _ in range(max(1, args.warmup // 3)):
-            cpu_reference(tasks_per_core=1)
+            cpu_reference(tasks_per_core=CPU_TASKS_PER_CORE)
         for _ in range(args.steps if args.steps <= 3 else 3):
-            v, info = cpu_reference(tasks_per_core=1)
+            v, info = cpu_reference(tasks_per_core=CPU_TASKS_PER_CORE)
             if v is None:
                 print(json.dumps({"impl": "reference", "unavailable": info["unavailable"]}))
                 return 0
@@ -185,7 +190,7 @@ def main():
     # The CPU-baseline pool starts (spawn) before the first GPU call.
     cpu_val, cpu_info = (None, None)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_val, cpu_info = cpu_reference(tasks_per_core=1)
+        cpu_val, cpu_info = cpu_reference(tasks_per_core=CPU_TASKS_PER_CORE)
 
     if world > 1:
         torch.cuda.set_device(local_rank)
@@ -241,18 +246,20 @@ def main():
     value = tokens / (ms_max / 1e3)
 
     # ---- per-kernel launch timing (forward and backward separately) ----
+    # back-to-back launches of one kind, so that host-side argument set-up
+    # overlaps the previous launch and the events see device time only
     fe = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     reps = max(3, min(args.steps, 10))
-    fwd_ms = bwd_ms = 0.0
+    fe[0].record(stream)
     for _ in range(reps):
-        fe[0].record(stream)
         ops.scan_forward(qd, kd, vd, mask=md, normalize=True, path=args.path)
-        fe[1].record(stream)
+    fe[1].record(stream)
+    for _ in range(reps):
         ops.scan_backward(qd, kd, vd, dod, mask=md, normalize=True, path=args.path)
-        fe[2].record(stream)
-        torch.cuda.synchronize(dev)
-        fwd_ms += fe[0].elapsed_time(fe[1]) / reps
-        bwd_ms += fe[1].elapsed_time(fe[2]) / reps
+    fe[2].record(stream)
+    torch.cuda.synchronize(dev)
+    fwd_ms = fe[0].elapsed_time(fe[1]) / reps
+    bwd_ms = fe[1].elapsed_time(fe[2]) / reps
     path_used = ops.last_path()
 
     # ---- end-to-end through the public API with host buffers ----

@@ -84,7 +84,9 @@ def _desc(q: torch.Tensor, v: torch.Tensor, log_gamma: LogGamma, mask: Optional[
             raise ValueError(f"mask must be [B, N] = [{B}, {N}], got {tuple(m.shape)}")
         if m.device != q.device:
             raise ValueError("mask must be on the device of q")
-        if m.dtype != torch.uint8 or m.stride(1) != 1:
+        if m.dtype == torch.bool and m.stride(1) == 1:
+            m = m.view(torch.uint8)  # same bytes (0/1), no conversion launch
+        elif m.dtype != torch.uint8 or m.stride(1) != 1:
             m = (m != 0).to(torch.uint8).contiguous()
         keep.append(m)
         desc.mask = m.data_ptr()
