@@ -270,7 +270,12 @@ class SubQAttentionFunction(torch.autograd.Function):
         with torch.no_grad():
             out, _ = chunkwise_flash_linear_attention(q, k, v, decay_w, chunk_size=chunk_size,
                                                       attention_mask=attention_mask, is_causal=is_causal)
-        w_t = decay_w if isinstance(decay_w, torch.Tensor) else torch.tensor(decay_w, dtype=q.dtype, device=q.device)
+        if decay_w is None:  # gamma == 1; a placeholder keeps save_for_backward uniform
+            w_t = torch.zeros((), dtype=q.dtype, device=q.device)
+        elif isinstance(decay_w, torch.Tensor):
+            w_t = decay_w
+        else:
+            w_t = torch.tensor(decay_w, dtype=q.dtype, device=q.device)
         ctx.save_for_backward(q, k, v, w_t)
         ctx.is_3d = q.ndim == 3
         ctx.is_causal = is_causal
