@@ -8,9 +8,11 @@
 //   [O|Zi] = phi~(Q) [S_c | z_c]                 tcgen05 128x80x64  -> TMEM O'[b]
 //   O     += P V                                 tcgen05 128x64x128
 //   [S|z] += phi~(K)^T [V | 1]                   tcgen05 64x80x128, TMEM-resident fp32
-//   out_t  = O_t / max(r_t + Zi_t, clamp)  (normalised)  or  O_t
-// with phi~(q) = scale phi(q) and phi~(k) = m phi(k): masked keys drop out of
-// P, S and z (z = phi~(K)^T 1). The normaliser rides along as an extra 16
+//   out_t  = s O_t / max(s (r_t + Zi_t), clamp)  (normalised)  or  s O_t
+// with phi~(q) = phi(q), phi~(k) = m phi(k) and s = scale (applied in the fp32
+// epilogue, so the 16-bit operands carry no rounded scale): masked keys drop
+// out of P, S and z (z = phi~(K)^T 1). The feature map runs on packed 16-bit
+// pairs in shared memory. The normaliser rides along as an extra 16
 // output columns of the state MMAs; bf16 [S_c | z_c] in shared memory is the
 // next chunk's operand.
 //
@@ -163,24 +165,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     };
     auto transform = [&](int jlo, int jhi) {
         const int r = tid - 256;
+        auto chunk_of = [&](int j) { return c_begin + (j >= n1 ? j - n1 : j); };
+        float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
         for (int j = jlo; j < jhi && ok; ++j) {
             const bool ph2 = j >= n1;
-            const int chunk = c_begin + (ph2 ? j - n1 : j);
             const int s = j % kStages, u = j / kStages;
+            const float m = m_next;
+            if (j + 1 < jhi) m_next = row_mask_at(chunk_of(j + 1), r);  // in flight during the wait
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
             uint8_t* base = sm + s * L::stage;
-            const float m = row_mask_at(chunk, r);
-            if (ph2) {
-                chunks_transform<kFp16>(base + L::q, r, 0, 8, [&](int, float* v) {
-#pragma unroll
-                    for (int x = 0; x < 8; ++x) v[x] = phi_fast(v[x]) * p.scale;
-                });
-            }
-            chunks_transform<kFp16>(base + L::k, r, 0, 8, [&](int, float* v) {
-#pragma unroll
-                for (int x = 0; x < 8; ++x) v[x] = phi_fast(v[x]) * m;
-            });
+            if (ph2) chunks_phi<kFp16>(base + L::q, r, 0, 8, true);  // scale is applied in the epilogue
+            chunks_phi<kFp16>(base + L::k, r, 0, 8, m != 0.f);
             tc::fence_proxy_async();
             tc::bar_sync(kBarTransform, kTransformThreads);
             if (r == 0) tc::mbar_arrive(&bars[B_TDONE + s]);
@@ -423,11 +419,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             tc::bar_sync(kBarCompute, kComputeThreads);
             if (tid == 0) tc::mbar_arrive(&bars[B_ODONE + bf]);  // every thread has read O'[bf]
             {
+                // O' and the row sums carry phi(q) unscaled: o = s O' / max(s Z', clamp)
                 const float m = row_mask_at(c, row);
-                float inv = m;
+                float inv = m * p.scale;
                 if (kNorm) {
-                    const float z = rsm[(bf * 2) * 128 + row] + rsm[(bf * 2 + 1) * 128 + row] + zi;
-                    inv = m / fmaxf(z, p.clamp_min);
+                    const float z = p.scale * (rsm[(bf * 2) * 128 + row] + rsm[(bf * 2 + 1) * 128 + row] + zi);
+                    inv = inv / fmaxf(z, p.clamp_min);
                 }
 #pragma unroll
                 for (int x = 0; x < 32; ++x) o[x] *= inv;

@@ -40,8 +40,57 @@ struct Elem<true> {
     static __device__ __forceinline__ T2 from2(float a, float b) { return __floats2half2_rn(a, b); }
 };
 
-// phi(x) = ELU(x) + 1 with the fast exponential intrinsic on non-positive inputs.
-__device__ __forceinline__ float phi_fast(float x) { return x > 0.f ? x + 1.f : __expf(x); }
+// NaN-propagating min / max (fminf / fmaxf would return the other operand).
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float min_nan(float a, float b) {
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// phi(x) = ELU(x) + 1 = max(x, 0) + exp(min(x, 0)), with the fast exponential
+// intrinsic. The branch-free form (exp(0) = 1 exactly) keeps straight-line
+// code, so the element updates of a row interleave instead of serialising
+// behind one exponential each; NaN propagates as in ELU.
+__device__ __forceinline__ float phi_fast(float x) { return max_nan(x, 0.f) + __expf(min_nan(x, 0.f)); }
+
+// phi on a packed pair of 16-bit values, computed in the pair's own format:
+// max(x, 0) + 2^(min(x, 0) * log2(e)). The log2(e) factor is applied as two
+// parts representable in the format (bf16: 1.4375 + 0.0051880; fp16:
+// 1.4423828 + 0.00031233) fused into one rounding, so the exponent carries no
+// systematic constant error.
+template <bool kFp16>
+__device__ __forceinline__ uint32_t phi2(uint32_t x);
+template <>
+__device__ __forceinline__ uint32_t phi2<false>(uint32_t x) {
+    constexpr uint32_t kHi = 0x3FB83FB8u;  // 1.4375 (bf16 pair)
+    constexpr uint32_t kLo = 0x3BAA3BAAu;  // 0.0051880 (bf16 pair); kHi + kLo = log2(e) to 2^-16
+    uint32_t neg, pos, t, e, r;
+    asm("min.NaN.bf16x2 %0, %1, %2;" : "=r"(neg) : "r"(x), "r"(0u));
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(pos) : "r"(x), "r"(0u));
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t) : "r"(neg), "r"(kLo));
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(t) : "r"(neg), "r"(kHi), "r"(t));
+    asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(e) : "r"(t));
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(pos), "r"(e));
+    return r;
+}
+template <>
+__device__ __forceinline__ uint32_t phi2<true>(uint32_t x) {
+    constexpr uint32_t kHi = 0x3DC53DC5u;  // 1.4423828 (fp16 pair)
+    constexpr uint32_t kLo = 0x0D1E0D1Eu;  // 0.00031233 (fp16 pair); kHi + kLo = log2(e) to 1e-7
+    uint32_t neg, pos, t, e, r;
+    asm("min.NaN.f16x2 %0, %1, %2;" : "=r"(neg) : "r"(x), "r"(0u));
+    asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(pos) : "r"(x), "r"(0u));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(t) : "r"(neg), "r"(kLo));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(t) : "r"(neg), "r"(kHi), "r"(t));
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(t));
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(pos), "r"(e));
+    return r;
+}
 
 // Bounded mbarrier wait; on expiry records SUBQ_ERR_TIMEOUT in *status (the
 // library's device status word) and returns false.
@@ -53,16 +102,18 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* st
 }
 
 // f(j, v[8]) over the 16-byte chunks j in [j0, j0 + nj) of row r of a 128-byte
-// swizzled tile, in place.
+// swizzled tile, in place. All chunks are loaded before the first store, so
+// the loads and the nj * 8 element updates overlap instead of running as one
+// dependent chain per chunk.
 template <bool kFp16, typename F>
 __device__ __forceinline__ void chunks_transform(uint8_t* tile, int r, int j0, int nj, F&& f) {
     using E = Elem<kFp16>;
+    uint4 raw[8];
+#pragma unroll
+    for (int jj = 0; jj < nj; ++jj) raw[jj] = *reinterpret_cast<const uint4*>(tile + tc::sw128_chunk(r, j0 + jj));
 #pragma unroll
     for (int jj = 0; jj < nj; ++jj) {
-        const int j = j0 + jj;
-        uint4* ptr = reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, j));
-        uint4 raw = *ptr;
-        typename E::T2* h = reinterpret_cast<typename E::T2*>(&raw);
+        typename E::T2* h = reinterpret_cast<typename E::T2*>(&raw[jj]);
         float v[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -70,11 +121,35 @@ __device__ __forceinline__ void chunks_transform(uint8_t* tile, int r, int j0, i
             v[2 * i] = f2.x;
             v[2 * i + 1] = f2.y;
         }
-        f(j, v);
+        f(j0 + jj, v);
 #pragma unroll
         for (int i = 0; i < 4; ++i) h[i] = E::from2(v[2 * i], v[2 * i + 1]);
-        *ptr = raw;
     }
+#pragma unroll
+    for (int jj = 0; jj < nj; ++jj) *reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, j0 + jj)) = raw[jj];
+}
+
+// Row r of a 128-byte swizzled tile, chunks [j0, j0 + nj), in place:
+// phi of every element (live = true) or zeros (a masked token).
+template <bool kFp16>
+__device__ __forceinline__ void chunks_phi(uint8_t* tile, int r, int j0, int nj, bool live) {
+    uint4 raw[8];
+    if (live) {
+#pragma unroll
+        for (int jj = 0; jj < nj; ++jj) raw[jj] = *reinterpret_cast<const uint4*>(tile + tc::sw128_chunk(r, j0 + jj));
+#pragma unroll
+        for (int jj = 0; jj < nj; ++jj) {
+            raw[jj].x = phi2<kFp16>(raw[jj].x);
+            raw[jj].y = phi2<kFp16>(raw[jj].y);
+            raw[jj].z = phi2<kFp16>(raw[jj].z);
+            raw[jj].w = phi2<kFp16>(raw[jj].w);
+        }
+    } else {
+#pragma unroll
+        for (int jj = 0; jj < nj; ++jj) raw[jj] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int jj = 0; jj < nj; ++jj) *reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, j0 + jj)) = raw[jj];
 }
 
 template <bool kFp16>

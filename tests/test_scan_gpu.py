@@ -175,6 +175,39 @@ def test_tensorcore_backward_matches_oracle(case):
     assert rel_err(dv, rv) < 2e-2, "dv"
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensorcore_wide_inputs_match_oracle(dtype):
+    """Inputs ~ N(0, 9): the feature map's exponential runs deep into its
+    negative range, where the packed 16-bit evaluation is least accurate."""
+    B, H, N = 1, 2, 640
+    q, k, v, do, _, m, _ = make_case(B, H, N, 64, 64, dtype, seed=77, mask=True, scale_in=3.0)
+    qn, kn, vn, don, lgn, mn, _, _ = oracle_inputs(q, k, v, do, None, m, None, B, H, N)
+    ref_o = oracle.forward(qn, kn, vn, mask=mn, normalize=True, scale=0.125)[0]
+    rq, rk, rv, _ = oracle.backward(qn, kn, vn, don, mask=mn, normalize=True, scale=0.125)
+    o, _ = ops.scan_forward(to_dev(q), to_dev(k), to_dev(v), mask=to_dev(m), path="tensorcore")
+    dq, dk, dv, _ = ops.scan_backward(to_dev(q), to_dev(k), to_dev(v), to_dev(do), mask=to_dev(m),
+                                      path="tensorcore")
+    assert rel_err(o, ref_o) < 2e-2
+    assert rel_err(dq, rq) < 2e-2 and rel_err(dk, rk) < 2e-2 and rel_err(dv, rv) < 2e-2
+
+
+def test_tensorcore_nan_propagates_like_elu():
+    """ELU(NaN) + 1 = NaN: a NaN query spoils its own output row; a NaN key
+    spoils every later row (through the state), and no earlier one."""
+    q, k, v, _, _, _, _ = make_case(1, 1, 256, 64, 64, torch.bfloat16, seed=5)
+    q, k, v = q.cuda(), k.cuda(), v.cuda()
+    qn = q.clone()
+    qn[0, 0, 5, 3] = float("nan")
+    o = ops.scan_forward(qn, k, v, path="tensorcore")[0][0, 0]
+    rows = torch.isnan(o).any(dim=-1).cpu()
+    assert rows[5] and rows.sum() == 1
+    kn = k.clone()
+    kn[0, 0, 130, 0] = float("nan")
+    o = ops.scan_forward(q, kn, v, path="tensorcore")[0][0, 0]
+    assert not torch.isnan(o[:130]).any()
+    assert torch.isnan(o[130:]).all()
+
+
 def test_tensorcore_backward_single_token_is_degenerate():
     """One token: out = v exactly, so dq and dk vanish; only rounding noise remains."""
     q, k, v, do, _, _, _ = make_case(1, 2, 1, 64, 64, torch.bfloat16, seed=3)
