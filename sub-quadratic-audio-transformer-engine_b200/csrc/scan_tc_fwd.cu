@@ -3,24 +3,28 @@
 //
 // One cluster of G CTAs per (batch, head) sequence; CTA g owns segment g
 // (a run of 128-token chunks). Per chunk (t, tau index the chunk's tokens):
+//   [S|z]' = [S|z] + phi~(K)^T [V | 1]           tcgen05 64x80x128, TMEM-resident fp32
 //   P      = phi~(Q) phi~(K)^T                   tcgen05 128x128x64 -> TMEM P[b]
-//   P     <- P [tau <= t];  r_t = sum_tau P            (compute warps)
-//   [O|Zi] = phi~(Q) [S_c | z_c]                 tcgen05 128x80x64  -> TMEM O'[b]
-//   O     += P V                                 tcgen05 128x64x128
-//   [S|z] += phi~(K)^T [V | 1]                   tcgen05 64x80x128, TMEM-resident fp32
-//   out_t  = s O_t / max(s (r_t + Zi_t), clamp)  (normalised)  or  s O_t
+//   P     <- bf16(P [tau <= t])                  (compute warps, in TMEM)
+//   [O|Z]  = phi~(Q) [S_c | z_c]                 tcgen05 128x80x64  -> TMEM O'[b]
+//   [O|Z] += P [V | 1]                           tcgen05 128x80x128, A = P from TMEM
+//   out_t  = s O_t / max(s Z_t, clamp)  (normalised)  or  s O_t
 // with phi~(q) = phi(q), phi~(k) = m phi(k) and s = scale (applied in the fp32
 // epilogue, so the 16-bit operands carry no rounded scale): masked keys drop
-// out of P, S and z (z = phi~(K)^T 1). The feature map runs on packed 16-bit
-// pairs in shared memory. The normaliser rides along as an extra 16
-// output columns of the state MMAs; bf16 [S_c | z_c] in shared memory is the
-// next chunk's operand.
+// out of P, S and z (z = phi~(K)^T 1). The normaliser rides along as 16 extra
+// output columns (a ones column beside V), so Z_t = q~_t . z_c + the causal
+// row sum of P comes out of the tensor core. The feature map runs on packed
+// 16-bit pairs in shared memory.
+//
+// The state MMA of chunk c is issued first; while the chunk's other MMAs run,
+// the compute warps convert [S|z]_c+1 into a bf16 copy (double-buffered in
+// shared memory), which is the B operand of chunk c+1.
 //
 // Roles (448 threads): warps 0-7 compute (TMEM lane = 32 (warp % 4) + lane,
 // column half = warp / 4); warps 8-11 transform (feature map in shared
 // memory); warp 12 TMA producer; warp 13 MMA issuer. P and O' are
-// double-buffered in TMEM: while the tensor core runs chunk c's O and state
-// MMAs, the compute warps mask P of chunk c+1.
+// double-buffered in TMEM: while the tensor core runs chunk c's O MMAs, the
+// compute warps mask P of chunk c+1.
 //
 // Segment prefix: CTA g first sums phi~(K)^T [V | 1] over its own segment
 // (phase 1), publishes the sums in shared memory, and after a cluster barrier
@@ -48,14 +52,16 @@ struct L {
     static constexpr uint32_t stage = 3 * kTile;  // q, k, v
     static constexpr uint32_t q = 0, k = kTile, v = 2 * kTile;
     static constexpr uint32_t ones = kStages * stage;  // 128 x 64 atom, column 0 = 1 (the "| 1" of [V | 1])
-    static constexpr uint32_t sb = ones + kTile;       // bf16 [S_c | z_c]: two 64 x 64 atoms (MN-major B)
-    static constexpr uint32_t os = sb + 2 * kD * kD * 2;  // output staging
-    static constexpr uint32_t xs = os + kTile;         // segment-sum exchange: [64][64] + [64] fp32
-    static constexpr uint32_t rs = xs + kD * kD * 4 + 1024;  // partial row sums [2 buf][2 half][128]
-    static constexpr uint32_t bars = rs + 2048;
+    static constexpr uint32_t sbuf = 2 * kD * kD * 2;  // one bf16 [S_c | z_c]: two 64 x 64 atoms (MN-major B)
+    static constexpr uint32_t sb = ones + kTile;       // two of them: chunk c reads sb[c % 2]
+    static constexpr uint32_t os = sb + 2 * sbuf;      // output staging; before phase 2 the
+                                                       // segment-sum exchange [64][64] fp32
+    static constexpr uint32_t xz = os + kTile;         // segment-sum exchange [64] fp32
+    static constexpr uint32_t bars = xz + 256;
     static constexpr uint32_t tslot = bars + 8 * 24;
     static constexpr uint32_t total = tslot + 16;
 };
+static_assert(kD * kD * 4 <= kTile, "exchange fits the staging tile");
 static_assert(L::stage % 1024 == 0 && L::ones % 1024 == 0 && L::sb % 1024 == 0 && L::os % 1024 == 0,
               "alignment");
 static_assert(L::total + 1024 <= 232448, "shared memory");
@@ -105,9 +111,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::bars);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L::tslot);
-    float* rsm = reinterpret_cast<float*>(sm + L::rs);
-    float* Xs = reinterpret_cast<float*>(sm + L::xs);                // [64][64] segment sum phi~(K)^T V
-    float* Xz = reinterpret_cast<float*>(sm + L::xs + kD * kD * 4);  // [64] segment sum phi~(K)^T 1
+    float* Xs = reinterpret_cast<float*>(sm + L::os);  // [64][64] segment sum phi~(K)^T V
+    float* Xz = reinterpret_cast<float*>(sm + L::xz);  // [64] segment sum phi~(K)^T 1
     const uint32_t sbase = tc::smem_u32(sm);
 
     if (tid == 0) {
@@ -147,12 +152,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                         tc::sdesc_sw128(va + kk * 2048, lbo, 1024), n80, (first && kk == 0) ? 0u : 1u);
     };
 
+    // Chunk of pipeline slot j: phase-1 slots (j < n1) visit the segment in an
+    // order rotated per sequence, so that the clusters do not all read the
+    // same offset of their sequences at the same time (the segment sum does not
+    // depend on the order); phase-2 slots run in order.
+    const int rot = n1 > 0 ? (bh * 7) % n1 : 0;
+    auto chunk_of = [&](int j) {
+        if (j >= n1) return c_begin + (j - n1);
+        const int r = j + rot;
+        return c_begin + (r >= n1 ? r - n1 : r);
+    };
+
     bool ok = true;
 
     auto produce = [&](int jlo, int jhi) {
         for (int j = jlo; j < jhi && ok; ++j) {
             const bool ph2 = j >= n1;
-            const int chunk = c_begin + (ph2 ? j - n1 : j);
+            const int chunk = chunk_of(j);
             const int s = j % kStages, u = j / kStages;
             if (u >= 1) ok = wait_bar(&bars[B_EMPTY + s], (u - 1) & 1, P.status);
             if (!ok) break;
@@ -165,7 +181,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     };
     auto transform = [&](int jlo, int jhi) {
         const int r = tid - 256;
-        auto chunk_of = [&](int j) { return c_begin + (j >= n1 ? j - n1 : j); };
         float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
         for (int j = jlo; j < jhi && ok; ++j) {
             const bool ph2 = j >= n1;
@@ -271,7 +286,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             if (lane < 16) {
                 float zc8[8] = {z, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                 store_chunk<kFp16>(sm + L::sb + kD * kD * 2, srow, 0, zc8);
+                // columns 1-15 of the z atom are read as zeros (N = 80) in both buffers
                 zero_chunks(sm + L::sb + kD * kD * 2, srow, 1, 1);
+                zero_chunks(sm + L::sb + L::sbuf + kD * kD * 2, srow, 1, 1);
             }
             float w[32];
 #pragma unroll
@@ -308,24 +325,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             if (n > 0) ok = issue_p(0);
             for (int i = 0; i < n && ok; ++i) {
                 const int j = n1 + i, s = j % kStages, bf = i & 1, pu = i >> 1;
+                // [S|z]_c+1 first: the compute warps turn it into the next chunk's
+                // bf16 operand while this chunk's other MMAs run. It may start once
+                // the previous refresh has read S' (and written sb[i % 2]).
+                if (i >= 1) ok = wait_bar(&bars[B_SBDONE], (i - 1) & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                mma_state(s, false);
+                tc::mma_commit(&bars[B_SFULL]);
                 if (i + 1 < n) ok = issue_p(i + 1);
                 if (ok) ok = wait_bar(&bars[B_PSDONE + bf], pu & 1, P.status);
                 if (ok && i >= 2) ok = wait_bar(&bars[B_ODONE + bf], (pu - 1) & 1, P.status);
-                if (ok && i >= 1) ok = wait_bar(&bars[B_SBDONE], (i - 1) & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
                 const uint32_t qa = sbase + s * L::stage + L::q, va = sbase + s * L::stage + L::v;
                 const uint32_t tOb = tmem + cO + bf * kNX;
+                const uint32_t sba = sbase + L::sb + (i & 1) * L::sbuf;
                 for (int kk = 0; kk < 4; ++kk)  // [O | Zi] = phi~(Q) [S_c | z_c]
                     tc::mma_f16(tOb, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(sbase + L::sb + kk * 2048, kD * kD * 2, 1024),
-                                kNorm ? idOX : idO, kk > 0);
-                for (int kk = 0; kk < 8; ++kk)  // O += P V, bf16 P read from TMEM (8 columns per 16 tokens)
-                    tc::mma_f16_ts(tOb, tmem + cP + bf * 128 + kk * 8, tc::sdesc_sw128(va + kk * 2048, kTile, 1024),
-                                   idO, 1u);
+                                tc::sdesc_sw128(sba + kk * 2048, kD * kD * 2, 1024), kNorm ? idOX : idO, kk > 0);
+                // [O | Zi] += P [V | 1]: bf16 P read from TMEM (8 columns per 16 tokens);
+                // the ones column adds the causal row sums to the normaliser
+                const uint32_t lbo = kNorm ? L::ones - (s * L::stage + L::v) : kTile;
+                for (int kk = 0; kk < 8; ++kk)
+                    tc::mma_f16_ts(tOb, tmem + cP + bf * 128 + kk * 8, tc::sdesc_sw128(va + kk * 2048, lbo, 1024),
+                                   kNorm ? idOX : idO, 1u);
                 tc::mma_commit(&bars[B_OFULL + bf]);
-                mma_state(s, false);  // [S|z]_c+1
-                tc::mma_commit(&bars[B_SFULL]);
                 tc::mma_commit(&bars[B_EMPTY + s]);
             }
         }
@@ -334,9 +359,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         const int quad = warp & 3, hf = warp >> 2;
         const int row = quad * 32 + lane, srow = quad * 16 + lane;
         const uint32_t loff = (uint32_t)(quad * 32) << 16;
-        // P of chunk i: causal mask on the diagonal block, row sums, and the bf16
-        // copy packed back into the first 64 TMEM columns of P[b] (the A operand
-        // of O += P V).
+        // P of chunk i: causal mask on the diagonal block and the bf16 copy packed
+        // back into the first 64 TMEM columns of P[b] (the A operand of O += P V).
         auto mask_p = [&](int i) -> bool {
             const int bf = i & 1;
             if (!tc::bar_and(kBarCompute, kComputeThreads, wait_bar(&bars[B_PFULL + bf], (i >> 1) & 1, P.status)))
@@ -344,7 +368,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             tc::tc_fence_after();
             using E = Elem<kFp16>;
             uint32_t packed[32];
-            float rs = 0.f;
             if (hf == 1 && quad < 2) {
 #pragma unroll
                 for (int x = 0; x < 32; ++x) packed[x] = 0u;
@@ -354,17 +377,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 tc::tmem_ld32(tmem + cP + bf * 128 + loff + hf * 64, v);
                 tc::tmem_ld32(tmem + cP + bf * 128 + loff + hf * 64 + 32, v + 32);
 #pragma unroll
-                for (int x = 0; x < 64; ++x) {
+                for (int x = 0; x < 64; ++x)
                     if (diag && (hf * 64 + x) > row) v[x] = 0.f;
-                    rs += v[x];
-                }
 #pragma unroll
                 for (int x = 0; x < 32; ++x) {
                     typename E::T2 h2 = E::from2(v[2 * x], v[2 * x + 1]);
                     packed[x] = *reinterpret_cast<uint32_t*>(&h2);
                 }
             }
-            if (kNorm) rsm[(bf * 2 + hf) * 128 + row] = rs;
             tc::tc_fence_before();
             tc::bar_sync(kBarCompute, kComputeThreads);  // every fp32 read of P[b] is done
             tc::tc_fence_after();
@@ -377,28 +397,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         if (n > 0) ok = mask_p(0);
         for (int i = 0; i < n && ok; ++i) {
             const int c = c_begin + i, bf = i & 1, pu = i >> 1;
-            if (i + 1 < n) {
-                ok = mask_p(i + 1);
-                if (!ok) break;
-            }
-            // state refresh: bf16 [S | z]_c+1 for the next chunk's operand
+            // state refresh: bf16 [S | z]_c+1 into sb[(i + 1) % 2], the next chunk's operand
             ok = tc::bar_and(kBarCompute, kComputeThreads,
                              wait_bar(&bars[B_SFULL], sfull_count & 1, P.status)) && ok;
             ++sfull_count;
             if (!ok) break;
             tc::tc_fence_after();
             {
+                uint8_t* sbn = sm + L::sb + ((i + 1) & 1) * L::sbuf;
                 float v[32];
                 tc::tmem_ld32(tmem + cS + loff + hf * 32, v);
                 if (lane < 16) {
 #pragma unroll
-                    for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + L::sb, srow, hf * 4 + x, v + 8 * x);
+                    for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sbn, srow, hf * 4 + x, v + 8 * x);
                 }
                 if (kNorm && hf == 0) {
                     const float zv = tmem_ld1(tmem + cS + loff + 64);
                     if (lane < 16) {
                         float zc8[8] = {zv, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                        store_chunk<kFp16>(sm + L::sb + kD * kD * 2, srow, 0, zc8);
+                        store_chunk<kFp16>(sbn + kD * kD * 2, srow, 0, zc8);
                     }
                 }
             }
@@ -406,6 +423,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             tc::tc_fence_before();
             tc::bar_sync(kBarCompute, kComputeThreads);
             if (tid == 0) tc::mbar_arrive(&bars[B_SBDONE]);
+            if (i + 1 < n) {
+                ok = mask_p(i + 1);
+                if (!ok) break;
+            }
             // output of chunk i
             ok = tc::bar_and(kBarCompute, kComputeThreads, wait_bar(&bars[B_OFULL + bf], pu & 1, P.status)) && ok;
             if (!ok) break;
@@ -419,13 +440,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             tc::bar_sync(kBarCompute, kComputeThreads);
             if (tid == 0) tc::mbar_arrive(&bars[B_ODONE + bf]);  // every thread has read O'[bf]
             {
-                // O' and the row sums carry phi(q) unscaled: o = s O' / max(s Z', clamp)
+                // O' and its normaliser column carry phi(q) unscaled: o = s O' / max(s Z', clamp)
                 const float m = row_mask_at(c, row);
                 float inv = m * p.scale;
-                if (kNorm) {
-                    const float z = p.scale * (rsm[(bf * 2) * 128 + row] + rsm[(bf * 2 + 1) * 128 + row] + zi);
-                    inv = inv / fmaxf(z, p.clamp_min);
-                }
+                if (kNorm) inv = inv / fmaxf(p.scale * zi, p.clamp_min);
 #pragma unroll
                 for (int x = 0; x < 32; ++x) o[x] *= inv;
 #pragma unroll
