@@ -1,25 +1,36 @@
-// Tensor-core backward scan (d = e = 64, bf16/fp16 inputs, fp32 accumulation).
+// Tensor-core backward scan (d = e = 64, bf16/fp16 inputs, fp32 accumulation),
+// warp-specialised and pipelined across chunks.
 //
 // One cluster of G CTAs per (batch, head) sequence; CTA g owns segment g.
-// With q~ = scale phi(q), k~ = m phi(k), Zc_t = max(Z_t, clamp) and the
-// quotient rule of the normaliser,
-//   o^_t = m_t dO_t / Zc_t,      c_t = -(m_t dO_t . num_t) / Zc_t^2
-// the gradients per 128-token chunk are
-//   dA   = (O^ V^T + c m^T) [tau <= t]
-//   dQ~  = dA K~ + O^ S_c^T + c z_c^T                (S_c, z_c: prefix state)
-//   dK~  = dA^T Q~ + V dS_c^T + m dz_c^T             (dS_c, dz_c: suffix adjoint)
-//   dV   = (P [tau <= t])^T O^ + K~ dS_c
-//   dS_c-1 = dS_c + Q~^T O^,   dz_c-1 = dz_c + Q~^T c
-// and dq = dQ~ scale phi'(q), dk = dK~ phi'(k) m, dv = dV m with
-// phi'(x) = min(phi(x), 1). The normaliser terms z and dz run on the tensor
-// core against a two-column tile [m | c].
+// With q^ = phi(q), k^ = m phi(k) (raw features; s = scale is applied in the
+// fp32 epilogues), the forward's num_t = s (q^_t S_c + sum_{tau<=t} P_t,tau v_tau)
+// and Z_t = s (q^_t z_c + sum_{tau<=t} P_t,tau) with P = q^ k^T, the quotient
+// rule of the normaliser gives, per 128-token chunk,
+//   o^_t = m_t dO_t / Zc_t,      c_t = -(m_t dO_t . num_t) / Zc_t^2,   Zc = max(Z, clamp)
+//   dA   = ([o^ | c] [V | 1]^T) [tau <= t]
+//   dQ~  = dA K^ + [o^ | c] [S_c | z_c]^T                    dq = s dQ~ phi'(q)
+//   dK~  = s (dA^T q^ + [V | 1] [dS^ | dz^]^T)              dk = dK~ phi'(k) m
+//   dV   = s ((P [tau <= t])^T o^ + K^ dS^)                 dv = dV m
+// with S_c, z_c the prefix state of the chunk and dS^, dz^ = sum over later
+// tokens of q^^T [o^ | c] (the raw suffix adjoint). phi'(x) = min(phi(x), 1).
+// Every normaliser term rides on the tensor core as 16 extra columns: a ones
+// atom beside V, a c atom beside o^, a z atom beside S.
 //
-// Phases of a CTA:
-//   A  segment sums of K~^T V and K~^T m (CTAs g < G-1)   -> DSMEM -> S_c, z_c
-//   B  chunks ascending: recompute num and Z, form O^ and c, emit dq, keep
-//      (Zc_t, c_t) in the workspace, sum Q~^T O^ and Q~^T c over the segment
-//                                                          -> DSMEM -> dS, dz
-//   C  chunks descending: rebuild O^ from dO and (Zc, c), emit dk and dv.
+// Phases of a CTA (chunk order within the segment):
+//   A  segment sums of K^^T [V | 1] (CTAs g < G-1)              -> DSMEM -> S_c, z_c
+//   B  ascending: recompute [num | Z], form o^ and c, emit dq, keep (Zc_t, c_t)
+//      in the workspace, sum q^^T [o^ | c] over the segment     -> DSMEM -> suffix
+//   C  descending: rebuild o^ from dO and (Zc, c); P^T = K^ q^^T and
+//      dA^T = [V | 1] [o^ | c]^T directly in the key-major orientation, so that
+//      dK and dV are tensor-core products with A read from TMEM; emit dk, dv.
+//
+// Roles (448 threads): warps 0-7 compute (TMEM lane = 32 (warp % 4) + lane,
+// column half = warp / 4), warps 8-11 feature map (packed 16-bit, in shared
+// memory), warp 12 TMA producer, warp 13 MMA issuer. The prefix state S_c
+// (phase B) and the suffix adjoint dS^ (phase C) accumulate in TMEM; their bf16
+// copies, the B operands of the next chunk, are double-buffered in shared
+// memory and refreshed while the chunk's other MMAs run. P and dA are masked
+// and packed to bf16 in place in TMEM and consumed from there (A operand).
 //
 // Reference: python/subq_audio/autograd.py:441-544 (quotient rule :497-499,
 // chunked adjoint :172-289); src/kernels/attention_backward.cpp:165-229.
@@ -32,33 +43,53 @@ namespace tcs {
 namespace {
 
 constexpr int kStages = 2;
+constexpr int kBwdThreads = 448;
+constexpr int kComputeThreads = 256, kTransformThreads = 128;
+constexpr int kBarCompute = 1, kBarTransform = 2;
+constexpr int kWarpProducer = 12, kWarpMma = 13;
+constexpr int kNX = 80;  // 64 value columns + 16 normaliser columns
 
-struct BwdLayout {
+struct BL {
     static constexpr uint32_t stage = 4 * kTile;  // q, k, v, dO
     static constexpr uint32_t q = 0, k = kTile, v = 2 * kTile, g = 3 * kTile;
-    static constexpr uint32_t p = kStages * stage;     // P (2 blocks); exchange buffer between phases
-    static constexpr uint32_t da = p + 2 * kTile;      // dA (2 blocks)
-    static constexpr uint32_t ob = da + 2 * kTile;     // O^ [t][e]
-    static constexpr uint32_t sb = ob + kTile;         // bf16 S_c (phase B) or dS_c (phase C)
-    static constexpr uint32_t mc = sb + kD * kD * 2;   // [m | c] column tile (128 x 16)
-    static constexpr uint32_t zc = mc + kMTile;        // z_c or dz_c, fp32 [2][64] (double buffer)
-    static constexpr uint32_t zq = zc + 512;           // partial q~.z [2][128]
-    static constexpr uint32_t rs = zq + 1024;          // partial row sums / dot products [2][128]
-    static constexpr uint32_t mb = rs + 1024;          // m_t [128]
-    static constexpr uint32_t bars = mb + 512;
-    static constexpr uint32_t tslot = bars + 8 * (kStages + 1);
+    static constexpr uint32_t ones = kStages * stage;  // 128 x 64 atom, column 0 = 1
+    static constexpr uint32_t ob = ones + kTile;       // o^ [t][e]; between phases the fp32 exchange
+    static constexpr uint32_t ca = ob + kTile;         // c atom: column 0 = c_t
+    static constexpr uint32_t sbuf = 2 * kD * kD * 2;  // bf16 [S | z] (or [dS | dz]): S atom + z atom
+    static constexpr uint32_t sb = ca + kTile;         // two of them
+    static constexpr uint32_t os = sb + 2 * sbuf;      // output staging (dq, dk)
+    static constexpr uint32_t xz = os + kTile;         // [64] fp32 exchange of z / dz
+    static constexpr uint32_t dx = xz + 256;           // [2][128] fp32 partial dot products
+    static constexpr uint32_t bars = dx + 1024;
+    static constexpr uint32_t tslot = bars + 8 * 32;
     static constexpr uint32_t total = tslot + 16;
 };
-static_assert(BwdLayout::p % 1024 == 0 && BwdLayout::da % 1024 == 0 && BwdLayout::ob % 1024 == 0 &&
-                  BwdLayout::sb % 1024 == 0 && BwdLayout::mc % 1024 == 0,
+static_assert(kD * kD * 4 <= kTile, "exchange fits the o^ tile");
+static_assert(BL::ones % 1024 == 0 && BL::ob % 1024 == 0 && BL::ca % 1024 == 0 && BL::sb % 1024 == 0 &&
+                  BL::os % 1024 == 0,
               "alignment");
-static_assert(BwdLayout::total + 1024 <= 232448, "shared memory");
+static_assert(BL::total + 1024 <= 232448, "shared memory");
 
-// TMEM (512 fp32 columns): P [0,128) -- reused for dQ~ / dV [0,64) once P is
-// consumed --, dA [128,256), X1 [256,320) (num / dK~), z' [320,352), dz' [352,384),
-// S [384,448), dS [448,512). z', dz', S, dS use the M = 64 layout.
+enum {
+    B_FULL = 0,                 // [kStages] TMA -> feature map
+    B_TDONE = B_FULL + kStages, // [kStages] feature map -> MMA
+    B_EMPTY = B_TDONE + kStages,// [kStages] consumers -> producer
+    B_AFULL = B_EMPTY + kStages,// phase A sums done
+    // phase B
+    B_SFULL, B_SBDONE, B_PFULL, B_PSDONE, B_NZFULL, B_OCDONE, B_DAFULL, B_DADONE, B_DQFULL, B_DQDONE,
+    // phase C
+    B_COCDONE, B_CPFULL, B_CPDONE, B_DSFULL, B_DSBDONE, B_KVFULL, B_KVDONE,
+    B_COUNT
+};
+static_assert(B_COUNT <= 32, "barrier slots");
+
+// TMEM (512 fp32 columns).
+//   phase B: P [0,128) | dA [128,256) | [N|Z], later dQ [256,336) | S [336,416) | dS^ sum [416,496)
+//   phase C: P^T [0,128) | dA^T [128,256) | dK [256,320) | dV [320,384) | dS^ [416,496)
+// S and dS^ use the M = 64 layout (column 64 = z / dz).
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t cP = 0, cdA = 128, cX1 = 256, cZ = 320, cdZ = 352, cS = 384, cdS = 448;
+constexpr uint32_t cP = 0, cDA = 128, cNZ = 256, cS = 336, cDS = 416;
+constexpr uint32_t cPT = 0, cDAT = 128, cDK = 256, cDV = 320;
 
 struct BwdParams {
     CUtensorMap tm_q, tm_k, tm_v, tm_g, tm_dq, tm_dk, tm_dv;
@@ -69,7 +100,7 @@ struct BwdParams {
 };
 
 template <bool kFp16, bool kNorm>
-__global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant__ BwdParams P) {
+__global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams P) {
     const ScanParams& p = P.p;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -79,536 +110,591 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     const int bh = blockIdx.y;
     const int b = bh / p.H, h = bh - b * p.H;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quad = warp & 3, hf = warp >> 2;
-    const int row = quad * 32 + lane;
-    const int srow = quad * 16 + lane;
     const int nC = (p.N + kC - 1) / kC;
     const int c_begin = min(nC, g * P.cps);
-    const int c_end = min(nC, c_begin + P.cps);
-    const int n = c_end - c_begin;
+    const int n = min(nC, c_begin + P.cps) - c_begin;
+    const int nA = (g < P.G - 1) ? n : 0;  // phase-A chunks
+    // pipeline slots: [0, nA) phase A, [nA, nA + n) phase B, [nA + n, nA + 2n) phase C
+    const int nslots = nA + 2 * n;
 
-    uint64_t* tma_bar = reinterpret_cast<uint64_t*>(sm + BwdLayout::bars);
-    uint64_t* mma_bar = tma_bar + kStages;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + BwdLayout::tslot);
-    float* zc = reinterpret_cast<float*>(sm + BwdLayout::zc);  // [2][64]
-    float* zqs = reinterpret_cast<float*>(sm + BwdLayout::zq);
-    float* rss = reinterpret_cast<float*>(sm + BwdLayout::rs);
-    float* mb = reinterpret_cast<float*>(sm + BwdLayout::mb);
-    uint8_t* Pt = sm + BwdLayout::p;
-    uint8_t* dAt = sm + BwdLayout::da;
-    uint8_t* Ot = sm + BwdLayout::ob;
-    uint8_t* Sb = sm + BwdLayout::sb;
-    uint8_t* MC = sm + BwdLayout::mc;
-    float* Xs = reinterpret_cast<float*>(Pt);
-    float* Xz = reinterpret_cast<float*>(Pt + kD * kD * 4);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BL::bars);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + BL::tslot);
+    float* Xs = reinterpret_cast<float*>(sm + BL::ob);  // [64][64] exchange (o^ tile between phases)
+    float* Xz = reinterpret_cast<float*>(sm + BL::xz);  // [64]
+    float* dxs = reinterpret_cast<float*>(sm + BL::dx);
+    const uint32_t sbase = tc::smem_u32(sm);
     float2* wsz = reinterpret_cast<float2*>(p.ws) + (int64_t)bh * p.N;
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) tc::mbar_init(&tma_bar[s], 1);
-        tc::mbar_init(mma_bar, 1);
+        for (int i = 0; i < B_COUNT; ++i) tc::mbar_init(&bars[i], 1);
         tc::fence_mbar_init();
     }
-    if (warp == 0) tc::tmem_alloc(tslot, kTmemCols);
+    if (warp == kWarpMma) tc::tmem_alloc(tslot, kTmemCols);
+    if (warp >= 8 && warp < 12) {
+        // constant ones atom; zero the columns 1-15 that the 16-wide normaliser
+        // K-steps / N-atoms read in the c atom and both z atoms
+        const int r = tid - 256;
+        float one[8] = {1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        store_chunk<kFp16>(sm + BL::ones, r, 0, one);
+        zero_chunks(sm + BL::ones, r, 1, 1);
+        zero_chunks(sm + BL::ca, r, 0, 2);
+        if (r < kD) {
+            zero_chunks(sm + BL::sb + kD * kD * 2, r, 0, 2);
+            zero_chunks(sm + BL::sb + BL::sbuf + kD * kD * 2, r, 0, 2);
+        }
+        tc::fence_proxy_async();
+    }
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tslot;
-    const uint32_t loff = (uint32_t)(quad * 32) << 16;
-    const uint32_t tP = tmem + cP, tdA = tmem + cdA, tX1 = tmem + cX1, tX2 = tmem + cP;
-    const uint32_t tZ = tmem + cZ, tdZ = tmem + cdZ, tS = tmem + cS, tdS = tmem + cdS;
-    const uint32_t sbase = tc::smem_u32(sm);
 
-    bool ok = true;
-    uint32_t tma_phase[kStages] = {0, 0};
-    int pending[kStages] = {0, 0};
-    uint32_t mma_phase = 0;
+    // instruction descriptors
+    constexpr uint32_t idPP = tc::idesc_f16<kFp16>(128, 128, false, false);  // K-major x K-major, N = 128
+    constexpr uint32_t idNZ = tc::idesc_f16<kFp16>(128, kNorm ? kNX : 64, false, true);
+    constexpr uint32_t idKK64 = tc::idesc_f16<kFp16>(128, 64, false, false);
+    constexpr uint32_t idKM64 = tc::idesc_f16<kFp16>(128, 64, false, true);
+    constexpr uint32_t idST = tc::idesc_f16<kFp16>(64, kNorm ? kNX : 64, true, true);  // X^T [Y | 1]
 
-    constexpr uint32_t idKK128 = tc::idesc_f16<kFp16>(128, 128, false, false);
-    constexpr uint32_t idKM = tc::idesc_f16<kFp16>(128, 64, false, true);
-    constexpr uint32_t idKK = tc::idesc_f16<kFp16>(128, 64, false, false);
-    constexpr uint32_t idMM = tc::idesc_f16<kFp16>(128, 64, true, true);
-    constexpr uint32_t idS = tc::idesc_f16<kFp16>(64, 64, true, true);
-    constexpr uint32_t idZ = tc::idesc_f16<kFp16>(64, 16, true, true);
-
-    auto stp = [&](int s, uint32_t w) { return sm + s * BwdLayout::stage + w; };
-    auto sta = [&](int s, uint32_t w) { return sbase + s * BwdLayout::stage + w; };
-    auto issue = [&](int chunk, int s, bool full) {
-        const int t0 = chunk * kC;
-        pending[s] = 1;
-        tc::mbar_arrive_expect_tx(&tma_bar[s], (full ? 4u : 2u) * kTile);
-        if (full) {
-            tc::tma_load_4d(stp(s, BwdLayout::q), &P.tm_q, 0, t0, h, b, &tma_bar[s]);
-            tc::tma_load_4d(stp(s, BwdLayout::g), &P.tm_g, 0, t0, h, b, &tma_bar[s]);
-        }
-        tc::tma_load_4d(stp(s, BwdLayout::k), &P.tm_k, 0, t0, h, b, &tma_bar[s]);
-        tc::tma_load_4d(stp(s, BwdLayout::v), &P.tm_v, 0, t0, h, b, &tma_bar[s]);
-    };
-    auto row_mask = [&](int chunk) -> float {
-        const int t = chunk * kC + row;
+    auto row_mask_at = [&](int chunk, int r) -> float {
+        const int t = chunk * kC + r;
         if (t >= p.N) return 0.f;
         return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
     };
-    auto wait_tma = [&](int s) {
-        ok = __syncthreads_and(wait_bar(&tma_bar[s], tma_phase[s], P.status)) && ok;
-        tma_phase[s] ^= 1u;
-        pending[s] = 0;
+    // chunk of pipeline slot j (phase A visits its segment rotated per sequence)
+    const int rot = nA > 0 ? (bh * 7) % nA : 0;
+    auto chunk_of = [&](int j) {
+        if (j < nA) {
+            const int r = j + rot;
+            return c_begin + (r >= nA ? r - nA : r);
+        }
+        if (j < nA + n) return c_begin + (j - nA);
+        return c_begin + n - 1 - (j - nA - n);
     };
-    auto wait_mma = [&]() {
-        ok = __syncthreads_and(wait_bar(mma_bar, mma_phase, P.status)) && ok;
-        mma_phase ^= 1u;
+    auto slot_addr = [&](int j, uint32_t w) { return sbase + (j % kStages) * BL::stage + w; };
+    auto slot_ptr = [&](int j, uint32_t w) { return sm + (j % kStages) * BL::stage + w; };
+    // acc (+)= X^T [Y | extra] over 128 tokens, X and Y [128][64] tiles read MN-major (M = 64)
+    auto mma_xt = [&](uint32_t dst, uint32_t xa, uint32_t ya, uint32_t extra, bool first) {
+        const uint32_t lbo = kNorm ? extra - ya : kTile;
+        for (int kk = 0; kk < 8; ++kk)
+            tc::mma_f16(dst, tc::sdesc_sw128(xa + kk * 2048, kTile, 1024), tc::sdesc_sw128(ya + kk * 2048, lbo, 1024),
+                        idST, (first && kk == 0) ? 0u : 1u);
+    };
+
+    bool ok = true;
+
+    // ---------------------------------------------------------------- roles
+    auto produce = [&](int jlo, int jhi) {
+        for (int j = jlo; j < jhi && ok; ++j) {
+            const int s = j % kStages, u = j / kStages;
+            if (u >= 1) ok = wait_bar(&bars[B_EMPTY + s], (u - 1) & 1, P.status);
+            if (!ok) break;
+            const bool full = j >= nA;
+            const int chunk = chunk_of(j);
+            uint8_t* base = sm + s * BL::stage;
+            tc::mbar_arrive_expect_tx(&bars[B_FULL + s], (full ? 4u : 2u) * kTile);
+            if (full) {
+                tc::tma_load_4d(base + BL::q, &P.tm_q, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+                tc::tma_load_4d(base + BL::g, &P.tm_g, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+            }
+            tc::tma_load_4d(base + BL::k, &P.tm_k, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + BL::v, &P.tm_v, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+        }
+    };
+    auto transform = [&](int jlo, int jhi) {
+        const int r = tid - 256;
+        float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
+        for (int j = jlo; j < jhi && ok; ++j) {
+            const int s = j % kStages, u = j / kStages;
+            const float m = m_next;
+            if (j + 1 < jhi) m_next = row_mask_at(chunk_of(j + 1), r);
+            ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
+            if (!ok) break;
+            uint8_t* base = sm + s * BL::stage;
+            if (j >= nA) chunks_phi<kFp16>(base + BL::q, r, 0, 8, true);
+            chunks_phi<kFp16>(base + BL::k, r, 0, 8, m != 0.f);
+            tc::fence_proxy_async();
+            tc::bar_sync(kBarTransform, kTransformThreads);
+            if (r == 0) tc::mbar_arrive(&bars[B_TDONE + s]);
+        }
+    };
+
+    // compute-warp geometry
+    const int quad = warp & 3, hf = (warp >> 2) & 1;
+    const int row = quad * 32 + lane, srow = quad * 16 + lane;
+    const uint32_t loff = (uint32_t)(quad * 32) << 16;
+    using E = Elem<kFp16>;
+
+    // 128 x 128 fp32 tile in TMEM -> causal-masked bf16 packed into its first 64
+    // columns (this thread's half of its row), after every thread's fp32 reads.
+    // keep_upper: keep col >= row (key-major tiles), else col <= row (query-major).
+    auto mask_to_bf16 = [&](uint32_t tcol, bool keep_upper) {
+        uint32_t packed[32];
+        const bool zero = keep_upper ? (hf == 0 && quad >= 2) : (hf == 1 && quad < 2);
+        if (zero) {
+#pragma unroll
+            for (int x = 0; x < 32; ++x) packed[x] = 0u;
+        } else {
+            const bool diag = (hf == (quad >> 1));
+            float v[64];
+            tc::tmem_ld32(tmem + tcol + loff + hf * 64, v);
+            tc::tmem_ld32(tmem + tcol + loff + hf * 64 + 32, v + 32);
+            if (diag) {
+#pragma unroll
+                for (int x = 0; x < 64; ++x) {
+                    const int col = hf * 64 + x;
+                    if (keep_upper ? (col < row) : (col > row)) v[x] = 0.f;
+                }
+            }
+#pragma unroll
+            for (int x = 0; x < 32; ++x) {
+                typename E::T2 h2 = E::from2(v[2 * x], v[2 * x + 1]);
+                packed[x] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+        }
+        tc::tc_fence_before();
+        tc::bar_sync(kBarCompute, kComputeThreads);
         tc::tc_fence_after();
+        tc::tmem_st32_raw(tmem + tcol + loff + hf * 32, packed);
     };
-    auto publish = [&]() {
+    // M = 64 accumulator [X | x] (TMEM, 80 columns) -> bf16 S atom + z atom of `dst`
+    auto refresh = [&](uint32_t tcol, uint8_t* dst) {
+        float v[32];
+        tc::tmem_ld32(tmem + tcol + loff + hf * 32, v);
+        if (lane < 16) {
+#pragma unroll
+            for (int x = 0; x < 4; ++x) store_chunk<kFp16>(dst, srow, hf * 4 + x, v + 8 * x);
+        }
+        if (kNorm && hf == 0) {
+            const float zv = tmem_ld1(tmem + tcol + loff + 64);
+            if (lane < 16) {
+                float z8[8] = {zv, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                store_chunk<kFp16>(dst + kD * kD * 2, srow, 0, z8);
+            }
+        }
+    };
+    // end of a compute step: shared-memory writes visible to the tensor core,
+    // TMEM accesses ordered, then one arrive on `bar`
+    auto publish = [&](uint64_t* bar) {
         tc::fence_proxy_async();
         tc::tc_fence_before();
-        __syncthreads();
+        tc::bar_sync(kBarCompute, kComputeThreads);
+        if (tid == 0) tc::mbar_arrive(bar);
     };
-    // acc (+)= X^T Y over 128 tokens (X, Y [128][64] tiles read MN-major; M = 64).
-    auto mma_xty = [&](uint32_t dst, uint32_t xa, uint32_t ya, bool first) {
-        for (int kk = 0; kk < 8; ++kk)
-            tc::mma_f16(dst, tc::sdesc_sw128(xa + kk * 2048, kTile, 1024), tc::sdesc_sw128(ya + kk * 2048, kTile, 1024),
-                        idS, (first && kk == 0) ? 0u : 1u);
+    auto cwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        ok = tc::bar_and(kBarCompute, kComputeThreads, wait_bar(bar, parity, P.status)) && ok;
+        if (ok) tc::tc_fence_after();
+        return ok;
     };
-    // acc (+)= X^T [m | c] (the two-column tile; M = 64, N = 16).
-    auto mma_xtm = [&](uint32_t dst, uint32_t xa, bool first) {
-        for (int kk = 0; kk < 8; ++kk)
-            tc::mma_f16(dst, tc::sdesc_sw128(xa + kk * 2048, kTile, 1024), sdesc_sw32(sbase + BwdLayout::mc + kk * 512),
-                        idZ, (first && kk == 0) ? 0u : 1u);
-    };
-    auto transform_q = [&](uint8_t* qt, const float* z, float* zq_out) {
-        float zq = 0.f;
-        chunks_transform<kFp16>(qt, row, hf * 4, 4, [&](int j, float* v) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                v[u] = phi_fast(v[u]) * p.scale;
-                if (kNorm && z) zq = fmaf(v[u], z[8 * j + u], zq);
-            }
-        });
-        if (zq_out) *zq_out = zq;
-    };
-    auto transform_k = [&](uint8_t* kt, float m) {
-        chunks_transform<kFp16>(kt, row, hf * 4, 4, [&](int, float* v) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = phi_fast(v[u]) * m;
-        });
-    };
-    // 128 x 128 causal tile (TMEM fp32) -> bf16 shared memory, this thread's column
-    // half; optionally adds c_t m_tau; returns the partial row sum.
-    auto tile_out = [&](uint32_t tsrc, uint8_t* dst, bool add_cm, float ct) -> float {
-        uint8_t* pb = dst + hf * kTile;
-        float rs = 0.f;
-        if (hf == 1 && quad < 2) {
-            zero_chunks(pb, row, 0, 8);
-            return 0.f;
-        }
-        const bool diag = (hf == (quad >> 1));
-#pragma unroll
-        for (int half32 = 0; half32 < 2; ++half32) {
-            float v[32];
-            tc::tmem_ld32(tsrc + loff + hf * 64 + half32 * 32, v);
-#pragma unroll
-            for (int u = 0; u < 32; ++u) {
-                const int tau = hf * 64 + half32 * 32 + u;
-                float x = add_cm ? fmaf(ct, mb[tau], v[u]) : v[u];
-                if (diag && tau > row) x = 0.f;
-                rs += x;
-                v[u] = x;
-            }
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) store_chunk<kFp16>(pb, row, half32 * 4 + q4, v + 8 * q4);
-        }
-        return rs;
-    };
-    // M = 64 state (TMEM) -> bf16 copy in Sb (this thread's column half).
-    auto refresh_sb = [&](uint32_t tsrc) {
+    // exchange helpers (compute warps): own M = 64 accumulator -> Xs / Xz
+    auto publish_sums = [&](uint32_t tcol, bool have) {
         float v[32];
-        tc::tmem_ld32(tsrc + loff + hf * 32, v);
-        if (lane < 16) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(Sb, srow, hf * 4 + j, v + 8 * j);
-        }
-    };
-    // Column `col` of an M = 64, N = 32 accumulator -> dst[64] (warps of half 0).
-    auto read_col = [&](uint32_t tsrc, int col, float* dst) {
-        if (hf == 0) {
-            const float x = tmem_ld1(tsrc + loff + col);
-            if (lane < 16) dst[srow] = x;
-        }
-    };
-    // 64 x 64 fp32 state rows (this thread's half) -> TMEM and Sb.
-    auto put_state = [&](uint32_t tdst, float* v) {
-        if (lane < 16) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(Sb, srow, hf * 4 + j, v + 8 * j);
-        }
-        tc::tmem_st32(tdst + loff + hf * 32, v);
-    };
-    // Column `col` of an M = 64, N = 32 accumulator <- src[64], other columns zero.
-    auto put_col = [&](uint32_t tdst, int col, const float* src) {
-        if (hf == 0) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
-            if (lane < 16) v[col] = src[srow];
-            tc::tmem_st32(tdst + loff, v);
-        }
-    };
-
-    // ------------------------------------------------------------ phase A
-    if (g < P.G - 1) {
-        if (tid == 0 && n > 0) issue(c_begin, 0, false);
-        for (int i = 0; i < n && ok; ++i) {
-            const int s = i % kStages;
-            if (tid == 0 && i + 1 < n) issue(c_begin + i + 1, (i + 1) % kStages, false);
-            wait_tma(s);
-            if (!ok) break;
-            const float m = row_mask(c_begin + i);
-            transform_k(stp(s, BwdLayout::k), m);
-            if (kNorm && hf == 0) mtile_row2<kFp16>(MC, row, m, 0.f);
-            publish();
-            if (tid == 0) {
-                tc::tc_fence_after();
-                mma_xty(tS, sta(s, BwdLayout::k), sta(s, BwdLayout::v), i == 0);
-                if (kNorm) mma_xtm(tZ, sta(s, BwdLayout::k), i == 0);
-                tc::mma_commit(mma_bar);
-            }
-            wait_mma();
-        }
-        float v[32];
-        if (n > 0 && ok) {
-            tc::tmem_ld32(tS + loff + hf * 32, v);
+        if (have) {
+            tc::tmem_ld32(tmem + tcol + loff + hf * 32, v);
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            for (int x = 0; x < 32; ++x) v[x] = 0.f;
         }
         if (lane < 16) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) Xs[srow * 64 + hf * 32 + j] = v[j];
+            for (int x = 0; x < 32; ++x) Xs[srow * 64 + hf * 32 + x] = v[x];
         }
         if (hf == 0) {
-            const float zv = (kNorm && n > 0 && ok) ? tmem_ld1(tZ + loff) : 0.f;
+            const float zv = (kNorm && have) ? tmem_ld1(tmem + tcol + loff + 64) : 0.f;
             if (lane < 16) Xz[srow] = zv;
         }
-    }
-    tc::tc_fence_before();
-    cluster.sync();
-    tc::tc_fence_after();
-    {
-        float v[32];
+    };
+    // sum of the exchanged values of CTAs [r0, r1) (+ an optional fp32 base)
+    // -> registers v (this thread's 32 columns of row srow) and z
+    auto gather_sums = [&](int r0, int r1, const float* base_S, const float* base_z, float* v, float& z) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        for (int x = 0; x < 32; ++x) v[x] = 0.f;
+        z = 0.f;
         if (lane < 16) {
-            if (p.S_in) {
-                const float* src = p.S_in + ((int64_t)bh * kD + srow) * kD + hf * 32;
+            if (base_S) {
+                const float* src = base_S + ((int64_t)bh * kD + srow) * kD + hf * 32;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = src[j];
+                for (int x = 0; x < 32; ++x) v[x] = src[x];
             }
-            for (int r = 0; r < g; ++r) {
+            for (int r = r0; r < r1; ++r) {
                 const float* rx = cluster.map_shared_rank(Xs, r) + srow * 64 + hf * 32;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] += rx[j];
+                for (int x = 0; x < 32; ++x) v[x] += rx[x];
+            }
+            if (kNorm && hf == 0) {
+                z = base_z ? base_z[(int64_t)bh * kD + srow] : 0.f;
+                for (int r = r0; r < r1; ++r) z += cluster.map_shared_rank(Xz, r)[srow];
             }
         }
-        put_state(tS, v);
-        if (kNorm && tid < 64) {
-            float z = p.z_in ? p.z_in[(int64_t)bh * kD + tid] : 0.f;
-            for (int r = 0; r < g; ++r) z += cluster.map_shared_rank(Xz, r)[tid];
-            zc[tid] = z;
+    };
+    // registers -> TMEM accumulator (M = 64 layout) and bf16 copy in `dst`
+    auto install_state = [&](uint32_t tcol, uint8_t* dst, const float* v, float z) {
+        if (lane < 16) {
+#pragma unroll
+            for (int x = 0; x < 4; ++x) store_chunk<kFp16>(dst, srow, hf * 4 + x, v + 8 * x);
+        }
+        tc::tmem_st32(tmem + tcol + loff + hf * 32, v);
+        if (hf == 0) {
+            if (kNorm && lane < 16) {
+                float z8[8] = {z, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                store_chunk<kFp16>(dst + kD * kD * 2, srow, 0, z8);
+            }
+            float w[32];
+#pragma unroll
+            for (int x = 0; x < 32; ++x) w[x] = 0.f;
+            w[0] = (lane < 16) ? z : 0.f;
+            tc::tmem_st32(tmem + tcol + loff + 64, w);
+        }
+    };
+
+    // ============================================================ phase A
+    if (warp == kWarpProducer) {
+        if (lane == 0) {
+            for (int m = 0; m < 7; ++m)
+                tc::prefetch_tmap(m == 0 ? &P.tm_q : m == 1 ? &P.tm_k : m == 2 ? &P.tm_v : m == 3 ? &P.tm_g
+                                  : m == 4 ? &P.tm_dq : m == 5 ? &P.tm_dk : &P.tm_dv);
+            produce(0, min(nslots, nA + kStages));
+        }
+        __syncwarp();
+    } else if (warp >= 8 && warp < 12) {
+        transform(0, nA);
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            for (int j = 0; j < nA && ok; ++j) {
+                const int s = j % kStages, u = j / kStages;
+                ok = wait_bar(&bars[B_TDONE + s], u & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                mma_xt(tmem + cS, slot_addr(j, BL::k), slot_addr(j, BL::v), sbase + BL::ones, j == 0);
+                tc::mma_commit(&bars[B_EMPTY + s]);
+            }
+            if (nA > 0 && ok) tc::mma_commit(&bars[B_AFULL]);
+        }
+        __syncwarp();
+    } else if (warp < 8) {
+        if (g < P.G - 1) {
+            if (nA > 0) cwait(&bars[B_AFULL], 0);
+            publish_sums(cS, nA > 0 && ok);
         }
     }
-    __syncthreads();
-    if (kNorm) put_col(tZ, 0, zc);
-    tc::fence_proxy_async();
     tc::tc_fence_before();
     cluster.sync();
     tc::tc_fence_after();
+    float carry[32], carry_z = 0.f;  // prefix (phase B) / suffix (phase C) state rows, compute warps
+    if (warp < 8) gather_sums(0, g, p.S_in, p.z_in, carry, carry_z);
+    tc::tc_fence_before();
+    cluster.sync();  // remote reads done before the exchange tile is reused
+    tc::tc_fence_after();
+    if (warp < 8) {
+        install_state(cS, sm + BL::sb, carry, carry_z);
+        tc::fence_proxy_async();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
 
-    // ------------------------------------------------------------ phase B
-    if (tid == 0 && n > 0) issue(c_begin, 0, true);
-    for (int i = 0; i < n && ok; ++i) {
-        const int c = c_begin + i, s = i % kStages;
-        float* zcur = zc + (i & 1) * 64;        // z_c
-        float* znext = zc + ((i + 1) & 1) * 64;  // z_c+1
-        if (tid == 0 && i + 1 < n) {
-            tc::bulk_wait_read0();
-            issue(c + 1, (i + 1) % kStages, true);
-        }
-        wait_tma(s);
-        if (!ok) break;
-        uint8_t* qt = stp(s, BwdLayout::q);
-        uint8_t* kt = stp(s, BwdLayout::k);
-        const uint32_t qa = sta(s, BwdLayout::q), ka = sta(s, BwdLayout::k), va = sta(s, BwdLayout::v);
-        const float m = row_mask(c);
-        float zq = 0.f;
-        transform_q(qt, zcur, &zq);
-        transform_k(kt, m);
-        if (kNorm) zqs[hf * 128 + row] = zq;
-        if (hf == 0) mb[row] = m;
-        publish();
-        if (tid == 0) {
-            tc::tc_fence_after();
-            for (int kk = 0; kk < 4; ++kk)  // P = Q~ K~^T
-                tc::mma_f16(tP, tc::sdesc_sw128(qa + kk * 32, 16, 1024), tc::sdesc_sw128(ka + kk * 32, 16, 1024),
-                            idKK128, kk > 0);
-            for (int kk = 0; kk < 4; ++kk)  // num = Q~ S_c
-                tc::mma_f16(tX1, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
-                            tc::sdesc_sw128(sbase + BwdLayout::sb + kk * 2048, 8192, 1024), idKM, kk > 0);
-            tc::mma_commit(mma_bar);
-        }
-        wait_mma();
-        if (!ok) break;
-        {
-            const float rs = tile_out(tP, Pt, false, 0.f);
-            if (kNorm) rss[hf * 128 + row] = rs;
-        }
-        publish();
-        if (tid == 0) {
-            tc::tc_fence_after();
-            for (int kk = 0; kk < 8; ++kk) {  // num += P V
-                const uint32_t pa = sbase + BwdLayout::p + (kk >> 2) * kTile + (kk & 3) * 32;
-                tc::mma_f16(tX1, tc::sdesc_sw128(pa, 16, 1024), tc::sdesc_sw128(va + kk * 2048, kTile, 1024), idKM, 1u);
+    // ============================================================ phase B
+    if (warp == kWarpProducer) {
+        if (lane == 0) produce(min(nslots, nA + kStages), min(nslots, nA + n + kStages));
+        __syncwarp();
+    } else if (warp >= 8 && warp < 12) {
+        transform(nA, nA + n);
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            auto issue_p = [&](int i) -> bool {  // P = q^ k^^T
+                const int j = nA + i;
+                if (!wait_bar(&bars[B_TDONE + j % kStages], (j / kStages) & 1, P.status)) return false;
+                tc::tc_fence_after();
+                const uint32_t qa = slot_addr(j, BL::q), ka = slot_addr(j, BL::k);
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16(tmem + cP, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(ka + kk * 32, 16, 1024), idPP, kk > 0);
+                tc::mma_commit(&bars[B_PFULL]);
+                return true;
+            };
+            if (n > 0) ok = issue_p(0);
+            for (int i = 0; i < n && ok; ++i) {
+                const int j = nA + i;
+                const uint32_t qa = slot_addr(j, BL::q), ka = slot_addr(j, BL::k), va = slot_addr(j, BL::v);
+                const uint32_t sba = sbase + BL::sb + (i & 1) * BL::sbuf;
+                const uint32_t lbo_v1 = kNorm ? (sbase + BL::ones) - va : kTile;
+                // [S|z]_c+1 = [S|z]_c + k^^T [V | 1]
+                if (i >= 1) ok = wait_bar(&bars[B_SBDONE], (i - 1) & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                mma_xt(tmem + cS, ka, va, sbase + BL::ones, false);
+                tc::mma_commit(&bars[B_SFULL]);
+                // [N | Z] = q^ [S_c | z_c] + bf16(P) [V | 1]   (into the NZ / dQ columns)
+                ok = wait_bar(&bars[B_PSDONE], i & 1, P.status);
+                if (ok && i >= 1) ok = wait_bar(&bars[B_DQDONE], (i - 1) & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(sba + kk * 2048, kD * kD * 2, 1024), idNZ, kk > 0);
+                for (int kk = 0; kk < 8; ++kk)
+                    tc::mma_f16_ts(tmem + cNZ, tmem + cP + kk * 8, tc::sdesc_sw128(va + kk * 2048, lbo_v1, 1024),
+                                   idNZ, 1u);
+                tc::mma_commit(&bars[B_NZFULL]);
+                if (i + 1 < n) ok = issue_p(i + 1);
+                if (!ok) break;
+                // dA = [o^ | c] [V | 1]^T ; dS^ sum += q^^T [o^ | c]
+                ok = wait_bar(&bars[B_OCDONE], i & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16(tmem + cDA, tc::sdesc_sw128(sbase + BL::ob + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(va + kk * 32, 16, 1024), idPP, kk > 0);
+                if (kNorm)
+                    tc::mma_f16(tmem + cDA, tc::sdesc_sw128(sbase + BL::ca, 16, 1024),
+                                tc::sdesc_sw128(sbase + BL::ones, 16, 1024), idPP, 1u);
+                tc::mma_commit(&bars[B_DAFULL]);
+                mma_xt(tmem + cDS, qa, sbase + BL::ob, sbase + BL::ca, i == 0);
+                // dQ~ = bf16(dA) K^ + [o^ | c] [S_c | z_c]^T   (into the NZ / dQ columns)
+                ok = wait_bar(&bars[B_DADONE], i & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                for (int kk = 0; kk < 8; ++kk)
+                    tc::mma_f16_ts(tmem + cNZ, tmem + cDA + kk * 8, tc::sdesc_sw128(ka + kk * 2048, kTile, 1024),
+                                   idKM64, kk > 0);
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ob + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(sba + kk * 32, 16, 1024), idKK64, 1u);
+                if (kNorm)
+                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ca, 16, 1024),
+                                tc::sdesc_sw128(sba + kD * kD * 2, 16, 1024), idKK64, 1u);
+                tc::mma_commit(&bars[B_DQFULL]);
             }
-            tc::mma_commit(mma_bar);
         }
-        wait_mma();
-        if (!ok) break;
-        // O^ and c from the recomputed numerator and denominator.
-        float num[32], go[32];
-        tc::tmem_ld32(tX1 + loff + hf * 32, num);
-        load_chunks<kFp16>(stp(s, BwdLayout::g), row, hf * 4, 4, go);
-        float zcl = 1.f;
-        if (kNorm) zcl = fmaxf(rss[row] + rss[128 + row] + zqs[row] + zqs[128 + row], p.clamp_min);
-        float dot = 0.f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) dot = fmaf(go[j], num[j], dot);
-        __syncthreads();  // everyone has read rss / zqs
-        if (kNorm) rss[hf * 128 + row] = dot * m;
-        __syncthreads();
-        const float ct = kNorm ? -(rss[row] + rss[128 + row]) / (zcl * zcl) : 0.f;
-        {
-            const float inv = m / zcl;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) go[j] *= inv;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(Ot, row, hf * 4 + j, go + 8 * j);
-        }
-        if (hf == 0) {
-            if (kNorm) mtile_row2<kFp16>(MC, row, m, ct);
-            if (c * kC + row < p.N) wsz[c * kC + row] = make_float2(zcl, ct);
-        }
-        publish();
-        if (tid == 0) {
-            tc::tc_fence_after();
-            for (int kk = 0; kk < 4; ++kk)  // dA = O^ V^T
-                tc::mma_f16(tdA, tc::sdesc_sw128(sbase + BwdLayout::ob + kk * 32, 16, 1024),
-                            tc::sdesc_sw128(va + kk * 32, 16, 1024), idKK128, kk > 0);
-            mma_xty(tdS, qa, sbase + BwdLayout::ob, i == 0);  // segment sum of Q~^T O^
-            mma_xty(tS, ka, va, false);                        // S_c+1
-            if (kNorm) {
-                mma_xtm(tdZ, qa, i == 0);  // column 1: segment sum of Q~^T c
-                mma_xtm(tZ, ka, false);    // column 0: z_c+1
+        __syncwarp();
+    } else if (warp < 8) {
+        if (n > 0) {
+            cwait(&bars[B_PFULL], 0);
+            if (ok) {
+                mask_to_bf16(cP, false);
+                publish(&bars[B_PSDONE]);
             }
-            tc::mma_commit(mma_bar);
         }
-        wait_mma();
-        if (!ok) break;
-        tile_out(tdA, dAt, kNorm, ct);
-        publish();
-        if (tid == 0) {
-            tc::tc_fence_after();
-            for (int kk = 0; kk < 8; ++kk) {  // dQ~ = dA K~
-                const uint32_t aa = sbase + BwdLayout::da + (kk >> 2) * kTile + (kk & 3) * 32;
-                tc::mma_f16(tX2, tc::sdesc_sw128(aa, 16, 1024), tc::sdesc_sw128(ka + kk * 2048, kTile, 1024), idKM,
-                            kk > 0);
-            }
-            for (int kk = 0; kk < 4; ++kk)  // dQ~ += O^ S_c^T
-                tc::mma_f16(tX2, tc::sdesc_sw128(sbase + BwdLayout::ob + kk * 32, 16, 1024),
-                            tc::sdesc_sw128(sbase + BwdLayout::sb + kk * 32, 16, 1024), idKK, 1u);
-            tc::mma_commit(mma_bar);
-        }
-        wait_mma();
-        if (!ok) break;
-        {
-            float dq[32], qv[32];
-            tc::tmem_ld32(tX2 + loff + hf * 32, dq);
-            load_chunks<kFp16>(qt, row, hf * 4, 4, qv);
-            const float inv_scale = 1.f / p.scale;
+        for (int i = 0; i < n && ok; ++i) {
+            const int j = nA + i, c = c_begin + i;
+            // (1) state refresh: bf16 [S | z]_c+1 into sb[(i + 1) % 2]
+            if (!cwait(&bars[B_SFULL], i & 1)) break;
+            refresh(cS, sm + BL::sb + ((i + 1) & 1) * BL::sbuf);
+            publish(&bars[B_SBDONE]);
+            // (2) o^ and c from [num | Z] and dO (the slot's q^ and dO are complete
+            // once its feature map is: TDONE implies FULL)
+            if (!cwait(&bars[B_NZFULL], i & 1)) break;
+            if (!cwait(&bars[B_TDONE + j % kStages], (j / kStages) & 1)) break;
+            const float m = row_mask_at(c, row);
+            float num[32], go[32];
+            tc::tmem_ld32(tmem + cNZ + loff + hf * 32, num);
+            const float zraw = kNorm ? tmem_ld1(tmem + cNZ + loff + 64) : 0.f;
+            load_chunks<kFp16>(slot_ptr(j, BL::g), row, hf * 4, 4, go);
+            float dot = 0.f;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float x = kNorm ? fmaf(ct, zcur[hf * 32 + j], dq[j]) : dq[j];
-                dq[j] = x * p.scale * fminf(qv[j] * inv_scale, 1.f) * m;
-            }
+            for (int x = 0; x < 32; ++x) dot = fmaf(go[x], num[x], dot);
+            dxs[hf * 128 + row] = dot;
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            const float zc = kNorm ? max_nan(p.scale * zraw, p.clamp_min) : 1.f;
+            const float inv = m / zc;
+            const float ct = kNorm ? -m * p.scale * (dxs[row] + dxs[128 + row]) * inv / zc : 0.f;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(qt, row, hf * 4 + j, dq + 8 * j);
-        }
-        refresh_sb(tS);
-        if (kNorm) read_col(tZ, 0, znext);
-        publish();
-        if (tid == 0) {
-            tc::tma_store_4d(&P.tm_dq, qt, 0, c * kC, h, b);
-            tc::bulk_commit();
+            for (int x = 0; x < 32; ++x) go[x] *= inv;
+#pragma unroll
+            for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + BL::ob, row, hf * 4 + x, go + 8 * x);
+            if (hf == 0) {
+                if (kNorm) {
+                    float c8[8] = {ct, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                    store_chunk<kFp16>(sm + BL::ca, row, 0, c8);
+                }
+                if (c * kC + row < p.N) wsz[c * kC + row] = make_float2(zc, ct);
+            }
+            publish(&bars[B_OCDONE]);  // also: every thread has read dxs and [N | Z]
+            // (3) P of the next chunk
+            if (i + 1 < n) {
+                if (!cwait(&bars[B_PFULL], (i + 1) & 1)) break;
+                mask_to_bf16(cP, false);
+                publish(&bars[B_PSDONE]);
+            }
+            // (4) dA: causal mask, bf16 in place
+            if (!cwait(&bars[B_DAFULL], i & 1)) break;
+            mask_to_bf16(cDA, false);
+            publish(&bars[B_DADONE]);
+            // (5) dq = s dQ~ phi'(q)
+            if (!cwait(&bars[B_DQFULL], i & 1)) break;
+            {
+                float dq[32], qv[32];
+                tc::tmem_ld32(tmem + cNZ + loff + hf * 32, dq);
+                load_chunks<kFp16>(slot_ptr(j, BL::q), row, hf * 4, 4, qv);
+#pragma unroll
+                for (int x = 0; x < 32; ++x) dq[x] *= p.scale * min_nan(qv[x], 1.f);
+                if (tid == 0) tc::bulk_wait_read0();  // the staging tile is free again
+                tc::tc_fence_before();
+                tc::bar_sync(kBarCompute, kComputeThreads);
+                if (tid == 0) {
+                    tc::mbar_arrive(&bars[B_DQDONE]);           // dQ~ columns read
+                    tc::mbar_arrive(&bars[B_EMPTY + j % kStages]);  // q^, dO of this slot read; MMAs done
+                }
+#pragma unroll
+                for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + BL::os, row, hf * 4 + x, dq + 8 * x);
+                tc::fence_proxy_async();
+                tc::bar_sync(kBarCompute, kComputeThreads);
+                if (tid == 0) {
+                    tc::tma_store_4d(&P.tm_dq, sm + BL::os, 0, c * kC, h, b);
+                    tc::bulk_commit();
+                }
+            }
         }
     }
 
-    // --------------------------------------------- suffix exchange (dS, dz)
-    {
-        float v[32];
-        if (n > 0 && ok) {
-            tc::tmem_ld32(tdS + loff + hf * 32, v);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
-        }
-        float dzv = 0.f;
-        if (hf == 0) {
-            const float x = (kNorm && n > 0 && ok) ? tmem_ld1(tdZ + loff + 1) : 0.f;
-            dzv = x;
-        }
-        if (tid == 0) tc::bulk_wait_read0();
-        tc::tc_fence_before();
-        __syncthreads();
-        if (lane < 16) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) Xs[srow * 64 + hf * 32 + j] = v[j];
-            if (hf == 0) Xz[srow] = dzv;
-        }
-    }
+    // ------------------------------------------------ suffix exchange (dS^, dz^)
+    if (warp < 8) publish_sums(cDS, n > 0 && ok);
+    tc::tc_fence_before();
     cluster.sync();
     tc::tc_fence_after();
-    {
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
-        if (lane < 16) {
-            for (int r = g + 1; r < P.G; ++r) {
-                const float* rx = cluster.map_shared_rank(Xs, r) + srow * 64 + hf * 32;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] += rx[j];
-            }
-        }
-        float dz = 0.f;
-        if (kNorm && tid < 64)
-            for (int r = g + 1; r < P.G; ++r) dz += cluster.map_shared_rank(Xz, r)[tid];
-        tc::tc_fence_before();
-        cluster.sync();  // remote reads done before the buffers are reused
-        tc::tc_fence_after();
-        put_state(tdS, v);
-        if (tid < 64) zc[tid] = dz;
+    if (warp < 8) gather_sums(g + 1, P.G, nullptr, nullptr, carry, carry_z);
+    tc::tc_fence_before();
+    cluster.sync();
+    tc::tc_fence_after();
+    if (warp < 8) {
+        install_state(cDS, sm + BL::sb, carry, carry_z);
+        tc::fence_proxy_async();
     }
-    __syncthreads();
-    if (kNorm) put_col(tdZ, 1, zc);
-    tc::fence_proxy_async();
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
 
-    // ------------------------------------------------------------ phase C
-    if (tid == 0 && n > 0) issue(c_end - 1, 0, true);
-    for (int i = 0; i < n && ok; ++i) {
-        const int c = c_end - 1 - i, s = i % kStages;
-        float* dzcur = zc + (i & 1) * 64;         // dz_c
-        float* dznext = zc + ((i + 1) & 1) * 64;  // dz_c-1
-        if (tid == 0 && i + 1 < n) {
-            tc::bulk_wait_read0();
-            issue(c - 1, (i + 1) % kStages, true);
-        }
-        wait_tma(s);
-        if (!ok) break;
-        uint8_t* qt = stp(s, BwdLayout::q);
-        uint8_t* kt = stp(s, BwdLayout::k);
-        uint8_t* vt = stp(s, BwdLayout::v);
-        const uint32_t qa = sta(s, BwdLayout::q), ka = sta(s, BwdLayout::k), va = sta(s, BwdLayout::v);
-        const float m = row_mask(c);
-        float2 zcc = make_float2(1.f, 0.f);
-        if (c * kC + row < p.N) zcc = wsz[c * kC + row];
-        const float ct = zcc.y;
-        transform_q(qt, nullptr, nullptr);
-        transform_k(kt, m);
-        {
-            float go[32];
-            load_chunks<kFp16>(stp(s, BwdLayout::g), row, hf * 4, 4, go);
-            const float inv = m / zcc.x;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) go[j] *= inv;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(Ot, row, hf * 4 + j, go + 8 * j);
-        }
-        if (hf == 0) {
-            mb[row] = m;
-            if (kNorm) mtile_row2<kFp16>(MC, row, m, ct);
-        }
-        publish();
-        if (tid == 0) {
-            tc::tc_fence_after();
-            for (int kk = 0; kk < 4; ++kk) {
-                tc::mma_f16(tP, tc::sdesc_sw128(qa + kk * 32, 16, 1024), tc::sdesc_sw128(ka + kk * 32, 16, 1024),
-                            idKK128, kk > 0);
-                tc::mma_f16(tdA, tc::sdesc_sw128(sbase + BwdLayout::ob + kk * 32, 16, 1024),
-                            tc::sdesc_sw128(va + kk * 32, 16, 1024), idKK128, kk > 0);
+    // ============================================================ phase C
+    if (warp == kWarpProducer) {
+        if (lane == 0) produce(min(nslots, nA + n + kStages), nslots);
+        __syncwarp();
+    } else if (warp >= 8 && warp < 12) {
+        transform(nA + n, nslots);
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            for (int i = 0; i < n && ok; ++i) {
+                const int j = nA + n + i;
+                const uint32_t qa = slot_addr(j, BL::q), ka = slot_addr(j, BL::k), va = slot_addr(j, BL::v);
+                const uint32_t dsa = sbase + BL::sb + (i & 1) * BL::sbuf;  // dS^ of the later chunks
+                ok = wait_bar(&bars[B_TDONE + j % kStages], (j / kStages) & 1, P.status);
+                if (ok) ok = wait_bar(&bars[B_COCDONE], i & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                // P^T = K^ q^^T ; dA^T = [V | 1] [o^ | c]^T   (key-major rows)
+                for (int kk = 0; kk < 4; ++kk) {
+                    tc::mma_f16(tmem + cPT, tc::sdesc_sw128(ka + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(qa + kk * 32, 16, 1024), idPP, kk > 0);
+                    tc::mma_f16(tmem + cDAT, tc::sdesc_sw128(va + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(sbase + BL::ob + kk * 32, 16, 1024), idPP, kk > 0);
+                }
+                if (kNorm)
+                    tc::mma_f16(tmem + cDAT, tc::sdesc_sw128(sbase + BL::ones, 16, 1024),
+                                tc::sdesc_sw128(sbase + BL::ca, 16, 1024), idPP, 1u);
+                tc::mma_commit(&bars[B_CPFULL]);
+                // dS^ += q^^T [o^ | c]   (after the previous refresh has read it)
+                if (i >= 1) ok = wait_bar(&bars[B_DSBDONE], (i - 1) & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                mma_xt(tmem + cDS, qa, sbase + BL::ob, sbase + BL::ca, false);
+                tc::mma_commit(&bars[B_DSFULL]);
+                // dK~ = bf16(dA^T) q^ + [V | 1] [dS^ | dz^]^T ;  dV = bf16(P^T) o^ + K^ dS^
+                ok = wait_bar(&bars[B_CPDONE], i & 1, P.status);
+                if (ok && i >= 1) ok = wait_bar(&bars[B_KVDONE], (i - 1) & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                for (int kk = 0; kk < 8; ++kk) {
+                    tc::mma_f16_ts(tmem + cDK, tmem + cDAT + kk * 8, tc::sdesc_sw128(qa + kk * 2048, kTile, 1024),
+                                   idKM64, kk > 0);
+                    tc::mma_f16_ts(tmem + cDV, tmem + cPT + kk * 8,
+                                   tc::sdesc_sw128(sbase + BL::ob + kk * 2048, kTile, 1024), idKM64, kk > 0);
+                }
+                for (int kk = 0; kk < 4; ++kk) {
+                    tc::mma_f16(tmem + cDK, tc::sdesc_sw128(va + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(dsa + kk * 32, 16, 1024), idKK64, 1u);
+                    tc::mma_f16(tmem + cDV, tc::sdesc_sw128(ka + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(dsa + kk * 2048, kTile, 1024), idKM64, 1u);
+                }
+                if (kNorm)
+                    tc::mma_f16(tmem + cDK, tc::sdesc_sw128(sbase + BL::ones, 16, 1024),
+                                tc::sdesc_sw128(dsa + kD * kD * 2, 16, 1024), idKK64, 1u);
+                tc::mma_commit(&bars[B_KVFULL]);
             }
-            tc::mma_commit(mma_bar);
         }
-        wait_mma();
-        if (!ok) break;
-        tile_out(tP, Pt, false, 0.f);
-        tile_out(tdA, dAt, kNorm, ct);
-        publish();
-        if (tid == 0) {
-            tc::tc_fence_after();
-            for (int kk = 0; kk < 8; ++kk) {
-                // dK~ = dA^T Q~ ; dV = P^T O^   (A read MN-major across both 64-token blocks)
-                tc::mma_f16(tX1, tc::sdesc_sw128(sbase + BwdLayout::da + kk * 2048, kTile, 1024),
-                            tc::sdesc_sw128(qa + kk * 2048, kTile, 1024), idMM, kk > 0);
-                tc::mma_f16(tX2, tc::sdesc_sw128(sbase + BwdLayout::p + kk * 2048, kTile, 1024),
-                            tc::sdesc_sw128(sbase + BwdLayout::ob + kk * 2048, kTile, 1024), idMM, kk > 0);
+        __syncwarp();
+    } else if (warp < 8) {
+        for (int i = 0; i < n && ok; ++i) {
+            const int j = nA + n + i, c = c_begin + n - 1 - i;
+            // (1) o^ = m dO / Zc and the c atom, from the workspace
+            {
+                const float m = row_mask_at(c, row);
+                float2 zcc = make_float2(1.f, 0.f);
+                if (c * kC + row < p.N) zcc = wsz[c * kC + row];
+                const float inv = m / zcc.x;
+                if (!cwait(&bars[B_TDONE + j % kStages], (j / kStages) & 1)) break;  // dO, q^, k^ ready
+                float go[32];
+                load_chunks<kFp16>(slot_ptr(j, BL::g), row, hf * 4, 4, go);
+#pragma unroll
+                for (int x = 0; x < 32; ++x) go[x] *= inv;
+                if (tid == 0) tc::bulk_wait_read0();  // the previous dv store has left the o^ tile
+                tc::bar_sync(kBarCompute, kComputeThreads);
+#pragma unroll
+                for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + BL::ob, row, hf * 4 + x, go + 8 * x);
+                if (kNorm && hf == 0) {
+                    float c8[8] = {zcc.y, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                    store_chunk<kFp16>(sm + BL::ca, row, 0, c8);
+                }
+                publish(&bars[B_COCDONE]);
             }
-            for (int kk = 0; kk < 4; ++kk) {
-                tc::mma_f16(tX1, tc::sdesc_sw128(va + kk * 32, 16, 1024),  // dK~ += V dS_c^T
-                            tc::sdesc_sw128(sbase + BwdLayout::sb + kk * 32, 16, 1024), idKK, 1u);
-                tc::mma_f16(tX2, tc::sdesc_sw128(ka + kk * 32, 16, 1024),  // dV += K~ dS_c
-                            tc::sdesc_sw128(sbase + BwdLayout::sb + kk * 2048, 8192, 1024), idKM, 1u);
+            // (2) P^T and dA^T: causal mask (keep t >= tau), bf16 in place
+            if (!cwait(&bars[B_CPFULL], i & 1)) break;
+            mask_to_bf16(cPT, true);
+            mask_to_bf16(cDAT, true);
+            publish(&bars[B_CPDONE]);
+            // (3) suffix refresh: bf16 [dS^ | dz^] into sb[(i + 1) % 2]
+            if (!cwait(&bars[B_DSFULL], i & 1)) break;
+            refresh(cDS, sm + BL::sb + ((i + 1) & 1) * BL::sbuf);
+            publish(&bars[B_DSBDONE]);
+            // (4) dk = s dK~ phi'(k) m, dv = s dV m
+            if (!cwait(&bars[B_KVFULL], i & 1)) break;
+            {
+                const float m = row_mask_at(c, row);
+                float dk[32], dv[32], kv[32];
+                tc::tmem_ld32(tmem + cDK + loff + hf * 32, dk);
+                tc::tmem_ld32(tmem + cDV + loff + hf * 32, dv);
+                load_chunks<kFp16>(slot_ptr(j, BL::k), row, hf * 4, 4, kv);
+                const float sm_ = p.scale * m;
+#pragma unroll
+                for (int x = 0; x < 32; ++x) {
+                    dk[x] *= sm_ * min_nan(kv[x], 1.f);
+                    dv[x] *= sm_;
+                }
+                if (tid == 0) tc::bulk_wait_read0();  // staging free (previous dk store read)
+                tc::tc_fence_before();
+                tc::bar_sync(kBarCompute, kComputeThreads);
+                if (tid == 0) {
+                    tc::mbar_arrive(&bars[B_KVDONE]);
+                    tc::mbar_arrive(&bars[B_EMPTY + j % kStages]);
+                }
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                    store_chunk<kFp16>(sm + BL::os, row, hf * 4 + x, dk + 8 * x);
+                    store_chunk<kFp16>(sm + BL::ob, row, hf * 4 + x, dv + 8 * x);  // o^ is dead
+                }
+                tc::fence_proxy_async();
+                tc::bar_sync(kBarCompute, kComputeThreads);
+                if (tid == 0) {
+                    tc::tma_store_4d(&P.tm_dk, sm + BL::os, 0, c * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dv, sm + BL::ob, 0, c * kC, h, b);
+                    tc::bulk_commit();
+                }
             }
-            mma_xty(tdS, qa, sbase + BwdLayout::ob, false);  // dS_c-1
-            if (kNorm) mma_xtm(tdZ, qa, false);              // dz_c-1 (column 1)
-            tc::mma_commit(mma_bar);
         }
-        wait_mma();
-        if (!ok) break;
-        {
-            float acc[32], kv[32];
-            tc::tmem_ld32(tX1 + loff + hf * 32, acc);
-            load_chunks<kFp16>(kt, row, hf * 4, 4, kv);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float x = kNorm ? fmaf(m, dzcur[hf * 32 + j], acc[j]) : acc[j];
-                acc[j] = x * fminf(kv[j], 1.f) * m;
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(kt, row, hf * 4 + j, acc + 8 * j);
-            tc::tmem_ld32(tX2 + loff + hf * 32, acc);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] *= m;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) store_chunk<kFp16>(vt, row, hf * 4 + j, acc + 8 * j);
-        }
-        refresh_sb(tdS);
-        if (kNorm) read_col(tdZ, 1, dznext);
-        publish();
-        if (tid == 0) {
-            tc::tma_store_4d(&P.tm_dk, kt, 0, c * kC, h, b);
-            tc::tma_store_4d(&P.tm_dv, vt, 0, c * kC, h, b);
-            tc::bulk_commit();
-        }
+        if (tid == 0) tc::bulk_wait0();
     }
 
-    if (tid == 0) {
-        for (int s = 0; s < kStages; ++s)
-            if (pending[s]) wait_bar(&tma_bar[s], tma_phase[s], P.status);
-        tc::bulk_wait0();
-    }
     tc::tc_fence_before();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
+    if (warp == kWarpMma) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
 template <bool kFp16, bool kNorm>
@@ -632,7 +718,7 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     P.cps = (nC + P.G - 1) / P.G;
     const void* kern = reinterpret_cast<const void*>(&bwd_kernel<kFp16, kNorm>);
     void* args[] = {&P};
-    return launch_cluster(kern, P.G, p.B * p.H, kThreads, BwdLayout::total + 1024, st, args);
+    return launch_cluster(kern, P.G, p.B * p.H, kBwdThreads, BL::total + 1024, st, args);
 }
 
 }  // namespace

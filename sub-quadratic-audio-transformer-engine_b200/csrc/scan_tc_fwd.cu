@@ -443,7 +443,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 // O' and its normaliser column carry phi(q) unscaled: o = s O' / max(s Z', clamp)
                 const float m = row_mask_at(c, row);
                 float inv = m * p.scale;
-                if (kNorm) inv = inv / fmaxf(p.scale * zi, p.clamp_min);
+                if (kNorm) inv = inv / max_nan(p.scale * zi, p.clamp_min);
 #pragma unroll
                 for (int x = 0; x < 32; ++x) o[x] *= inv;
 #pragma unroll
