@@ -57,16 +57,14 @@ struct BL {
     static constexpr uint32_t ca = ob + kTile;         // c atom: column 0 = c_t
     static constexpr uint32_t sbuf = 2 * kD * kD * 2;  // bf16 [S | z] (or [dS | dz]): S atom + z atom
     static constexpr uint32_t sb = ca + kTile;         // two of them
-    static constexpr uint32_t os = sb + 2 * sbuf;      // output staging (dq, dk)
-    static constexpr uint32_t xz = os + kTile;         // [64] fp32 exchange of z / dz
+    static constexpr uint32_t xz = sb + 2 * sbuf;      // [64] fp32 exchange of z / dz
     static constexpr uint32_t dx = xz + 256;           // [2][128] fp32 partial dot products
     static constexpr uint32_t bars = dx + 1024;
     static constexpr uint32_t tslot = bars + 8 * 32;
     static constexpr uint32_t total = tslot + 16;
 };
 static_assert(kD * kD * 4 <= kTile, "exchange fits the o^ tile");
-static_assert(BL::ones % 1024 == 0 && BL::ob % 1024 == 0 && BL::ca % 1024 == 0 && BL::sb % 1024 == 0 &&
-                  BL::os % 1024 == 0,
+static_assert(BL::ones % 1024 == 0 && BL::ob % 1024 == 0 && BL::ca % 1024 == 0 && BL::sb % 1024 == 0,
               "alignment");
 static_assert(BL::total + 1024 <= 232448, "shared memory");
 
@@ -111,11 +109,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     const int b = bh / p.H, h = bh - b * p.H;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nC = (p.N + kC - 1) / kC;
-    const int c_begin = min(nC, g * P.cps);
-    const int n = min(nC, c_begin + P.cps) - c_begin;
-    const int nA = (g < P.G - 1) ? n : 0;  // phase-A chunks
-    // pipeline slots: [0, nA) phase A, [nA, nA + n) phase B, [nA + n, nA + 2n) phase C
-    const int nslots = nA + 2 * n;
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BL::bars);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + BL::tslot);
@@ -148,6 +141,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tslot;
+    // The segments split the live chunks (up to the sequence's last live token);
+    // the gradients of the chunks after them are zero-filled at the end.
+    const int nL = live_chunks(p, b, nC, reinterpret_cast<int*>(tslot + 1));
+    const int cps = (nL + P.G - 1) / P.G;
+    const int c_begin = min(nL, g * cps);
+    const int n = min(nL, c_begin + cps) - c_begin;
+    const int nA = (g < P.G - 1) ? n : 0;  // phase-A chunks
+    // pipeline slots: [0, nA) phase A, [nA, nA + n) phase B, [nA + n, nA + 2n) phase C
+    const int nslots = nA + 2 * n;
 
     // instruction descriptors
     constexpr uint32_t idPP = tc::idesc_f16<kFp16>(128, 128, false, false);  // K-major x K-major, N = 128
@@ -436,8 +438,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                     tc::mma_f16_ts(tmem + cNZ, tmem + cP + kk * 8, tc::sdesc_sw128(va + kk * 2048, lbo_v1, 1024),
                                    idNZ, 1u);
                 tc::mma_commit(&bars[B_NZFULL]);
-                if (i + 1 < n) ok = issue_p(i + 1);
-                if (!ok) break;
                 // dA = [o^ | c] [V | 1]^T ; dS^ sum += q^^T [o^ | c]
                 ok = wait_bar(&bars[B_OCDONE], i & 1, P.status);
                 if (!ok) break;
@@ -464,6 +464,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                     tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ca, 16, 1024),
                                 tc::sdesc_sw128(sba + kD * kD * 2, 16, 1024), idKK64, 1u);
                 tc::mma_commit(&bars[B_DQFULL]);
+                // P of the next chunk (its feature map has had this whole chunk to finish)
+                if (i + 1 < n) ok = issue_p(i + 1);
             }
         }
         __syncwarp();
@@ -475,17 +477,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 publish(&bars[B_PSDONE]);
             }
         }
+        float m_cur = n > 0 ? row_mask_at(c_begin, row) : 0.f;
         for (int i = 0; i < n && ok; ++i) {
             const int j = nA + i, c = c_begin + i;
-            // (1) state refresh: bf16 [S | z]_c+1 into sb[(i + 1) % 2]
+            const float m = m_cur;
+            if (i + 1 < n) m_cur = row_mask_at(c + 1, row);  // in flight during this chunk
+            // (1) state refresh: bf16 [S | z]_c+1 into sb[(i + 1) % 2]; the previous
+            // chunk's dq store has left its dO tile, so that slot is released
             if (!cwait(&bars[B_SFULL], i & 1)) break;
             refresh(cS, sm + BL::sb + ((i + 1) & 1) * BL::sbuf);
+            if (tid == 0 && i >= 1) {
+                tc::bulk_wait_read0();
+                tc::mbar_arrive(&bars[B_EMPTY + (j - 1) % kStages]);
+            }
             publish(&bars[B_SBDONE]);
             // (2) o^ and c from [num | Z] and dO (the slot's q^ and dO are complete
             // once its feature map is: TDONE implies FULL)
             if (!cwait(&bars[B_NZFULL], i & 1)) break;
             if (!cwait(&bars[B_TDONE + j % kStages], (j / kStages) & 1)) break;
-            const float m = row_mask_at(c, row);
             float num[32], go[32];
             tc::tmem_ld32(tmem + cNZ + loff + hf * 32, num);
             const float zraw = kNorm ? tmem_ld1(tmem + cNZ + loff + 64) : 0.f;
@@ -509,18 +518,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 }
                 if (c * kC + row < p.N) wsz[c * kC + row] = make_float2(zc, ct);
             }
-            publish(&bars[B_OCDONE]);  // also: every thread has read dxs and [N | Z]
-            // (3) P of the next chunk
-            if (i + 1 < n) {
-                if (!cwait(&bars[B_PFULL], (i + 1) & 1)) break;
-                mask_to_bf16(cP, false);
-                publish(&bars[B_PSDONE]);
-            }
-            // (4) dA: causal mask, bf16 in place
+            publish(&bars[B_OCDONE]);  // also: every thread has read dxs, [N | Z] and dO
+            // (3) dA: causal mask, bf16 in place
             if (!cwait(&bars[B_DAFULL], i & 1)) break;
             mask_to_bf16(cDA, false);
             publish(&bars[B_DADONE]);
-            // (5) dq = s dQ~ phi'(q)
+            // (4) dq = s dQ~ phi'(q), written over the slot's (dead) dO tile
             if (!cwait(&bars[B_DQFULL], i & 1)) break;
             {
                 float dq[32], qv[32];
@@ -528,22 +531,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 load_chunks<kFp16>(slot_ptr(j, BL::q), row, hf * 4, 4, qv);
 #pragma unroll
                 for (int x = 0; x < 32; ++x) dq[x] *= p.scale * min_nan(qv[x], 1.f);
-                if (tid == 0) tc::bulk_wait_read0();  // the staging tile is free again
+                uint8_t* dst = slot_ptr(j, BL::g);
+#pragma unroll
+                for (int x = 0; x < 4; ++x) store_chunk<kFp16>(dst, row, hf * 4 + x, dq + 8 * x);
+                tc::fence_proxy_async();
                 tc::tc_fence_before();
                 tc::bar_sync(kBarCompute, kComputeThreads);
                 if (tid == 0) {
-                    tc::mbar_arrive(&bars[B_DQDONE]);           // dQ~ columns read
-                    tc::mbar_arrive(&bars[B_EMPTY + j % kStages]);  // q^, dO of this slot read; MMAs done
-                }
-#pragma unroll
-                for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + BL::os, row, hf * 4 + x, dq + 8 * x);
-                tc::fence_proxy_async();
-                tc::bar_sync(kBarCompute, kComputeThreads);
-                if (tid == 0) {
-                    tc::tma_store_4d(&P.tm_dq, sm + BL::os, 0, c * kC, h, b);
+                    tc::mbar_arrive(&bars[B_DQDONE]);  // dQ~ columns read
+                    tc::tma_store_4d(&P.tm_dq, dst, 0, c * kC, h, b);
                     tc::bulk_commit();
                 }
             }
+            // (5) P of the next chunk: causal mask, bf16 in place
+            if (i + 1 < n) {
+                if (!cwait(&bars[B_PFULL], (i + 1) & 1)) break;
+                mask_to_bf16(cP, false);
+                publish(&bars[B_PSDONE]);
+            }
+        }
+        if (tid == 0 && n > 0) {  // release the last slot once its dq has left
+            tc::bulk_wait_read0();
+            tc::mbar_arrive(&bars[B_EMPTY + (nA + n - 1) % kStages]);
         }
     }
 
@@ -622,20 +631,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         }
         __syncwarp();
     } else if (warp < 8) {
+        // mask and (Zc, c) of a chunk's row, fetched one chunk ahead
+        auto fetch = [&](int cc, float& m_, float2& z_) {
+            m_ = row_mask_at(cc, row);
+            z_ = (cc * kC + row < p.N) ? wsz[cc * kC + row] : make_float2(1.f, 0.f);
+        };
+        float m_cur = 0.f;
+        float2 zcc_cur = make_float2(1.f, 0.f);
+        if (n > 0) fetch(c_begin + n - 1, m_cur, zcc_cur);
         for (int i = 0; i < n && ok; ++i) {
             const int j = nA + n + i, c = c_begin + n - 1 - i;
+            const float m = m_cur;
+            const float2 zcc = zcc_cur;
+            if (i + 1 < n) fetch(c - 1, m_cur, zcc_cur);
             // (1) o^ = m dO / Zc and the c atom, from the workspace
             {
-                const float m = row_mask_at(c, row);
-                float2 zcc = make_float2(1.f, 0.f);
-                if (c * kC + row < p.N) zcc = wsz[c * kC + row];
                 const float inv = m / zcc.x;
                 if (!cwait(&bars[B_TDONE + j % kStages], (j / kStages) & 1)) break;  // dO, q^, k^ ready
                 float go[32];
                 load_chunks<kFp16>(slot_ptr(j, BL::g), row, hf * 4, 4, go);
 #pragma unroll
                 for (int x = 0; x < 32; ++x) go[x] *= inv;
-                if (tid == 0) tc::bulk_wait_read0();  // the previous dv store has left the o^ tile
+                if (tid == 0 && i >= 1) {
+                    // the previous chunk's dk / dv stores have left its dO tile and
+                    // the o^ tile: that slot is released
+                    tc::bulk_wait_read0();
+                    tc::mbar_arrive(&bars[B_EMPTY + (j - 1) % kStages]);
+                }
                 tc::bar_sync(kBarCompute, kComputeThreads);
 #pragma unroll
                 for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + BL::ob, row, hf * 4 + x, go + 8 * x);
@@ -654,10 +676,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             if (!cwait(&bars[B_DSFULL], i & 1)) break;
             refresh(cDS, sm + BL::sb + ((i + 1) & 1) * BL::sbuf);
             publish(&bars[B_DSBDONE]);
-            // (4) dk = s dK~ phi'(k) m, dv = s dV m
+            // (4) dk = s dK~ phi'(k) m over the (dead) dO tile, dv = s dV m over o^
             if (!cwait(&bars[B_KVFULL], i & 1)) break;
             {
-                const float m = row_mask_at(c, row);
                 float dk[32], dv[32], kv[32];
                 tc::tmem_ld32(tmem + cDK + loff + hf * 32, dk);
                 tc::tmem_ld32(tmem + cDV + loff + hf * 32, dv);
@@ -668,25 +689,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                     dk[x] *= sm_ * min_nan(kv[x], 1.f);
                     dv[x] *= sm_;
                 }
-                if (tid == 0) tc::bulk_wait_read0();  // staging free (previous dk store read)
+                uint8_t* dst = slot_ptr(j, BL::g);
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                    store_chunk<kFp16>(dst, row, hf * 4 + x, dk + 8 * x);
+                    store_chunk<kFp16>(sm + BL::ob, row, hf * 4 + x, dv + 8 * x);
+                }
+                tc::fence_proxy_async();
                 tc::tc_fence_before();
                 tc::bar_sync(kBarCompute, kComputeThreads);
                 if (tid == 0) {
-                    tc::mbar_arrive(&bars[B_KVDONE]);
-                    tc::mbar_arrive(&bars[B_EMPTY + j % kStages]);
-                }
-#pragma unroll
-                for (int x = 0; x < 4; ++x) {
-                    store_chunk<kFp16>(sm + BL::os, row, hf * 4 + x, dk + 8 * x);
-                    store_chunk<kFp16>(sm + BL::ob, row, hf * 4 + x, dv + 8 * x);  // o^ is dead
-                }
-                tc::fence_proxy_async();
-                tc::bar_sync(kBarCompute, kComputeThreads);
-                if (tid == 0) {
-                    tc::tma_store_4d(&P.tm_dk, sm + BL::os, 0, c * kC, h, b);
+                    tc::mbar_arrive(&bars[B_KVDONE]);  // dK / dV columns read
+                    tc::tma_store_4d(&P.tm_dk, dst, 0, c * kC, h, b);
                     tc::tma_store_4d(&P.tm_dv, sm + BL::ob, 0, c * kC, h, b);
                     tc::bulk_commit();
                 }
+            }
+        }
+        // zero gradients of the chunks past the last live token (round-robin over the cluster)
+        if (nL + g < nC) {
+            if (tid == 0) tc::bulk_wait_read0();  // the o^ tile has been read by the last store
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            zero_chunks(sm + BL::ob, row, hf * 4, 4);
+            tc::fence_proxy_async();
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) {
+                for (int d = nL + g; d < nC; d += P.G) {
+                    tc::tma_store_4d(&P.tm_dq, sm + BL::ob, 0, d * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dk, sm + BL::ob, 0, d * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dv, sm + BL::ob, 0, d * kC, h, b);
+                }
+                tc::bulk_commit();
             }
         }
         if (tid == 0) tc::bulk_wait0();

@@ -105,9 +105,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     const int b = bh / p.H, h = bh - b * p.H;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nC = (p.N + kC - 1) / kC;
-    const int c_begin = min(nC, g * P.cps);
-    const int n = min(nC, c_begin + P.cps) - c_begin;
-    const int n1 = (g < P.G - 1) ? n : 0;  // phase-1 chunks
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::bars);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L::tslot);
@@ -131,6 +128,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tslot;
+    // The segments split the live chunks (up to the sequence's last live token);
+    // the chunks after them are zero-filled at the end.
+    const int nL = live_chunks(p, b, nC, reinterpret_cast<int*>(tslot + 1));
+    const int cps = (nL + P.G - 1) / P.G;
+    const int c_begin = min(nL, g * cps);
+    const int n = min(nL, c_begin + cps) - c_begin;
+    const int n1 = (g < P.G - 1) ? n : 0;  // phase-1 chunks
 
     constexpr uint32_t idP = tc::idesc_f16<kFp16>(128, 128, false, false);
     constexpr uint32_t idOX = tc::idesc_f16<kFp16>(128, kNX, false, true);  // phi~(Q) [S | z]
@@ -467,6 +471,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             if (p.z_out && hf == 0) {
                 const float zv = kNorm ? tmem_ld1(tmem + cS + loff + 64) : 0.f;
                 if (lane < 16) p.z_out[(int64_t)bh * kD + srow] = zv;
+            }
+        }
+        // zero outputs of the chunks past the last live token (round-robin over the cluster)
+        if (nL + g < nC) {
+            if (tid == 0) tc::bulk_wait_read0();  // the staging tile has been read
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            zero_chunks(sm + L::os, row, hf * 4, 4);
+            tc::fence_proxy_async();
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) {
+                for (int d = nL + g; d < nC; d += P.G) tc::tma_store_4d(&P.tm_o, sm + L::os, 0, d * kC, h, b);
+                tc::bulk_commit();
             }
         }
         if (tid == 0) tc::bulk_wait0();

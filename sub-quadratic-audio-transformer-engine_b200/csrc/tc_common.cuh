@@ -92,6 +92,40 @@ __device__ __forceinline__ uint32_t phi2<true>(uint32_t x) {
     return r;
 }
 
+// Number of leading 128-token chunks of sequence b up to and including the one
+// that holds its last live token (0 for a fully masked sequence; all chunks
+// without a mask). The chunks after it contribute nothing to any state and
+// their outputs are zero, so the scans skip them. Every thread of the CTA
+// calls this (it synchronises the block); `scratch` is one int of shared memory.
+__device__ __forceinline__ int live_chunks(const ScanParams& p, int b, int nC, int* scratch) {
+    if (!p.mask) return nC;
+    if (threadIdx.x == 0) *scratch = -1;
+    __syncthreads();
+    const uint8_t* row = p.mask + (int64_t)b * p.mask_sb;
+    int last = -1;
+    int t0 = 0;
+    if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {  // 16 tokens per load
+        const int nv = p.N >> 4;
+        const uint4* rv = reinterpret_cast<const uint4*>(row);
+        for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+            const uint4 w = rv[i];
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (ws[k]) last = max(last, i * 16 + k * 4 + (31 - __clz(ws[k])) / 8);
+        }
+        t0 = nv << 4;
+    }
+    for (int t = t0 + (int)threadIdx.x; t < p.N; t += blockDim.x)
+        if (row[t]) last = max(last, t);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+    if ((threadIdx.x & 31) == 0 && last >= 0) atomicMax(scratch, last);
+    __syncthreads();
+    const int l = *scratch;
+    return l < 0 ? 0 : l / kC + 1;
+}
+
 // Bounded mbarrier wait; on expiry records SUBQ_ERR_TIMEOUT in *status (the
 // library's device status word) and returns false.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {

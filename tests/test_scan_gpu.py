@@ -191,6 +191,33 @@ def test_tensorcore_wide_inputs_match_oracle(dtype):
     assert rel_err(dq, rq) < 2e-2 and rel_err(dk, rk) < 2e-2 and rel_err(dv, rv) < 2e-2
 
 
+def test_tensorcore_skips_masked_tails():
+    """Chunks after a sequence's last live token are skipped and zero-filled:
+    a full row, a short row, a row with one live token in the middle and an
+    empty row, fed through several segment splits (H changes the cluster size)."""
+    B, N = 4, 1000
+    for H in (1, 8):
+        q, k, v, do, _, _, _ = make_case(B, H, N, 64, 64, torch.bfloat16, seed=31 + H)
+        m = torch.zeros(B, N, dtype=torch.bool)
+        m[0] = True
+        m[1, :130] = True
+        m[2, 500] = True
+        qn, kn, vn, don, _, mn, _, _ = oracle_inputs(q, k, v, do, None, m, None, B, H, N)
+        ref_o, ref_S, ref_z, _ = oracle.forward(qn, kn, vn, mask=mn, normalize=True, scale=0.125)
+        rq, rk, rv, _ = oracle.backward(qn, kn, vn, don, mask=mn, normalize=True, scale=0.125)
+        dev = [to_dev(x) for x in (q, k, v, do, m)]
+        o = torch.full_like(dev[0], float("nan"))  # stale contents must be overwritten
+        o, (S, z) = ops.scan_forward(dev[0], dev[1], dev[2], mask=dev[4], return_state=True, out=o,
+                                     path="tensorcore")
+        dq, dk, dv, _ = ops.scan_backward(*dev[:4], mask=dev[4], path="tensorcore")
+        torch.cuda.synchronize()
+        assert rel_err(o, ref_o) < 2e-2
+        assert rel_err(S, ref_S) < 2e-2 and rel_err(z, ref_z) < 2e-2
+        assert rel_err(dq, rq) < 2e-2 and rel_err(dk, rk) < 2e-2 and rel_err(dv, rv) < 2e-2
+        for t in (o, dq, dk, dv):
+            assert torch.count_nonzero(t[1:, :, 501:]) == 0 and torch.count_nonzero(t[3]) == 0
+
+
 def test_tensorcore_nan_propagates_like_elu():
     """ELU(NaN) + 1 = NaN: a NaN query spoils its own output row; a NaN key
     spoils every later row (through the state), and no earlier one."""
