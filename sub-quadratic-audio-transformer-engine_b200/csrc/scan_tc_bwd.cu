@@ -57,8 +57,8 @@ struct BL {
     static constexpr uint32_t ca = ob + kTile;         // c atom: column 0 = c_t
     static constexpr uint32_t sbuf = 2 * kD * kD * 2;  // bf16 [S | z] (or [dS | dz]): S atom + z atom
     static constexpr uint32_t sb = ca + kTile;         // two of them
-    static constexpr uint32_t xz = sb + 2 * sbuf;      // [64] fp32 exchange of z / dz
-    static constexpr uint32_t dx = xz + 256;           // [2][128] fp32 partial dot products
+    static constexpr uint32_t xz = sb + 2 * sbuf;      // [2][64] fp32 exchange of z / dz
+    static constexpr uint32_t dx = xz + 512;           // [2][128] fp32 partial dot products
     static constexpr uint32_t bars = dx + 1024;
     static constexpr uint32_t tslot = bars + 8 * 32;
     static constexpr uint32_t total = tslot + 16;
@@ -112,8 +112,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BL::bars);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + BL::tslot);
-    float* Xs = reinterpret_cast<float*>(sm + BL::ob);  // [64][64] exchange (o^ tile between phases)
-    float* Xz = reinterpret_cast<float*>(sm + BL::xz);  // [64]
+    // exchange buffers between phases: [64][64] fp32 partial sums in the o^ tile
+    // (and a second one in sb[0]), their normaliser parts [2][64] in xz
+    float* Xs = reinterpret_cast<float*>(sm + BL::ob);
+    float* Xs2 = reinterpret_cast<float*>(sm + BL::sb);
+    float* Xz = reinterpret_cast<float*>(sm + BL::xz);
     float* dxs = reinterpret_cast<float*>(sm + BL::dx);
     const uint32_t sbase = tc::smem_u32(sm);
     float2* wsz = reinterpret_cast<float2*>(p.ws) + (int64_t)bh * p.N;
@@ -147,7 +150,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     const int cps = (nL + P.G - 1) / P.G;
     const int c_begin = min(nL, g * cps);
     const int n = min(nL, c_begin + cps) - c_begin;
-    const int nA = (g < P.G - 1) ? n : 0;  // phase-A chunks
+    const PrefixShare share = prefix_share(g, P.G, nL, cps);
+    const int nA = share.b - share.a;  // phase-A chunks: this CTA's share of the segment sums
     // pipeline slots: [0, nA) phase A, [nA, nA + n) phase B, [nA + n, nA + 2n) phase C
     const int nslots = nA + 2 * n;
 
@@ -163,12 +167,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         if (t >= p.N) return 0.f;
         return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
     };
-    // chunk of pipeline slot j (phase A visits its segment rotated per sequence)
+    // chunk of pipeline slot j (phase A visits its share rotated per sequence)
     const int rot = nA > 0 ? (bh * 7) % nA : 0;
     auto chunk_of = [&](int j) {
         if (j < nA) {
             const int r = j + rot;
-            return c_begin + (r >= nA ? r - nA : r);
+            return share.a + (r >= nA ? r - nA : r);
         }
         if (j < nA + n) return c_begin + (j - nA);
         return c_begin + n - 1 - (j - nA - n);
@@ -288,8 +292,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         if (ok) tc::tc_fence_after();
         return ok;
     };
-    // exchange helpers (compute warps): own M = 64 accumulator -> Xs / Xz
-    auto publish_sums = [&](uint32_t tcol, bool have) {
+    // exchange helpers (compute warps): own M = 64 accumulator -> X / Xz[piece]
+    auto publish_sums = [&](uint32_t tcol, bool have, float* X, int piece) {
         float v[32];
         if (have) {
             tc::tmem_ld32(tmem + tcol + loff + hf * 32, v);
@@ -299,11 +303,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         }
         if (lane < 16) {
 #pragma unroll
-            for (int x = 0; x < 32; ++x) Xs[srow * 64 + hf * 32 + x] = v[x];
+            for (int x = 0; x < 32; ++x) X[srow * 64 + hf * 32 + x] = v[x];
         }
         if (hf == 0) {
             const float zv = (kNorm && have) ? tmem_ld1(tmem + tcol + loff + 64) : 0.f;
-            if (lane < 16) Xz[srow] = zv;
+            if (lane < 16) Xz[piece * 64 + srow] = zv;
+        }
+    };
+    // S_in plus the partial segment sums of the segments before this CTA's
+    auto gather_prefix = [&](float* v, float& z) {
+#pragma unroll
+        for (int x = 0; x < 32; ++x) v[x] = 0.f;
+        z = 0.f;
+        if (lane < 16) {
+            if (p.S_in) {
+                const float* src = p.S_in + ((int64_t)bh * kD + srow) * kD + hf * 32;
+#pragma unroll
+                for (int x = 0; x < 32; ++x) v[x] = src[x];
+            }
+            if (kNorm && hf == 0) z = p.z_in ? p.z_in[(int64_t)bh * kD + srow] : 0.f;
+            for (int r = 0; r < P.G; ++r) {
+                const PrefixShare sr = prefix_share(r, P.G, nL, cps);
+#pragma unroll
+                for (int piece = 0; piece < 2; ++piece) {
+                    const bool used = piece == 0 ? (min(sr.b, sr.x) > sr.a && sr.seg < g)
+                                                 : (sr.b > sr.x && sr.seg + 1 < g);
+                    if (!used) continue;
+                    const float* rx = cluster.map_shared_rank(piece == 0 ? Xs : Xs2, r) + srow * 64 + hf * 32;
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) v[x] += rx[x];
+                    if (kNorm && hf == 0) z += cluster.map_shared_rank(Xz, r)[piece * 64 + srow];
+                }
+            }
         }
     };
     // sum of the exchanged values of CTAs [r0, r1) (+ an optional fp32 base)
@@ -337,9 +368,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         }
         tc::tmem_st32(tmem + tcol + loff + hf * 32, v);
         if (hf == 0) {
-            if (kNorm && lane < 16) {
+            if (lane < 16) {
                 float z8[8] = {z, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                 store_chunk<kFp16>(dst + kD * kD * 2, srow, 0, z8);
+                zero_chunks(dst + kD * kD * 2, srow, 1, 1);
             }
             float w[32];
 #pragma unroll
@@ -362,28 +394,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         transform(0, nA);
     } else if (warp == kWarpMma) {
         if (lane == 0) {
+            // the share's two partial sums accumulate in S (before the segment
+            // boundary) and in the still unused P columns (after it)
+            bool first1 = true, first2 = true;
             for (int j = 0; j < nA && ok; ++j) {
                 const int s = j % kStages, u = j / kStages;
                 ok = wait_bar(&bars[B_TDONE + s], u & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
-                mma_xt(tmem + cS, slot_addr(j, BL::k), slot_addr(j, BL::v), sbase + BL::ones, j == 0);
+                const bool second = chunk_of(j) >= share.x;
+                mma_xt(tmem + (second ? cP : cS), slot_addr(j, BL::k), slot_addr(j, BL::v), sbase + BL::ones,
+                       second ? first2 : first1);
+                (second ? first2 : first1) = false;
                 tc::mma_commit(&bars[B_EMPTY + s]);
             }
             if (nA > 0 && ok) tc::mma_commit(&bars[B_AFULL]);
         }
         __syncwarp();
     } else if (warp < 8) {
-        if (g < P.G - 1) {
-            if (nA > 0) cwait(&bars[B_AFULL], 0);
-            publish_sums(cS, nA > 0 && ok);
-        }
+        if (nA > 0) cwait(&bars[B_AFULL], 0);
+        publish_sums(cS, ok && min(share.b, share.x) > share.a, Xs, 0);
+        publish_sums(cP, ok && share.b > share.x, Xs2, 1);
     }
     tc::tc_fence_before();
     cluster.sync();
     tc::tc_fence_after();
     float carry[32], carry_z = 0.f;  // prefix (phase B) / suffix (phase C) state rows, compute warps
-    if (warp < 8) gather_sums(0, g, p.S_in, p.z_in, carry, carry_z);
+    if (warp < 8) gather_prefix(carry, carry_z);
     tc::tc_fence_before();
     cluster.sync();  // remote reads done before the exchange tile is reused
     tc::tc_fence_after();
@@ -557,7 +594,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     }
 
     // ------------------------------------------------ suffix exchange (dS^, dz^)
-    if (warp < 8) publish_sums(cDS, n > 0 && ok);
+    if (warp < 8) publish_sums(cDS, n > 0 && ok, Xs, 0);
     tc::tc_fence_before();
     cluster.sync();
     tc::tc_fence_after();

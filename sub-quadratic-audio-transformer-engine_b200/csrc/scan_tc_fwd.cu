@@ -54,10 +54,11 @@ struct L {
     static constexpr uint32_t ones = kStages * stage;  // 128 x 64 atom, column 0 = 1 (the "| 1" of [V | 1])
     static constexpr uint32_t sbuf = 2 * kD * kD * 2;  // one bf16 [S_c | z_c]: two 64 x 64 atoms (MN-major B)
     static constexpr uint32_t sb = ones + kTile;       // two of them: chunk c reads sb[c % 2]
-    static constexpr uint32_t os = sb + 2 * sbuf;      // output staging; before phase 2 the
-                                                       // segment-sum exchange [64][64] fp32
-    static constexpr uint32_t xz = os + kTile;         // segment-sum exchange [64] fp32
-    static constexpr uint32_t bars = xz + 256;
+    static constexpr uint32_t os = sb + 2 * sbuf;      // output staging; before phase 2 the first
+                                                       // partial segment sum [64][64] fp32 (the
+                                                       // second one uses sb[0])
+    static constexpr uint32_t xz = os + kTile;         // their normaliser parts [2][64] fp32
+    static constexpr uint32_t bars = xz + 512;
     static constexpr uint32_t tslot = bars + 8 * 24;
     static constexpr uint32_t total = tslot + 16;
 };
@@ -108,8 +109,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::bars);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L::tslot);
-    float* Xs = reinterpret_cast<float*>(sm + L::os);  // [64][64] segment sum phi~(K)^T V
-    float* Xz = reinterpret_cast<float*>(sm + L::xz);  // [64] segment sum phi~(K)^T 1
+    float* Xs1 = reinterpret_cast<float*>(sm + L::os);  // [64][64] partial sums phi~(K)^T V
+    float* Xs2 = reinterpret_cast<float*>(sm + L::sb);
+    float* Xz = reinterpret_cast<float*>(sm + L::xz);   // [2][64] partial sums phi~(K)^T 1
     const uint32_t sbase = tc::smem_u32(sm);
 
     if (tid == 0) {
@@ -134,7 +136,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     const int cps = (nL + P.G - 1) / P.G;
     const int c_begin = min(nL, g * cps);
     const int n = min(nL, c_begin + cps) - c_begin;
-    const int n1 = (g < P.G - 1) ? n : 0;  // phase-1 chunks
+    const PrefixShare share = prefix_share(g, P.G, nL, cps);
+    const int n1 = share.b - share.a;  // phase-1 chunks: this CTA's share of the segment sums
 
     constexpr uint32_t idP = tc::idesc_f16<kFp16>(128, 128, false, false);
     constexpr uint32_t idOX = tc::idesc_f16<kFp16>(128, kNX, false, true);  // phi~(Q) [S | z]
@@ -146,25 +149,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         if (t >= p.N) return 0.f;
         return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
     };
-    // [S|z] (+)= phi~(K)^T [V | 1] over the chunk in stage s (8 K-steps of 16 tokens).
-    auto mma_state = [&](int s, bool first) {
+    // [S|z] (+)= phi~(K)^T [V | 1] over the chunk in stage s (8 K-steps of 16 tokens),
+    // into the M = 64 accumulator at TMEM column `col`.
+    auto mma_state = [&](int s, bool first, uint32_t col = cS) {
         const uint32_t ka = sbase + s * L::stage + L::k, va = sbase + s * L::stage + L::v;
         const uint32_t lbo = L::ones - (s * L::stage + L::v);  // V atom -> ones atom
         const uint32_t n80 = kNorm ? idSX : tc::idesc_f16<kFp16>(64, 64, true, true);
         for (int kk = 0; kk < 8; ++kk)
-            tc::mma_f16(tmem + cS, tc::sdesc_sw128(ka + kk * 2048, kTile, 1024),
+            tc::mma_f16(tmem + col, tc::sdesc_sw128(ka + kk * 2048, kTile, 1024),
                         tc::sdesc_sw128(va + kk * 2048, lbo, 1024), n80, (first && kk == 0) ? 0u : 1u);
     };
 
-    // Chunk of pipeline slot j: phase-1 slots (j < n1) visit the segment in an
+    // Chunk of pipeline slot j: phase-1 slots (j < n1) visit the share in an
     // order rotated per sequence, so that the clusters do not all read the
-    // same offset of their sequences at the same time (the segment sum does not
-    // depend on the order); phase-2 slots run in order.
+    // same offset of their sequences at the same time (the sums do not depend
+    // on the order); phase-2 slots run the segment in order.
     const int rot = n1 > 0 ? (bh * 7) % n1 : 0;
     auto chunk_of = [&](int j) {
         if (j >= n1) return c_begin + (j - n1);
         const int r = j + rot;
-        return c_begin + (r >= n1 ? r - n1 : r);
+        return share.a + (r >= n1 ? r - n1 : r);
     };
 
     bool ok = true;
@@ -216,12 +220,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         transform(0, n1);
     } else if (warp == kWarpMma) {
         if (lane == 0) {
+            // the share's two partial sums accumulate in S' (before the segment
+            // boundary) and in the still unused P columns (after it)
+            bool first1 = true, first2 = true;
             for (int j = 0; j < n1 && ok; ++j) {
                 const int s = j % kStages, u = j / kStages;
                 ok = wait_bar(&bars[B_TDONE + s], u & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
-                mma_state(s, j == 0);
+                if (chunk_of(j) < share.x) {
+                    mma_state(s, first1, cS);
+                    first1 = false;
+                } else {
+                    mma_state(s, first2, cP);
+                    first2 = false;
+                }
                 tc::mma_commit(&bars[B_EMPTY + s]);
             }
             if (n1 > 0 && ok) tc::mma_commit(&bars[B_SFULL]);
@@ -237,21 +250,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             sfull_count = 1;
             tc::tc_fence_after();
         }
-        if (g < P.G - 1) {
+        const bool have1 = ok && min(share.b, share.x) > share.a, have2 = ok && share.b > share.x;
+#pragma unroll
+        for (int piece = 0; piece < 2; ++piece) {
+            const bool have = piece == 0 ? have1 : have2;
+            const uint32_t col = piece == 0 ? cS : cP;
+            float* X = piece == 0 ? Xs1 : Xs2;
             float v[32];
-            if (n1 > 0 && ok) {
-                tc::tmem_ld32(tmem + cS + loff + hf * 32, v);
+            if (have) {
+                tc::tmem_ld32(tmem + col + loff + hf * 32, v);
             } else {
 #pragma unroll
                 for (int x = 0; x < 32; ++x) v[x] = 0.f;
             }
             if (lane < 16) {
 #pragma unroll
-                for (int x = 0; x < 32; ++x) Xs[srow * 64 + hf * 32 + x] = v[x];
+                for (int x = 0; x < 32; ++x) X[srow * 64 + hf * 32 + x] = v[x];
             }
             if (hf == 0) {
-                const float zv = (kNorm && n1 > 0 && ok) ? tmem_ld1(tmem + cS + loff + 64) : 0.f;
-                if (lane < 16) Xz[srow] = zv;
+                const float zv = (kNorm && have) ? tmem_ld1(tmem + col + loff + 64) : 0.f;
+                if (lane < 16) Xz[piece * 64 + srow] = zv;
             }
         }
     }
@@ -260,33 +278,46 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     tc::tc_fence_after();
 
     // ------------------------------------------------------ segment prefix
+    // S_in plus every partial sum of a segment before this CTA's, read over DSMEM
+    float v[32], z = 0.f;
+#pragma unroll
+    for (int x = 0; x < 32; ++x) v[x] = 0.f;
     if (warp < 8) {
         const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
-        const uint32_t loff = (uint32_t)(quad * 32) << 16;
-        float v[32];
-#pragma unroll
-        for (int x = 0; x < 32; ++x) v[x] = 0.f;
         if (lane < 16) {
             if (p.S_in) {
                 const float* src = p.S_in + ((int64_t)bh * kD + srow) * kD + hf * 32;
 #pragma unroll
                 for (int x = 0; x < 32; ++x) v[x] = src[x];
             }
-            for (int r = 0; r < g; ++r) {
-                const float* rx = cluster.map_shared_rank(Xs, r) + srow * 64 + hf * 32;
+            if (kNorm && hf == 0) z = p.z_in ? p.z_in[(int64_t)bh * kD + srow] : 0.f;
+            for (int r = 0; r < P.G; ++r) {
+                const PrefixShare sr = prefix_share(r, P.G, nL, cps);
 #pragma unroll
-                for (int x = 0; x < 32; ++x) v[x] += rx[x];
+                for (int piece = 0; piece < 2; ++piece) {
+                    const bool used = piece == 0 ? (min(sr.b, sr.x) > sr.a && sr.seg < g)
+                                                 : (sr.b > sr.x && sr.seg + 1 < g);
+                    if (!used) continue;
+                    const float* rx = cluster.map_shared_rank(piece == 0 ? Xs1 : Xs2, r) + srow * 64 + hf * 32;
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) v[x] += rx[x];
+                    if (kNorm && hf == 0) z += cluster.map_shared_rank(Xz, r)[piece * 64 + srow];
+                }
             }
+        }
+    }
+    tc::tc_fence_before();
+    cluster.sync();  // remote reads done before the exchange buffers are reused
+    tc::tc_fence_after();
+    if (warp < 8) {
+        const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
+        const uint32_t loff = (uint32_t)(quad * 32) << 16;
+        if (lane < 16) {
 #pragma unroll
             for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + L::sb, srow, hf * 4 + x, v + 8 * x);
         }
         tc::tmem_st32(tmem + cS + loff + hf * 32, v);
         if (hf == 0) {
-            float z = 0.f;
-            if (kNorm && lane < 16) {
-                z = p.z_in ? p.z_in[(int64_t)bh * kD + srow] : 0.f;
-                for (int r = 0; r < g; ++r) z += cluster.map_shared_rank(Xz, r)[srow];
-            }
             if (lane < 16) {
                 float zc8[8] = {z, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                 store_chunk<kFp16>(sm + L::sb + kD * kD * 2, srow, 0, zc8);
@@ -303,7 +334,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         tc::fence_proxy_async();
     }
     tc::tc_fence_before();
-    cluster.sync();  // remote reads done; prefix state published
+    __syncthreads();  // prefix state in place
     tc::tc_fence_after();
 
     // ============================================================ phase 2

@@ -126,6 +126,26 @@ __device__ __forceinline__ int live_chunks(const ScanParams& p, int b, int nC, i
     return l < 0 ? 0 : l / kC + 1;
 }
 
+// Work split of the segment sums. Segment s of a sequence is the chunk range
+// [s cps, (s + 1) cps) of its live chunks; CTA g of the cluster needs the sum of
+// phi~(K)^T [V | 1] over segments 0..g-1. The chunks [0, Ptot) before the last
+// segment are summed once, by all G CTAs together: CTA r takes [a, b) (an even
+// share). A share is shorter than a segment, so it crosses at most one segment
+// boundary x and yields two partial sums: [a, min(b, x)) of segment seg and
+// [x, b) of segment seg + 1 (empty when b <= x).
+struct PrefixShare {
+    int a, b, x, seg;
+};
+__device__ __forceinline__ PrefixShare prefix_share(int r, int G, int nL, int cps) {
+    PrefixShare s;
+    const int total = min(nL, (G - 1) * cps);
+    s.a = (int)((int64_t)r * total / G);
+    s.b = (int)((int64_t)(r + 1) * total / G);
+    s.seg = cps > 0 ? s.a / cps : 0;
+    s.x = (s.seg + 1) * cps;
+    return s;
+}
+
 // Bounded mbarrier wait; on expiry records SUBQ_ERR_TIMEOUT in *status (the
 // library's device status word) and returns false.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {
