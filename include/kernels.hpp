@@ -139,6 +139,20 @@ size_t subq_bwd_workspace_bytes(const subq_bwd_args* args);
 /* In-place phi(x) = ELU(x) + 1 over n contiguous elements (run_feature_map). */
 int subq_feature_map(void* x, int64_t n, int32_t dtype, void* stream);
 
+/* Backward scan with no allocation and no caller workspace (no counterpart in
+ * the reference, whose backward allocates its scratch on every call). For
+ * callers that may not supply or grow device memory per call, such as a
+ * real-time audio callback or a host with a fixed device budget: the scratch
+ * is a static 8 MiB device buffer of the library (1,048,576 token-heads
+ * B x H x N on the tensor-core path, 699,050 on the float32 exact path);
+ * larger calls return SUBQ_ERR_WORKSPACE. `workspace` and `workspace_bytes`
+ * of args are ignored. Nothing in the buffer needs to start at zero. There is
+ * one buffer per device, so calls that overlap in time on one device race:
+ * serialise them. The first call on a device looks the buffer up with that
+ * device current; make it before capturing any of the device's streams.
+ * Results equal subq_bwd's. */
+int subq_bwd_noalloc(const subq_bwd_args* args);
+
 /* Synchronises `stream`, then reads and clears the device status word of the
  * current device: SUBQ_OK, or SUBQ_ERR_TIMEOUT when a bounded device-side wait
  * of a tensor-core kernel gave up since the last query (its outputs are then

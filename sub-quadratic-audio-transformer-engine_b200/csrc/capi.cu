@@ -4,6 +4,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
 
 #include "kernels.hpp"
@@ -269,3 +270,73 @@ int subq_device_info(int device, char* arch, size_t arch_len, size_t* memory_byt
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free backward (subq_bwd_noalloc).
+//
+// Some callers cannot hand the library any device memory for scratch: a
+// real-time audio callback must not block on, or fail in, an allocator in the
+// middle of a frame, and a host that owns a fixed device budget (a pool sized
+// up front) may not grow it per call. For them the backward runs with a
+// scratch buffer that is part of this library's static device memory, placed
+// when the module loads, so the call itself allocates nothing.
+//
+//  * Capacity: kNoAllocScratchBytes = 8 MiB, enough for 1,048,576 token-heads
+//    (B x H x N) on the tensor-core path (8 bytes each) and 699,050 on the
+//    float32 exact path (12 bytes each). A larger call is rejected with
+//    SUBQ_ERR_WORKSPACE before anything is launched.
+//  * Nothing in the scratch has to start at zero: every call writes each
+//    per-token entry it later reads (the clamped normaliser and the quotient
+//    coefficient, or the exact path's per-token values) before reading it.
+//  * One buffer per device: calls that overlap in time on one device (two
+//    streams, or host threads without ordering between them) race on it, so
+//    such callers must serialise their calls.
+//  * The first call on a device looks the buffer's address up with
+//    cudaGetSymbolAddress while that device is current; make that first call
+//    before capturing any stream of the device, so the lookup is not part of
+//    a capture.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Address of this device's scratch; looked up once per device.
+int noalloc_scratch(void** out) {
+    int dev = -1;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return fail_cuda(err, "subq_bwd_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(SUBQ_ERR_UNSUPPORTED, "subq_bwd_noalloc: device index above 63");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (err != cudaSuccess) return fail_cuda(err, "subq_bwd_noalloc: cudaGetSymbolAddress");
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return SUBQ_OK;
+}
+
+}  // namespace
+
+extern "C" int subq_bwd_noalloc(const subq_bwd_args* args) {
+    if (!args) return fail(SUBQ_ERR_INVALID_ARGUMENT, "args is null");
+    const size_t need = subq_bwd_workspace_bytes(args);
+    if (need > kNoAllocScratchBytes)
+        return fail(SUBQ_ERR_WORKSPACE, "subq_bwd_noalloc: this call needs " + std::to_string(need) +
+                                            " bytes of scratch, above the built-in " +
+                                            std::to_string(kNoAllocScratchBytes) +
+                                            " bytes (8 MiB); use subq_bwd with a caller workspace");
+    void* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    subq_bwd_args a = *args;
+    a.workspace = scratch;
+    a.workspace_bytes = kNoAllocScratchBytes;
+    return subq_bwd(&a);
+}

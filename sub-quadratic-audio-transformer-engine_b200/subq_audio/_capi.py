@@ -29,7 +29,7 @@ SUBQ_PATH_AUTO, SUBQ_PATH_EXACT, SUBQ_PATH_TENSORCORE = 0, 1, 2
 EXPORTED = (
     "subq_fwd", "subq_bwd", "subq_fwd_workspace_bytes", "subq_bwd_workspace_bytes",
     "subq_feature_map", "subq_last_path", "subq_last_launches", "subq_last_error",
-    "subq_abi_version", "subq_device_info", "subq_device_status",
+    "subq_abi_version", "subq_device_info", "subq_device_status", "subq_bwd_noalloc",
 )
 
 
@@ -99,6 +99,8 @@ def load() -> ctypes.CDLL:
             lib.subq_fwd.restype = ctypes.c_int
             lib.subq_bwd.argtypes = [ctypes.POINTER(BwdArgs)]
             lib.subq_bwd.restype = ctypes.c_int
+            lib.subq_bwd_noalloc.argtypes = [ctypes.POINTER(BwdArgs)]
+            lib.subq_bwd_noalloc.restype = ctypes.c_int
             lib.subq_fwd_workspace_bytes.argtypes = [ctypes.POINTER(FwdArgs)]
             lib.subq_fwd_workspace_bytes.restype = ctypes.c_size_t
             lib.subq_bwd_workspace_bytes.argtypes = [ctypes.POINTER(BwdArgs)]
@@ -132,6 +134,11 @@ def fwd(args: FwdArgs) -> None:
 
 def bwd(args: BwdArgs) -> None:
     check(load().subq_bwd(ctypes.byref(args)))
+
+
+def bwd_noalloc(args: BwdArgs) -> None:
+    """subq_bwd_noalloc: the backward with the library's static scratch."""
+    check(load().subq_bwd_noalloc(ctypes.byref(args)))
 
 
 def fwd_workspace_bytes(args: FwdArgs) -> int:

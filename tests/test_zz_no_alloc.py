@@ -1,0 +1,68 @@
+"""subq_bwd_noalloc (the backward with the library's static scratch), called
+through the C ABI and compared with subq_bwd on the same inputs.
+
+The file name sorts last, so in a full run it executes after every other
+test; it also passes alone in a fresh process.
+"""
+import math
+
+import pytest
+import torch
+
+from subq_audio import _capi, ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(B, H, N, d, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v, do = (torch.randn(B, H, N, d, generator=g).to(dtype).cuda() for _ in range(4))
+    lens = torch.randint(N // 2, N + 1, (B,), generator=g)
+    mask = (torch.arange(N)[None, :] < lens[:, None]).cuda()
+    return q, k, v, do, mask
+
+
+def _noalloc_backward(q, k, v, do, mask):
+    """One subq_bwd_noalloc call: the caller provides inputs and outputs only."""
+    B, H, N, d = q.shape
+    keep = []
+    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+    a = _capi.BwdArgs()
+    a.desc = ops._desc(q, v, None, mask, True, None, 1e-5, False, "auto", keep)
+    a.q, a.k, a.v, a.dout = ops._t4(q), ops._t4(k), ops._t4(v), ops._t4(do)
+    a.dq, a.dk, a.dv = ops._t4(dq), ops._t4(dk), ops._t4(dv)
+    a.stream = torch.cuda.current_stream().cuda_stream
+    a.workspace, a.workspace_bytes = None, 0
+    _capi.bwd_noalloc(a)
+    return dq, dk, dv
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 64), (torch.float32, 16)])
+def test_noalloc_backward_equals_subq_bwd_twice(dtype, d):
+    q, k, v, do, mask = _case(2, 4, 1000, d, dtype, seed=11 + d)
+    ref = ops.scan_backward(q, k, v, do, mask=mask)[:3]
+    path = ops.last_path()
+    for _ in range(2):  # the static scratch is reused by back-to-back calls
+        got = _noalloc_backward(q, k, v, do, mask)
+        torch.cuda.synchronize()
+        assert ops.last_path() == path
+        for x, y in zip(got, ref):
+            assert torch.equal(x, y)
+
+
+def test_noalloc_backward_rejects_calls_above_its_scratch():
+    # 1,048,577 token-heads on the tensor-core path: one above the 8 MiB scratch
+    N = (8 << 20) // 8 + 1
+    q = torch.zeros(1, 1, N, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_capi.SubqError) as err:
+        _noalloc_backward(q, q, q, q, None)
+    assert err.value.code == _capi.SUBQ_ERR_WORKSPACE
+    assert "8 MiB" in str(err.value)
+    # exactly at capacity the call runs
+    n_ok = (8 << 20) // 8 // 1024
+    q2, k2, v2, do2, _ = _case(1, 1024, n_ok, 64, torch.bfloat16, seed=5)
+    got = _noalloc_backward(q2, k2, v2, do2, None)
+    ref = ops.scan_backward(q2, k2, v2, do2)[:3]
+    for x, y in zip(got, ref):
+        assert torch.equal(x, y)
+    assert math.isfinite(got[0].float().abs().max().item())
