@@ -242,19 +242,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             for (int x = 0; x < 32; ++x) packed[x] = 0u;
         } else {
             const bool diag = (hf == (quad >> 1));
-            float v[64];
-            tc::tmem_ld32(tmem + tcol + loff + hf * 64, v);
-            tc::tmem_ld32(tmem + tcol + loff + hf * 64 + 32, v + 32);
-            if (diag) {
-#pragma unroll
-                for (int x = 0; x < 64; ++x) {
-                    const int col = hf * 64 + x;
-                    if (keep_upper ? (col < row) : (col > row)) v[x] = 0.f;
-                }
-            }
+            uint32_t r[64];
+            tc::tmem_ld32_issue(tmem + tcol + loff + hf * 64, r);
+            tc::tmem_ld32_issue(tmem + tcol + loff + hf * 64 + 32, r + 32);
+            tc::tmem_wait_ld();
+            tc::tmem_regs_ready<64>(r);
 #pragma unroll
             for (int x = 0; x < 32; ++x) {
-                typename E::T2 h2 = E::from2(v[2 * x], v[2 * x + 1]);
+                float a = __uint_as_float(r[2 * x]), bb = __uint_as_float(r[2 * x + 1]);
+                if (diag) {
+                    const int col = hf * 64 + 2 * x;
+                    if (keep_upper ? (col < row) : (col > row)) a = 0.f;
+                    if (keep_upper ? (col + 1 < row) : (col + 1 > row)) bb = 0.f;
+                }
+                typename E::T2 h2 = E::from2(a, bb);
                 packed[x] = *reinterpret_cast<uint32_t*>(&h2);
             }
         }
@@ -440,9 +441,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         transform(nA, nA + n);
     } else if (warp == kWarpMma) {
         if (lane == 0) {
-            auto issue_p = [&](int i) -> bool {  // P = q^ k^^T
+            auto issue_p = [&](int i, bool ready = false) -> bool {  // P = q^ k^^T
                 const int j = nA + i;
-                if (!wait_bar(&bars[B_TDONE + j % kStages], (j / kStages) & 1, P.status)) return false;
+                if (!ready && !wait_bar(&bars[B_TDONE + j % kStages], (j / kStages) & 1, P.status)) return false;
                 tc::tc_fence_after();
                 const uint32_t qa = slot_addr(j, BL::q), ka = slot_addr(j, BL::k);
                 for (int kk = 0; kk < 4; ++kk)
@@ -475,6 +476,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                     tc::mma_f16_ts(tmem + cNZ, tmem + cP + kk * 8, tc::sdesc_sw128(va + kk * 2048, lbo_v1, 1024),
                                    idNZ, 1u);
                 tc::mma_commit(&bars[B_NZFULL]);
+                // P of the next chunk now when its feature map is already done (the
+                // NZ MMAs above have taken their bf16 P), else after dQ~
+                const int jn = j + 1;
+                const bool p_early = i + 1 < n && tc::mbar_test_wait(&bars[B_TDONE + jn % kStages], (jn / kStages) & 1);
+                if (p_early) issue_p(i + 1, true);
                 // dA = [o^ | c] [V | 1]^T ; dS^ sum += q^^T [o^ | c]
                 ok = wait_bar(&bars[B_OCDONE], i & 1, P.status);
                 if (!ok) break;
@@ -487,22 +493,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                                 tc::sdesc_sw128(sbase + BL::ones, 16, 1024), idPP, 1u);
                 tc::mma_commit(&bars[B_DAFULL]);
                 mma_xt(tmem + cDS, qa, sbase + BL::ob, sbase + BL::ca, i == 0);
-                // dQ~ = bf16(dA) K^ + [o^ | c] [S_c | z_c]^T   (into the NZ / dQ columns)
+                // dQ~ = [o^ | c] [S_c | z_c]^T (issued while the compute warps mask dA)
+                //     + bf16(dA) K^                (into the NZ / dQ columns)
+                for (int kk = 0; kk < 4; ++kk)
+                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ob + kk * 32, 16, 1024),
+                                tc::sdesc_sw128(sba + kk * 32, 16, 1024), idKK64, kk > 0);
+                if (kNorm)
+                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ca, 16, 1024),
+                                tc::sdesc_sw128(sba + kD * kD * 2, 16, 1024), idKK64, 1u);
                 ok = wait_bar(&bars[B_DADONE], i & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
                 for (int kk = 0; kk < 8; ++kk)
                     tc::mma_f16_ts(tmem + cNZ, tmem + cDA + kk * 8, tc::sdesc_sw128(ka + kk * 2048, kTile, 1024),
-                                   idKM64, kk > 0);
-                for (int kk = 0; kk < 4; ++kk)
-                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ob + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(sba + kk * 32, 16, 1024), idKK64, 1u);
-                if (kNorm)
-                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ca, 16, 1024),
-                                tc::sdesc_sw128(sba + kD * kD * 2, 16, 1024), idKK64, 1u);
+                                   idKM64, 1u);
                 tc::mma_commit(&bars[B_DQFULL]);
-                // P of the next chunk (its feature map has had this whole chunk to finish)
-                if (i + 1 < n) ok = issue_p(i + 1);
+                // P of the next chunk, if not issued above
+                if (i + 1 < n && !p_early) ok = issue_p(i + 1);
             }
         }
         __syncwarp();
@@ -643,26 +650,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 tc::tc_fence_after();
                 mma_xt(tmem + cDS, qa, sbase + BL::ob, sbase + BL::ca, false);
                 tc::mma_commit(&bars[B_DSFULL]);
-                // dK~ = bf16(dA^T) q^ + [V | 1] [dS^ | dz^]^T ;  dV = bf16(P^T) o^ + K^ dS^
-                ok = wait_bar(&bars[B_CPDONE], i & 1, P.status);
-                if (ok && i >= 1) ok = wait_bar(&bars[B_KVDONE], (i - 1) & 1, P.status);
+                // dK~ = [V | 1] [dS^ | dz^]^T + bf16(dA^T) q^ ;  dV = K^ dS^ + bf16(P^T) o^.
+                // The state terms go first, while the compute warps mask P^T and dA^T.
+                if (i >= 1) ok = wait_bar(&bars[B_KVDONE], (i - 1) & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
-                for (int kk = 0; kk < 8; ++kk) {
-                    tc::mma_f16_ts(tmem + cDK, tmem + cDAT + kk * 8, tc::sdesc_sw128(qa + kk * 2048, kTile, 1024),
-                                   idKM64, kk > 0);
-                    tc::mma_f16_ts(tmem + cDV, tmem + cPT + kk * 8,
-                                   tc::sdesc_sw128(sbase + BL::ob + kk * 2048, kTile, 1024), idKM64, kk > 0);
-                }
                 for (int kk = 0; kk < 4; ++kk) {
                     tc::mma_f16(tmem + cDK, tc::sdesc_sw128(va + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(dsa + kk * 32, 16, 1024), idKK64, 1u);
+                                tc::sdesc_sw128(dsa + kk * 32, 16, 1024), idKK64, kk > 0);
                     tc::mma_f16(tmem + cDV, tc::sdesc_sw128(ka + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(dsa + kk * 2048, kTile, 1024), idKM64, 1u);
+                                tc::sdesc_sw128(dsa + kk * 2048, kTile, 1024), idKM64, kk > 0);
                 }
                 if (kNorm)
                     tc::mma_f16(tmem + cDK, tc::sdesc_sw128(sbase + BL::ones, 16, 1024),
                                 tc::sdesc_sw128(dsa + kD * kD * 2, 16, 1024), idKK64, 1u);
+                ok = wait_bar(&bars[B_CPDONE], i & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                for (int kk = 0; kk < 8; ++kk) {
+                    tc::mma_f16_ts(tmem + cDK, tmem + cDAT + kk * 8, tc::sdesc_sw128(qa + kk * 2048, kTile, 1024),
+                                   idKM64, 1u);
+                    tc::mma_f16_ts(tmem + cDV, tmem + cPT + kk * 8,
+                                   tc::sdesc_sw128(sbase + BL::ob + kk * 2048, kTile, 1024), idKM64, 1u);
+                }
                 tc::mma_commit(&bars[B_KVFULL]);
             }
         }
