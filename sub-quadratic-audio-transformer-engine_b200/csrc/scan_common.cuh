@@ -33,6 +33,11 @@ struct ScanParams {
     float* S_out; float* z_out;
     float* dlg;                                    // [B,H,N] or null
     float* ws;                                     // float workspace
+    // [B*H] per-sequence flags: the tensor-core kernels with per-token decay set
+    // fallback[b*H + h] when a chunk of the sequence leaves their decay range;
+    // the exact kernels, given the array, then compute only the flagged
+    // sequences (null: every sequence).
+    int* fallback;
 };
 
 // phi(x) = ELU(x) + 1 and its derivative (reference python/subq_audio/autograd.py:15-28).

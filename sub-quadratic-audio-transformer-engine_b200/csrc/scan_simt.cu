@@ -27,6 +27,7 @@ constexpr int kCT = 32;  // tokens staged in shared memory per step
 template <typename T, typename A, int RPT>
 __global__ void __launch_bounds__(288) scan_fwd_exact_kernel(ScanParams p, int ET) {
     const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    if (p.fallback && !p.fallback[b * p.H + h]) return;  // only the sequences flagged for this path
     const int d = p.d;
     const int j0 = tile * ET;
     const int ncols = min(ET, p.e - j0);
@@ -166,6 +167,7 @@ __device__ __forceinline__ A block_sum(A v, A* red) {
 template <typename T, typename A>
 __global__ void __launch_bounds__(256) scan_bwd_exact_kernel(ScanParams p) {
     const int h = blockIdx.x, b = blockIdx.y;
+    if (p.fallback && !p.fallback[b * p.H + h]) return;  // only the sequences flagged for this path
     const int d = p.d, e = p.e;
     const int ep = e + (p.normalize ? 1 : 0);
     const int LD = ep | 1;

@@ -114,7 +114,10 @@ bool tc_supported(const ScanParams& p, int dtype) {
     using namespace tcs;
     if (dtype != SUBQ_BF16 && dtype != SUBQ_FP16) return false;
     if (p.d != kD || p.e != kD || p.N < 1) return false;
-    if (p.decay_mode != SUBQ_DECAY_NONE || p.flush) return false;
+    if (p.flush) return false;
+    // per-token decay runs factorised through the chunk midpoint, which needs
+    // bf16's exponent range (fp16 decayed scans take the exact path)
+    if (p.decay_mode != SUBQ_DECAY_NONE && dtype != SUBQ_BF16) return false;
     if (!(p.scale > 0.f)) return false;  // phi'(q) is recovered from scale * phi(q)
     if (p.B * p.H > 65535) return false;
     return strides_ok(p.q_sb, p.q_sh, p.q_sn, p.q) && strides_ok(p.k_sb, p.k_sh, p.k_sn, p.k) &&
@@ -123,11 +126,17 @@ bool tc_supported(const ScanParams& p, int dtype) {
 
 bool tc_bwd_supported(const ScanParams& p, int) {
     using namespace tcs;
+    if (p.decay_mode != SUBQ_DECAY_NONE) return false;
     return p.dlg == nullptr && strides_ok(p.g_sb, p.g_sh, p.g_sn, p.g) &&
            strides_ok(p.dk_sb, p.dk_sh, p.dk_sn, p.dk) && strides_ok(p.dv_sb, p.dv_sh, p.dv_sn, p.dv);
 }
 
-size_t tc_fwd_workspace_bytes(const ScanParams&) { return 0; }
+static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// With decay: the per-sequence fallback flags.
+size_t tc_fwd_workspace_bytes(const ScanParams& p) {
+    return p.decay_mode == SUBQ_DECAY_NONE ? 0 : align256((size_t)p.B * p.H * sizeof(int));
+}
 
 // (Zc_t, c_t) per token, written by the backward's dQ pass and read by its dK/dV pass.
 size_t tc_bwd_workspace_bytes(const ScanParams& p) {
@@ -136,7 +145,16 @@ size_t tc_bwd_workspace_bytes(const ScanParams& p) {
 
 cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches) {
     *launches = 1;
-    return tcs::launch_fwd_v2(p, dtype, st);
+    if (p.decay_mode == SUBQ_DECAY_NONE) return tcs::launch_fwd_v2(p, dtype, st);
+    // decayed: the tensor-core kernel flags the sequences whose decay leaves its
+    // range; the exact kernel then recomputes exactly those
+    ScanParams q = p;
+    q.fallback = reinterpret_cast<int*>(p.ws);
+    cudaError_t err = cudaMemsetAsync(q.fallback, 0, (size_t)p.B * p.H * sizeof(int), st);
+    if (err == cudaSuccess) err = tcs::launch_fwd_v2(q, dtype, st);
+    if (err == cudaSuccess) err = launch_fwd_exact(q, dtype, st);
+    *launches = 2;
+    return err;
 }
 
 cudaError_t launch_bwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches) {

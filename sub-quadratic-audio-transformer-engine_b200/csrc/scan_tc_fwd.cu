@@ -60,7 +60,13 @@ struct L {
     static constexpr uint32_t xz = os + kTile;         // their normaliser parts [2][64] fp32
     static constexpr uint32_t bars = xz + 512;
     static constexpr uint32_t tslot = bars + 8 * 24;
-    static constexpr uint32_t total = tslot + 16;
+    // per-token decay: B_63, B_127 (log2 decay prefix at the chunk midpoint and
+    // end) of each stage's chunk, the feature-map group's scan totals, and the
+    // log2 decay totals of the two partial segment sums (read over DSMEM)
+    static constexpr uint32_t dec = tslot + 16;
+    static constexpr uint32_t wt = dec + 8 * kStages;
+    static constexpr uint32_t lam = wt + 16;
+    static constexpr uint32_t total = lam + 8;
 };
 static_assert(kD * kD * 4 <= kTile, "exchange fits the staging tile");
 static_assert(L::stage % 1024 == 0 && L::ones % 1024 == 0 && L::sb % 1024 == 0 && L::os % 1024 == 0,
@@ -77,7 +83,9 @@ enum {
     B_ODONE = B_OFULL + 2,         // [2] compute -> MMA (O' consumed)
     B_SFULL = B_ODONE + 2,         // MMA -> compute (state updated)
     B_SBDONE = B_SFULL + 1,        // compute -> MMA (state read, bf16 copy written)
-    B_COUNT = B_SBDONE + 1
+    B_UFULL = B_SBDONE + 1,        // [2] decay, phase 1: MMA -> compute (chunk sum ready)
+    B_UDONE = B_UFULL + 2,         // [2] decay, phase 1: compute -> MMA (chunk sum read)
+    B_COUNT = B_UDONE + 2
 };
 static_assert(B_COUNT <= 24, "barrier slots");
 
@@ -94,7 +102,7 @@ struct FwdParams {
     int* status;
 };
 
-template <bool kFp16, bool kNorm>
+template <bool kFp16, bool kNorm, bool kDecay>
 __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdParams P) {
     const ScanParams& p = P.p;
     extern __shared__ uint8_t smem_raw[];
@@ -112,10 +120,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     float* Xs1 = reinterpret_cast<float*>(sm + L::os);  // [64][64] partial sums phi~(K)^T V
     float* Xs2 = reinterpret_cast<float*>(sm + L::sb);
     float* Xz = reinterpret_cast<float*>(sm + L::xz);   // [2][64] partial sums phi~(K)^T 1
+    float* dec = reinterpret_cast<float*>(sm + L::dec);
+    float* Lam = reinterpret_cast<float*>(sm + L::lam);
     const uint32_t sbase = tc::smem_u32(sm);
 
     if (tid == 0) {
-        for (int i = 0; i < B_COUNT; ++i) tc::mbar_init(&bars[i], 1);
+        // with decay a stage is released by the tensor core (its operands read)
+        // and by the compute warps (its decay scalars read)
+        for (int i = 0; i < B_COUNT; ++i)
+            tc::mbar_init(&bars[i], (kDecay && i >= B_EMPTY && i < B_EMPTY + kStages) ? 2 : 1);
         tc::fence_mbar_init();
     }
     if (warp == kWarpMma) tc::tmem_alloc(tslot, kTmemCols);
@@ -164,7 +177,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     // order rotated per sequence, so that the clusters do not all read the
     // same offset of their sequences at the same time (the sums do not depend
     // on the order); phase-2 slots run the segment in order.
-    const int rot = n1 > 0 ? (bh * 7) % n1 : 0;
+    const int rot = (!kDecay && n1 > 0) ? (bh * 7) % n1 : 0;  // decayed sums run in order
     auto chunk_of = [&](int j) {
         if (j >= n1) return c_begin + (j - n1);
         const int r = j + rot;
@@ -190,16 +203,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     auto transform = [&](int jlo, int jhi) {
         const int r = tid - 256;
         float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
+        float a_next = (kDecay && jlo < jhi) ? decay_log2_at(p, b, h, chunk_of(jlo) * kC + r, m_next) : 0.f;
         for (int j = jlo; j < jhi && ok; ++j) {
             const bool ph2 = j >= n1;
             const int s = j % kStages, u = j / kStages;
-            const float m = m_next;
-            if (j + 1 < jhi) m_next = row_mask_at(chunk_of(j + 1), r);  // in flight during the wait
+            const float m = m_next, a = a_next;
+            if (j + 1 < jhi) {  // in flight during the wait
+                m_next = row_mask_at(chunk_of(j + 1), r);
+                if (kDecay) a_next = decay_log2_at(p, b, h, chunk_of(j + 1) * kC + r, m_next);
+            }
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
             uint8_t* base = sm + s * L::stage;
-            if (ph2) chunks_phi<kFp16>(base + L::q, r, 0, 8, true);  // scale is applied in the epilogue
-            chunks_phi<kFp16>(base + L::k, r, 0, 8, m != 0.f);
+            if constexpr (kDecay) {
+                float b63, b127;
+                const float br = decay_scan128(a, r, reinterpret_cast<float*>(sm + L::wt), kBarTransform, b63, b127);
+                if (r == 0) {
+                    dec[2 * s] = b63;
+                    dec[2 * s + 1] = b127;
+                    if (!decay_in_range(b63, b127)) p.fallback[bh] = 1;
+                }
+                if (ph2) chunks_phi_scaled<kFp16>(base + L::q, r, true, exp2_fast(br - b63));
+                chunks_phi_scaled<kFp16>(base + L::k, r, m != 0.f, exp2_fast(b63 - br));
+            } else {
+                if (ph2) chunks_phi<kFp16>(base + L::q, r, 0, 8, true);  // scale is applied in the epilogue
+                chunks_phi<kFp16>(base + L::k, r, 0, 8, m != 0.f);
+            }
             tc::fence_proxy_async();
             tc::bar_sync(kBarTransform, kTransformThreads);
             if (r == 0) tc::mbar_arrive(&bars[B_TDONE + s]);
@@ -219,7 +248,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     } else if (warp >= 8 && warp < 12) {
         transform(0, n1);
     } else if (warp == kWarpMma) {
-        if (lane == 0) {
+        if (kDecay && lane == 0) {
+            // decayed sums: each chunk's phi~(K')^T [V | 1] into one of two
+            // buffers in the O' columns; the compute warps chain them
+            for (int j = 0; j < n1 && ok; ++j) {
+                const int s = j % kStages, u = j / kStages;
+                ok = wait_bar(&bars[B_TDONE + s], u & 1, P.status);
+                if (ok && j >= 2) ok = wait_bar(&bars[B_UDONE + (j & 1)], ((j >> 1) - 1) & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                mma_state(s, true, cO + (j & 1) * kNX);
+                tc::mma_commit(&bars[B_EMPTY + s]);
+                tc::mma_commit(&bars[B_UFULL + (j & 1)]);
+            }
+        } else if (lane == 0) {
             // the share's two partial sums accumulate in S' (before the segment
             // boundary) and in the still unused P columns (after it)
             bool first1 = true, first2 = true;
@@ -242,7 +284,59 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         __syncwarp();
     }
     uint32_t sfull_count = 0;
-    if (warp < 8) {
+    if (kDecay && warp < 8) {
+        // Horner over the share in chunk order: X = exp(b_end) X + exp(b_end - b_m) U'
+        // per piece, and the piece's log2 decay total
+        const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
+        const uint32_t loff = (uint32_t)(quad * 32) << 16;
+        float X[32], xz = 0.f, lam0 = 0.f, lam1 = 0.f;
+#pragma unroll
+        for (int x = 0; x < 32; ++x) X[x] = 0.f;
+        int piece = 0;
+        auto flush = [&](int pc) {
+            float* dst = pc == 0 ? Xs1 : Xs2;
+            if (lane < 16) {
+#pragma unroll
+                for (int x = 0; x < 32; ++x) dst[srow * 64 + hf * 32 + x] = X[x];
+                if (hf == 0) Xz[pc * 64 + srow] = xz;
+            }
+        };
+        for (int j = 0; j < n1 && ok; ++j) {
+            const int s = j % kStages;
+            if (piece == 0 && chunk_of(j) >= share.x) {
+                if (j > 0) flush(0);
+#pragma unroll
+                for (int x = 0; x < 32; ++x) X[x] = 0.f;
+                xz = 0.f;
+                piece = 1;
+            }
+            ok = tc::bar_and(kBarCompute, kComputeThreads,
+                             wait_bar(&bars[B_UFULL + (j & 1)], (j >> 1) & 1, P.status) &&
+                                 wait_bar(&bars[B_TDONE + s], (j / kStages) & 1, P.status)) && ok;
+            if (!ok) break;
+            tc::tc_fence_after();
+            const float b63 = dec[2 * s], b127 = dec[2 * s + 1];
+            const float ld = exp2_fast(b127), mu = exp2_fast(b127 - b63);
+            float uu[32];
+            tc::tmem_ld32(tmem + cO + (j & 1) * kNX + loff + hf * 32, uu);
+#pragma unroll
+            for (int x = 0; x < 32; ++x) X[x] = fmaf(ld, X[x], mu * uu[x]);
+            if (kNorm && hf == 0) xz = fmaf(ld, xz, mu * tmem_ld1(tmem + cO + (j & 1) * kNX + loff + 64));
+            if (piece) lam1 += b127;
+            else lam0 += b127;
+            tc::tc_fence_before();
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) {
+                tc::mbar_arrive(&bars[B_UDONE + (j & 1)]);
+                tc::mbar_arrive(&bars[B_EMPTY + s]);
+            }
+        }
+        if (n1 > 0) flush(piece);
+        if (tid == 0) {
+            Lam[0] = lam0;
+            Lam[1] = lam1;
+        }
+    } else if (warp < 8) {
         const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
         const uint32_t loff = (uint32_t)(quad * 32) << 16;
         if (n1 > 0) {
@@ -299,9 +393,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                                                  : (sr.b > sr.x && sr.seg + 1 < g);
                     if (!used) continue;
                     const float* rx = cluster.map_shared_rank(piece == 0 ? Xs1 : Xs2, r) + srow * 64 + hf * 32;
+                    // decayed: the state so far decays over the piece, then takes its sum
+                    const float f = kDecay ? exp2_fast(cluster.map_shared_rank(Lam, r)[piece]) : 1.f;
 #pragma unroll
-                    for (int x = 0; x < 32; ++x) v[x] += rx[x];
-                    if (kNorm && hf == 0) z += cluster.map_shared_rank(Xz, r)[piece * 64 + srow];
+                    for (int x = 0; x < 32; ++x) v[x] = fmaf(f, v[x], rx[x]);
+                    if (kNorm && hf == 0) z = fmaf(f, z, cluster.map_shared_rank(Xz, r)[piece * 64 + srow]);
                 }
             }
         }
@@ -312,24 +408,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     if (warp < 8) {
         const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
         const uint32_t loff = (uint32_t)(quad * 32) << 16;
-        if (lane < 16) {
+        // (with decay the state stays in these registers and the first chunk's
+        // operand is written at the start of phase 2, scaled by its exp(b_m))
+        if (!kDecay && lane < 16) {
 #pragma unroll
             for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + L::sb, srow, hf * 4 + x, v + 8 * x);
         }
-        tc::tmem_st32(tmem + cS + loff + hf * 32, v);
+        if (!kDecay) tc::tmem_st32(tmem + cS + loff + hf * 32, v);
         if (hf == 0) {
             if (lane < 16) {
                 float zc8[8] = {z, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                store_chunk<kFp16>(sm + L::sb + kD * kD * 2, srow, 0, zc8);
+                if (!kDecay) store_chunk<kFp16>(sm + L::sb + kD * kD * 2, srow, 0, zc8);
                 // columns 1-15 of the z atom are read as zeros (N = 80) in both buffers
                 zero_chunks(sm + L::sb + kD * kD * 2, srow, 1, 1);
                 zero_chunks(sm + L::sb + L::sbuf + kD * kD * 2, srow, 1, 1);
             }
-            float w[32];
+            if (!kDecay) {
+                float w[32];
 #pragma unroll
-            for (int x = 0; x < 32; ++x) w[x] = 0.f;
-            w[0] = (lane < 16) ? z : 0.f;
-            tc::tmem_st32(tmem + cS + loff + 64, w);
+                for (int x = 0; x < 32; ++x) w[x] = 0.f;
+                w[0] = (lane < 16) ? z : 0.f;
+                tc::tmem_st32(tmem + cS + loff + 64, w);
+            }
         }
         tc::fence_proxy_async();
     }
@@ -366,7 +466,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 if (i >= 1) ok = wait_bar(&bars[B_SBDONE], (i - 1) & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
-                mma_state(s, false);
+                mma_state(s, kDecay);  // with decay: this chunk's sum alone, chained in registers
                 tc::mma_commit(&bars[B_SFULL]);
                 if (i + 1 < n) ok = issue_p(i + 1);
                 if (ok) ok = wait_bar(&bars[B_PSDONE + bf], pu & 1, P.status);
@@ -406,6 +506,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             if (hf == 1 && quad < 2) {
 #pragma unroll
                 for (int x = 0; x < 32; ++x) packed[x] = 0u;
+            } else if (kDecay) {  // 32 columns at a time: the decayed state occupies 33 registers
+                const bool diag = (hf == (quad >> 1));
+#pragma unroll
+                for (int part = 0; part < 2; ++part) {
+                    float v[32];
+                    tc::tmem_ld32(tmem + cP + bf * 128 + loff + hf * 64 + part * 32, v);
+#pragma unroll
+                    for (int x = 0; x < 32; ++x)
+                        if (diag && (hf * 64 + part * 32 + x) > row) v[x] = 0.f;
+#pragma unroll
+                    for (int x = 0; x < 16; ++x) {
+                        typename E::T2 h2 = E::from2(v[2 * x], v[2 * x + 1]);
+                        packed[part * 16 + x] = *reinterpret_cast<uint32_t*>(&h2);
+                    }
+                }
             } else {
                 const bool diag = (hf == (quad >> 1));
                 float v[64];
@@ -429,7 +544,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             if (tid == 0) tc::mbar_arrive(&bars[B_PSDONE + bf]);
             return true;
         };
-        if (n > 0) ok = mask_p(0);
+        // decay: bf16 f [S | z] (registers v, z) into the operand buffer `dst`
+        auto write_operand = [&](uint8_t* dst, float f) {
+            if (lane < 16) {
+                float w[8];
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+#pragma unroll
+                    for (int y = 0; y < 8; ++y) w[y] = f * v[8 * x + y];
+                    store_chunk<kFp16>(dst, srow, hf * 4 + x, w);
+                }
+                if (kNorm && hf == 0) {
+                    float zc8[8] = {f * z, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                    store_chunk<kFp16>(dst + kD * kD * 2, srow, 0, zc8);
+                }
+            }
+        };
+        if (kDecay && n > 0) {  // the first chunk's operand exp(b_m) [S | z]_in
+            const int s0 = n1 % kStages;
+            ok = tc::bar_and(kBarCompute, kComputeThreads,
+                             wait_bar(&bars[B_TDONE + s0], (n1 / kStages) & 1, P.status)) && ok;
+            if (ok) write_operand(sm + L::sb, exp2_fast(dec[2 * s0]));
+            tc::fence_proxy_async();
+        }
+        if (n > 0 && ok) ok = mask_p(0);
         for (int i = 0; i < n && ok; ++i) {
             const int c = c_begin + i, bf = i & 1, pu = i >> 1;
             // state refresh: bf16 [S | z]_c+1 into sb[(i + 1) % 2], the next chunk's operand
@@ -438,6 +576,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             ++sfull_count;
             if (!ok) break;
             tc::tc_fence_after();
+            if constexpr (kDecay) {
+                // [S|z]_c+1 = exp(b_end) [S|z]_c + exp(b_end - b_m) U'_c in registers; the
+                // operand of chunk c+1 carries its own exp(b_m). The decay scalars of
+                // both chunks are final once their feature maps are (TDONE), and their
+                // stages stay until this warp group releases them.
+                const int j = n1 + i, s = j % kStages, s1 = (j + 1) % kStages;
+                ok = tc::bar_and(kBarCompute, kComputeThreads,
+                                 wait_bar(&bars[B_TDONE + s], (j / kStages) & 1, P.status) &&
+                                     (i + 1 >= n ||
+                                      wait_bar(&bars[B_TDONE + s1], ((j + 1) / kStages) & 1, P.status))) && ok;
+                if (!ok) break;
+                const float b63 = dec[2 * s], b127 = dec[2 * s + 1];
+                const float ld = exp2_fast(b127), mu = exp2_fast(b127 - b63);
+                float uu[32];
+                tc::tmem_ld32(tmem + cS + loff + hf * 32, uu);
+#pragma unroll
+                for (int x = 0; x < 32; ++x) v[x] = fmaf(ld, v[x], mu * uu[x]);
+                if (kNorm && hf == 0) z = fmaf(ld, z, mu * tmem_ld1(tmem + cS + loff + 64));
+                if (i + 1 < n) write_operand(sm + L::sb + ((i + 1) & 1) * L::sbuf, exp2_fast(dec[2 * s1]));
+                tc::fence_proxy_async();
+                tc::tc_fence_before();
+                tc::bar_sync(kBarCompute, kComputeThreads);
+                if (tid == 0) {
+                    tc::mbar_arrive(&bars[B_SBDONE]);
+                    tc::mbar_arrive(&bars[B_EMPTY + s]);
+                }
+            } else {
             {
                 uint8_t* sbn = sm + L::sb + ((i + 1) & 1) * L::sbuf;
                 float v[32];
@@ -458,6 +623,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             tc::tc_fence_before();
             tc::bar_sync(kBarCompute, kComputeThreads);
             if (tid == 0) tc::mbar_arrive(&bars[B_SBDONE]);
+            }
             if (i + 1 < n) {
                 ok = mask_p(i + 1);
                 if (!ok) break;
@@ -492,15 +658,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             }
         }
         if (g == P.G - 1 && ok) {  // final state of the whole sequence
-            float v[32];
-            tc::tmem_ld32(tmem + cS + loff + hf * 32, v);
+            float fs[32];
+            if (kDecay) {
+#pragma unroll
+                for (int x = 0; x < 32; ++x) fs[x] = v[x];
+            } else {
+                tc::tmem_ld32(tmem + cS + loff + hf * 32, fs);
+            }
             if (lane < 16 && p.S_out) {
                 float* dst = p.S_out + ((int64_t)bh * kD + srow) * kD + hf * 32;
 #pragma unroll
-                for (int x = 0; x < 32; ++x) dst[x] = v[x];
+                for (int x = 0; x < 32; ++x) dst[x] = fs[x];
             }
             if (p.z_out && hf == 0) {
-                const float zv = kNorm ? tmem_ld1(tmem + cS + loff + 64) : 0.f;
+                const float zv = !kNorm ? 0.f : kDecay ? z : tmem_ld1(tmem + cS + loff + 64);
                 if (lane < 16) p.z_out[(int64_t)bh * kD + srow] = zv;
             }
         }
@@ -524,7 +695,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     if (warp == kWarpMma) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
-template <bool kFp16, bool kNorm>
+template <bool kFp16, bool kNorm, bool kDecay>
 cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     FwdParams P;
     memset(&P, 0, sizeof(P));
@@ -540,7 +711,7 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     if (!P.status) return cudaErrorInvalidDevice;
     P.G = pick_segments(p);
     P.cps = (nC + P.G - 1) / P.G;
-    const void* kern = reinterpret_cast<const void*>(&fwd_kernel<kFp16, kNorm>);
+    const void* kern = reinterpret_cast<const void*>(&fwd_kernel<kFp16, kNorm, kDecay>);
     void* args[] = {&P};
     return launch_cluster(kern, P.G, p.B * p.H, kFwdThreads, L::total + 1024, st, args);
 }
@@ -548,8 +719,12 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_fwd_v2(const ScanParams& p, int dtype, cudaStream_t st) {
-    if (dtype == SUBQ_FP16) return p.normalize ? launch<true, true>(p, st) : launch<true, false>(p, st);
-    return p.normalize ? launch<false, true>(p, st) : launch<false, false>(p, st);
+    if (p.decay_mode != SUBQ_DECAY_NONE) {  // bf16 only (the factorised decay needs its exponent range)
+        if (dtype != SUBQ_BF16 || !p.fallback) return cudaErrorInvalidValue;
+        return p.normalize ? launch<false, true, true>(p, st) : launch<false, false, true>(p, st);
+    }
+    if (dtype == SUBQ_FP16) return p.normalize ? launch<true, true, false>(p, st) : launch<true, false, false>(p, st);
+    return p.normalize ? launch<false, true, false>(p, st) : launch<false, false, false>(p, st);
 }
 
 }  // namespace tcs

@@ -206,6 +206,93 @@ __device__ __forceinline__ void chunks_phi(uint8_t* tile, int r, int j0, int nj,
     for (int jj = 0; jj < nj; ++jj) *reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, j0 + jj)) = raw[jj];
 }
 
+// ------------------------------------------------------------ per-token decay
+// Within a 128-token chunk with inclusive log-decay prefix b_t (b_t = sum of
+// log gamma over tokens 0..t of the chunk; masked tokens and tokens past the
+// end carry log gamma = 0, reference python/subq_audio/autograd.py:336-341 and
+// :130-134), the decay between key tau and query t >= tau is exp(b_t - b_tau).
+// The kernels factor it through the chunk midpoint m = 63:
+//   q' = phi(q) exp(b_t - b_m),   k' = m phi(k) exp(b_m - b_tau),
+// so q' k'^T = (phi(q) phi(k)^T) exp(b_t - b_tau) exactly and the causal mask,
+// the tensor-core products and the epilogues keep their form; the inter-chunk
+// terms take the scalars exp(b_m) (query side) and exp(b_end - b_m) (state
+// side). Both factors stay within 2^kDecaySpan when each half of the chunk
+// decays by at most 2^-kDecaySpan; a chunk outside that range marks its
+// sequence for the exact path (the `fallback` flags), which then recomputes
+// the whole sequence.
+constexpr float kDecaySpan = 80.f;  // log2 units per half chunk
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float exp2_fast(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// log2 decay of token t (0 when masked or past the end).
+__device__ __forceinline__ float decay_log2_at(const ScanParams& p, int b, int h, int t, float m) {
+    if (t >= p.N || m == 0.f) return 0.f;
+    return token_log_gamma(p, b, h, t) * kLog2e;
+}
+
+// Inclusive scan of the chunk's log2 decay over the 128 threads of a 4-warp
+// group (thread r holds token r's value a). Returns B_r; b63 and b127 receive
+// B_63 and B_127, summed in the same order as the row values so that row 63
+// and row 127 reproduce them exactly. `wt` is 4 floats of shared memory; the
+// caller separates successive calls with a barrier of the same group.
+__device__ __forceinline__ float decay_scan128(float a, int r, float* wt, int bar_id, float& b63, float& b127) {
+    const int lane = r & 31, w = r >> 5;
+    float x = a;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wt[w] = x;
+    tc::bar_sync(bar_id, 128);
+    const float w0 = wt[0], w1 = wt[1], w2 = wt[2];
+    const float p01 = w0 + w1, p012 = p01 + w2;
+    b63 = p01;
+    b127 = p012 + wt[3];
+    const float pre = w == 0 ? 0.f : w == 1 ? w0 : w == 2 ? p01 : p012;
+    return w == 0 ? x : x + pre;
+}
+
+// Whether both halves of a chunk stay within the factorisation's range (NaN
+// decay passes and propagates like the reference's).
+__device__ __forceinline__ bool decay_in_range(float b63, float b127) {
+    return !(fabsf(b63) > kDecaySpan) && !(fabsf(b127 - b63) > kDecaySpan);
+}
+
+// Row r of a 128-byte swizzled tile, in place: f * phi of every element (live)
+// or zeros (a masked token); f is applied in float32 to the feature map's
+// 16-bit result.
+template <bool kFp16>
+__device__ __forceinline__ void chunks_phi_scaled(uint8_t* tile, int r, bool live, float f) {
+    using E = Elem<kFp16>;
+    uint4 raw[8];
+    if (live) {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) raw[jj] = *reinterpret_cast<const uint4*>(tile + tc::sw128_chunk(r, jj));
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+            uint32_t* w = reinterpret_cast<uint32_t*>(&raw[jj]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint32_t ph = phi2<kFp16>(w[i]);
+                const float2 v = E::to2(*reinterpret_cast<typename E::T2*>(&ph));
+                typename E::T2 o = E::from2(v.x * f, v.y * f);
+                w[i] = *reinterpret_cast<uint32_t*>(&o);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) raw[jj] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) *reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, jj)) = raw[jj];
+}
+
 template <bool kFp16>
 __device__ __forceinline__ void store_chunk(uint8_t* tile, int r, int j, const float* v) {
     using E = Elem<kFp16>;
