@@ -126,8 +126,9 @@ bool tc_supported(const ScanParams& p, int dtype) {
 
 bool tc_bwd_supported(const ScanParams& p, int) {
     using namespace tcs;
-    if (p.decay_mode != SUBQ_DECAY_NONE) return false;
-    return p.dlg == nullptr && strides_ok(p.g_sb, p.g_sh, p.g_sn, p.g) &&
+    // d log(gamma) comes with the decayed kernels only (without decay it is not defined)
+    if (p.dlg != nullptr && p.decay_mode == SUBQ_DECAY_NONE) return false;
+    return strides_ok(p.g_sb, p.g_sh, p.g_sn, p.g) &&
            strides_ok(p.dk_sb, p.dk_sh, p.dk_sn, p.dk) && strides_ok(p.dv_sb, p.dv_sh, p.dv_sn, p.dv);
 }
 
@@ -138,9 +139,18 @@ size_t tc_fwd_workspace_bytes(const ScanParams& p) {
     return p.decay_mode == SUBQ_DECAY_NONE ? 0 : align256((size_t)p.B * p.H * sizeof(int));
 }
 
-// (Zc_t, c_t) per token, written by the backward's dQ pass and read by its dK/dV pass.
+// (Zc_t, c_t) per token, written by the backward's dQ pass and read by its dK/dV pass;
+// with decay also s q~ . dQ~ per token (12 bytes per token, which also holds the
+// exact kernel's three floats per token of a sequence it takes over), then the
+// per-sequence fallback flags.
+static size_t tc_bwd_token_bytes(const ScanParams& p) {
+    const size_t per = p.decay_mode == SUBQ_DECAY_NONE ? sizeof(float2) : 3 * sizeof(float);
+    return align256((size_t)p.B * p.H * (size_t)p.N * per);
+}
+
 size_t tc_bwd_workspace_bytes(const ScanParams& p) {
-    return ((size_t)p.B * p.H * (size_t)p.N * sizeof(float2) + 255) / 256 * 256;
+    const size_t flags = p.decay_mode == SUBQ_DECAY_NONE ? 0 : align256((size_t)p.B * p.H * sizeof(int));
+    return tc_bwd_token_bytes(p) + flags;
 }
 
 cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches) {
@@ -159,7 +169,14 @@ cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* 
 
 cudaError_t launch_bwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches) {
     *launches = 1;
-    return tcs::launch_bwd_v2(p, dtype, st);
+    if (p.decay_mode == SUBQ_DECAY_NONE) return tcs::launch_bwd_v2(p, dtype, st);
+    ScanParams q = p;
+    q.fallback = reinterpret_cast<int*>(reinterpret_cast<char*>(p.ws) + tc_bwd_token_bytes(p));
+    cudaError_t err = cudaMemsetAsync(q.fallback, 0, (size_t)p.B * p.H * sizeof(int), st);
+    if (err == cudaSuccess) err = tcs::launch_bwd_v2(q, dtype, st);
+    if (err == cudaSuccess) err = launch_bwd_exact(q, dtype, st);
+    *launches = 2;
+    return err;
 }
 
 cudaError_t tc_read_status(cudaStream_t st, int* status) {

@@ -61,7 +61,16 @@ struct BL {
     static constexpr uint32_t dx = xz + 512;           // [2][128] fp32 partial dot products
     static constexpr uint32_t bars = dx + 1024;
     static constexpr uint32_t tslot = bars + 8 * 32;
-    static constexpr uint32_t total = tslot + 16;
+    // per-token decay: per stage the chunk's log2 decay prefix B_t of every row
+    // and (B_63, B_127) at [128], [129]; the feature-map group's scan totals;
+    // misc: [0,2) the partial sums' log2 decay totals, [2] the segment's log2
+    // decay total, [3] its d log(gamma) total, [4,8) quad totals of the
+    // d log(gamma) suffix scan (all read over DSMEM where exchanged)
+    static constexpr uint32_t decs = 132 * 4;
+    static constexpr uint32_t dec = tslot + 16;
+    static constexpr uint32_t wt = dec + kStages * decs;
+    static constexpr uint32_t misc = wt + 16;
+    static constexpr uint32_t total = misc + 32;
 };
 static_assert(kD * kD * 4 <= kTile, "exchange fits the o^ tile");
 static_assert(BL::ones % 1024 == 0 && BL::ob % 1024 == 0 && BL::ca % 1024 == 0 && BL::sb % 1024 == 0,
@@ -77,7 +86,9 @@ enum {
     B_SFULL, B_SBDONE, B_PFULL, B_PSDONE, B_NZFULL, B_OCDONE, B_DAFULL, B_DADONE, B_DQFULL, B_DQDONE,
     // phase C
     B_COCDONE, B_CPFULL, B_CPDONE, B_DSFULL, B_DSBDONE, B_KVFULL, B_KVDONE,
-    B_COUNT
+    // decay, phase A: per-chunk sums, double-buffered
+    B_UFULL, B_UDONE = B_UFULL + 2,
+    B_COUNT = B_UDONE + 2
 };
 static_assert(B_COUNT <= 32, "barrier slots");
 
@@ -97,7 +108,7 @@ struct BwdParams {
     int* status;
 };
 
-template <bool kFp16, bool kNorm>
+template <bool kFp16, bool kNorm, bool kDecay>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams P) {
     const ScanParams& p = P.p;
     extern __shared__ uint8_t smem_raw[];
@@ -120,6 +131,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     float* dxs = reinterpret_cast<float*>(sm + BL::dx);
     const uint32_t sbase = tc::smem_u32(sm);
     float2* wsz = reinterpret_cast<float2*>(p.ws) + (int64_t)bh * p.N;
+    // decay: s q~ . dQ~ per token (the query part of d log(gamma)), after the (Zc, c) pairs
+    float* wgq = p.ws + 2 * (int64_t)p.B * p.H * p.N + (int64_t)bh * p.N;
+    float* dec = reinterpret_cast<float*>(sm + BL::dec);
+    float* misc = reinterpret_cast<float*>(sm + BL::misc);
+    const bool want_dlg = kDecay && p.dlg != nullptr;
 
     if (tid == 0) {
         for (int i = 0; i < B_COUNT; ++i) tc::mbar_init(&bars[i], 1);
@@ -168,7 +184,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
     };
     // chunk of pipeline slot j (phase A visits its share rotated per sequence)
-    const int rot = nA > 0 ? (bh * 7) % nA : 0;
+    const int rot = (!kDecay && nA > 0) ? (bh * 7) % nA : 0;  // decayed sums run in order
     auto chunk_of = [&](int j) {
         if (j < nA) {
             const int r = j + rot;
@@ -210,15 +226,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     auto transform = [&](int jlo, int jhi) {
         const int r = tid - 256;
         float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
+        float a_next = (kDecay && jlo < jhi) ? decay_log2_at(p, b, h, chunk_of(jlo) * kC + r, m_next) : 0.f;
         for (int j = jlo; j < jhi && ok; ++j) {
             const int s = j % kStages, u = j / kStages;
-            const float m = m_next;
-            if (j + 1 < jhi) m_next = row_mask_at(chunk_of(j + 1), r);
+            const float m = m_next, a = a_next;
+            if (j + 1 < jhi) {
+                m_next = row_mask_at(chunk_of(j + 1), r);
+                if (kDecay) a_next = decay_log2_at(p, b, h, chunk_of(j + 1) * kC + r, m_next);
+            }
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
             uint8_t* base = sm + s * BL::stage;
-            if (j >= nA) chunks_phi<kFp16>(base + BL::q, r, 0, 8, true);
-            chunks_phi<kFp16>(base + BL::k, r, 0, 8, m != 0.f);
+            if constexpr (kDecay) {
+                float b63, b127;
+                const float br = decay_scan128(a, r, reinterpret_cast<float*>(sm + BL::wt), kBarTransform, b63, b127);
+                float* dc = dec + s * (BL::decs / 4);
+                dc[r] = br;
+                if (r == 0) {
+                    dc[128] = b63;
+                    dc[129] = b127;
+                    if (!decay_in_range(b63, b127)) p.fallback[bh] = 1;
+                }
+                if (j >= nA) chunks_phi_scaled<kFp16>(base + BL::q, r, true, exp2_fast(br - b63));
+                chunks_phi_scaled<kFp16>(base + BL::k, r, m != 0.f, exp2_fast(b63 - br));
+            } else {
+                if (j >= nA) chunks_phi<kFp16>(base + BL::q, r, 0, 8, true);
+                chunks_phi<kFp16>(base + BL::k, r, 0, 8, m != 0.f);
+            }
             tc::fence_proxy_async();
             tc::bar_sync(kBarTransform, kTransformThreads);
             if (r == 0) tc::mbar_arrive(&bars[B_TDONE + s]);
@@ -240,6 +274,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         if (zero) {
 #pragma unroll
             for (int x = 0; x < 32; ++x) packed[x] = 0u;
+        } else if (kDecay) {  // 32 columns at a time: the decayed state occupies 33 registers
+            const bool diag = (hf == (quad >> 1));
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+                uint32_t r[32];
+                tc::tmem_ld32_issue(tmem + tcol + loff + hf * 64 + part * 32, r);
+                tc::tmem_wait_ld();
+                tc::tmem_regs_ready<32>(r);
+#pragma unroll
+                for (int x = 0; x < 16; ++x) {
+                    float a = __uint_as_float(r[2 * x]), bb = __uint_as_float(r[2 * x + 1]);
+                    if (diag) {
+                        const int col = hf * 64 + part * 32 + 2 * x;
+                        if (keep_upper ? (col < row) : (col > row)) a = 0.f;
+                        if (keep_upper ? (col + 1 < row) : (col + 1 > row)) bb = 0.f;
+                    }
+                    typename E::T2 h2 = E::from2(a, bb);
+                    packed[part * 16 + x] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+            }
         } else {
             const bool diag = (hf == (quad >> 1));
             uint32_t r[64];
@@ -331,9 +385,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                                                  : (sr.b > sr.x && sr.seg + 1 < g);
                     if (!used) continue;
                     const float* rx = cluster.map_shared_rank(piece == 0 ? Xs : Xs2, r) + srow * 64 + hf * 32;
+                    // decayed: the state so far decays over the piece, then takes its sum
+                    const float f = kDecay ? exp2_fast(cluster.map_shared_rank(misc, r)[piece]) : 1.f;
 #pragma unroll
-                    for (int x = 0; x < 32; ++x) v[x] += rx[x];
-                    if (kNorm && hf == 0) z += cluster.map_shared_rank(Xz, r)[piece * 64 + srow];
+                    for (int x = 0; x < 32; ++x) v[x] = fmaf(f, v[x], rx[x]);
+                    if (kNorm && hf == 0) z = fmaf(f, z, cluster.map_shared_rank(Xz, r)[piece * 64 + srow]);
                 }
             }
         }
@@ -382,6 +438,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         }
     };
 
+    // decay: bf16 f [X | x] from registers (rows in lanes 0-15) into the operand
+    // buffer `dst` (the z atom's columns 8-15 zeroed alongside)
+    auto write_operand = [&](uint8_t* dst, float f, const float* v, float z) {
+        if (lane < 16) {
+            float w[8];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+#pragma unroll
+                for (int y = 0; y < 8; ++y) w[y] = f * v[8 * x + y];
+                store_chunk<kFp16>(dst, srow, hf * 4 + x, w);
+            }
+            if (kNorm && hf == 0) {
+                float z8[8] = {f * z, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                store_chunk<kFp16>(dst + kD * kD * 2, srow, 0, z8);
+                zero_chunks(dst + kD * kD * 2, srow, 1, 1);
+            }
+        }
+    };
+    // decay: the adjoint at this segment's end, Horner over the later segments
+    // r = G-1 .. g+1: G = X_r + exp(Lambda_r) G (X_r at segment r's start)
+    auto gather_suffix_decayed = [&](float* v, float& z) {
+#pragma unroll
+        for (int x = 0; x < 32; ++x) v[x] = 0.f;
+        z = 0.f;
+        if (lane < 16) {
+            for (int r = P.G - 1; r > g; --r) {
+                const float f = exp2_fast(cluster.map_shared_rank(misc, r)[2]);
+                const float* rx = cluster.map_shared_rank(Xs, r) + srow * 64 + hf * 32;
+#pragma unroll
+                for (int x = 0; x < 32; ++x) v[x] = fmaf(f, v[x], rx[x]);
+                if (kNorm && hf == 0) z = fmaf(f, z, cluster.map_shared_rank(Xz, r)[srow]);
+            }
+        }
+    };
+
     // ============================================================ phase A
     if (warp == kWarpProducer) {
         if (lane == 0) {
@@ -394,7 +485,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     } else if (warp >= 8 && warp < 12) {
         transform(0, nA);
     } else if (warp == kWarpMma) {
-        if (lane == 0) {
+        if (kDecay && lane == 0) {
+            // decayed sums: each chunk's k'^T [V | 1] into one of two buffers (the
+            // NZ and S columns); the compute warps chain them and release the stage
+            for (int j = 0; j < nA && ok; ++j) {
+                const int s = j % kStages, u = j / kStages;
+                ok = wait_bar(&bars[B_TDONE + s], u & 1, P.status);
+                if (ok && j >= 2) ok = wait_bar(&bars[B_UDONE + (j & 1)], ((j >> 1) - 1) & 1, P.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                mma_xt(tmem + ((j & 1) ? cS : cNZ), slot_addr(j, BL::k), slot_addr(j, BL::v), sbase + BL::ones, true);
+                tc::mma_commit(&bars[B_UFULL + (j & 1)]);
+            }
+        } else if (lane == 0) {
             // the share's two partial sums accumulate in S (before the segment
             // boundary) and in the still unused P columns (after it)
             bool first1 = true, first2 = true;
@@ -412,6 +515,57 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             if (nA > 0 && ok) tc::mma_commit(&bars[B_AFULL]);
         }
         __syncwarp();
+    } else if (kDecay && warp < 8) {
+        // Horner over the share in chunk order, per piece: X = exp(b_end) X + exp(b_end - b_m) U'
+        float X[32], xz = 0.f, lam0 = 0.f, lam1 = 0.f;
+#pragma unroll
+        for (int x = 0; x < 32; ++x) X[x] = 0.f;
+        int piece = 0;
+        auto flush = [&](int pc) {
+            float* dst = pc == 0 ? Xs : Xs2;
+            if (lane < 16) {
+#pragma unroll
+                for (int x = 0; x < 32; ++x) dst[srow * 64 + hf * 32 + x] = X[x];
+                if (hf == 0) Xz[pc * 64 + srow] = xz;
+            }
+        };
+        for (int j = 0; j < nA && ok; ++j) {
+            const int s = j % kStages;
+            if (piece == 0 && chunk_of(j) >= share.x) {
+                if (j > 0) flush(0);
+#pragma unroll
+                for (int x = 0; x < 32; ++x) X[x] = 0.f;
+                xz = 0.f;
+                piece = 1;
+            }
+            ok = tc::bar_and(kBarCompute, kComputeThreads,
+                             wait_bar(&bars[B_UFULL + (j & 1)], (j >> 1) & 1, P.status) &&
+                                 wait_bar(&bars[B_TDONE + s], (j / kStages) & 1, P.status)) && ok;
+            if (!ok) break;
+            tc::tc_fence_after();
+            const float* dc = dec + s * (BL::decs / 4);
+            const float b63 = dc[128], b127 = dc[129];
+            const float ld = exp2_fast(b127), mu = exp2_fast(b127 - b63);
+            const uint32_t ucol = (j & 1) ? cS : cNZ;
+            float uu[32];
+            tc::tmem_ld32(tmem + ucol + loff + hf * 32, uu);
+#pragma unroll
+            for (int x = 0; x < 32; ++x) X[x] = fmaf(ld, X[x], mu * uu[x]);
+            if (kNorm && hf == 0) xz = fmaf(ld, xz, mu * tmem_ld1(tmem + ucol + loff + 64));
+            if (piece) lam1 += b127;
+            else lam0 += b127;
+            tc::tc_fence_before();
+            tc::bar_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) {
+                tc::mbar_arrive(&bars[B_UDONE + (j & 1)]);
+                tc::mbar_arrive(&bars[B_EMPTY + s]);
+            }
+        }
+        if (nA > 0) flush(piece);
+        if (tid == 0) {
+            misc[0] = lam0;
+            misc[1] = lam1;
+        }
     } else if (warp < 8) {
         if (nA > 0) cwait(&bars[B_AFULL], 0);
         publish_sums(cS, ok && min(share.b, share.x) > share.a, Xs, 0);
@@ -421,11 +575,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     cluster.sync();
     tc::tc_fence_after();
     float carry[32], carry_z = 0.f;  // prefix (phase B) / suffix (phase C) state rows, compute warps
+    float lf = 0.f;                  // decay: log2 decay total of the segment's chunks (phase B)
     if (warp < 8) gather_prefix(carry, carry_z);
     tc::tc_fence_before();
     cluster.sync();  // remote reads done before the exchange tile is reused
     tc::tc_fence_after();
-    if (warp < 8) {
+    if (warp < 8 && !kDecay) {  // (with decay the state stays in registers, lanes 0-15)
         install_state(cS, sm + BL::sb, carry, carry_z);
         tc::fence_proxy_async();
     }
@@ -462,7 +617,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 if (i >= 1) ok = wait_bar(&bars[B_SBDONE], (i - 1) & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
-                mma_xt(tmem + cS, ka, va, sbase + BL::ones, false);
+                mma_xt(tmem + cS, ka, va, sbase + BL::ones, kDecay);  // decay: this chunk's sum alone
                 tc::mma_commit(&bars[B_SFULL]);
                 // [N | Z] = q^ [S_c | z_c] + bf16(P) [V | 1]   (into the NZ / dQ columns)
                 ok = wait_bar(&bars[B_PSDONE], i & 1, P.status);
@@ -492,7 +647,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                     tc::mma_f16(tmem + cDA, tc::sdesc_sw128(sbase + BL::ca, 16, 1024),
                                 tc::sdesc_sw128(sbase + BL::ones, 16, 1024), idPP, 1u);
                 tc::mma_commit(&bars[B_DAFULL]);
-                mma_xt(tmem + cDS, qa, sbase + BL::ob, sbase + BL::ca, i == 0);
+                mma_xt(tmem + cDS, qa, sbase + BL::ob, sbase + BL::ca, kDecay || i == 0);
                 // dQ~ = [o^ | c] [S_c | z_c]^T (issued while the compute warps mask dA)
                 //     + bf16(dA) K^                (into the NZ / dQ columns)
                 for (int kk = 0; kk < 4; ++kk)
@@ -514,6 +669,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         }
         __syncwarp();
     } else if (warp < 8) {
+        // decay: lanes 0-15 carry the prefix state [S | z] (rows srow), lanes 16-31
+        // the segment's adjoint sum X = sum_c exp(B_c - B_seg) exp(b_m) q'^T [o^ | c]
+        // (rows srow - 16); lf = log2 decay of the segment's chunks so far
+        if (kDecay && n > 0) {  // the first chunk's operand exp(b_m) [S | z]_in
+            const int s0 = nA % kStages;
+            if (cwait(&bars[B_TDONE + s0], (nA / kStages) & 1))
+                write_operand(sm + BL::sb, exp2_fast(dec[s0 * (BL::decs / 4) + 128]), carry, carry_z);
+        }
         if (n > 0) {
             cwait(&bars[B_PFULL], 0);
             if (ok) {
@@ -529,7 +692,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             // (1) state refresh: bf16 [S | z]_c+1 into sb[(i + 1) % 2]; the previous
             // chunk's dq store has left its dO tile, so that slot is released
             if (!cwait(&bars[B_SFULL], i & 1)) break;
-            refresh(cS, sm + BL::sb + ((i + 1) & 1) * BL::sbuf);
+            if constexpr (kDecay) {
+                // [S|z]_c+1 = exp(b_end) [S|z]_c + exp(b_end - b_m) U'_c (the chunk's decay
+                // values are final once its feature map is; its stage stays until
+                // released by this warp group). The operand of chunk c+1, which carries
+                // that chunk's exp(b_m), is written when its P is masked (step 5): with
+                // two stages, chunk c+1 may not be loaded before this chunk's
+                // predecessor leaves its stage.
+                const int s = j % kStages;
+                if (!cwait(&bars[B_TDONE + s], (j / kStages) & 1)) break;
+                const float* dc = dec + s * (BL::decs / 4);
+                const float ld = exp2_fast(dc[129]), mu = exp2_fast(dc[129] - dc[128]);
+                float uu[32];
+                tc::tmem_ld32(tmem + cS + loff + hf * 32, uu);
+                const float uz = (kNorm && hf == 0) ? tmem_ld1(tmem + cS + loff + 64) : 0.f;
+                if (lane < 16) {
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) carry[x] = fmaf(ld, carry[x], mu * uu[x]);
+                    carry_z = fmaf(ld, carry_z, mu * uz);
+                }
+            } else {
+                refresh(cS, sm + BL::sb + ((i + 1) & 1) * BL::sbuf);
+            }
             if (tid == 0 && i >= 1) {
                 tc::bulk_wait_read0();
                 tc::mbar_arrive(&bars[B_EMPTY + (j - 1) % kStages]);
@@ -573,8 +757,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 float dq[32], qv[32];
                 tc::tmem_ld32(tmem + cNZ + loff + hf * 32, dq);
                 load_chunks<kFp16>(slot_ptr(j, BL::q), row, hf * 4, 4, qv);
+                if constexpr (kDecay) {
+                    // q' = phi(q) f_t and dQ~ = f_t x (the accumulator), f_t = exp(b_t - b_m);
+                    // s q' . acc is the query part of d log(gamma_t)
+                    const float* dc = dec + (j % kStages) * (BL::decs / 4);
+                    const float ft = exp2_fast(dc[row] - dc[128]), ift = exp2_fast(dc[128] - dc[row]);
+                    float gq = 0.f;
 #pragma unroll
-                for (int x = 0; x < 32; ++x) dq[x] *= p.scale * min_nan(qv[x], 1.f);
+                    for (int x = 0; x < 32; ++x) {
+                        gq = fmaf(qv[x], dq[x], gq);
+                        dq[x] *= p.scale * ft * min_nan(qv[x] * ift, 1.f);
+                    }
+                    if (want_dlg) dxs[hf * 128 + row] = gq;
+                } else {
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) dq[x] *= p.scale * min_nan(qv[x], 1.f);
+                }
                 uint8_t* dst = slot_ptr(j, BL::g);
 #pragma unroll
                 for (int x = 0; x < 4; ++x) store_chunk<kFp16>(dst, row, hf * 4 + x, dq + 8 * x);
@@ -586,10 +784,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                     tc::tma_store_4d(&P.tm_dq, dst, 0, c * kC, h, b);
                     tc::bulk_commit();
                 }
+                if (want_dlg && hf == 0 && c * kC + row < p.N) wgq[c * kC + row] = p.scale * (dxs[row] + dxs[128 + row]);
+            }
+            if constexpr (kDecay) {
+                // X += exp(B_c - B_seg) exp(b_m) W'_c, W'_c = q'^T [o^ | c] of this chunk
+                // (TMEM, rows in lanes 0-15, handed to lanes 16-31)
+                const float* dc = dec + (j % kStages) * (BL::decs / 4);
+                const float sg = exp2_fast(lf + dc[128]);
+                lf += dc[129];
+                float ww[32];
+                tc::tmem_ld32(tmem + cDS + loff + hf * 32, ww);
+                float wz = (kNorm && hf == 0) ? tmem_ld1(tmem + cDS + loff + 64) : 0.f;
+#pragma unroll
+                for (int x = 0; x < 32; ++x) ww[x] = __shfl_sync(0xffffffffu, ww[x], lane & 15);
+                wz = __shfl_sync(0xffffffffu, wz, lane & 15);
+                if (lane >= 16) {
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) carry[x] = fmaf(sg, ww[x], carry[x]);
+                    carry_z = fmaf(sg, wz, carry_z);
+                }
             }
             // (5) P of the next chunk: causal mask, bf16 in place
             if (i + 1 < n) {
                 if (!cwait(&bars[B_PFULL], (i + 1) & 1)) break;
+                if constexpr (kDecay) {  // and its operand exp(b_m) [S | z]_c+1 (its stage is loaded: P is done)
+                    const int s1 = (j + 1) % kStages;
+                    if (!cwait(&bars[B_TDONE + s1], ((j + 1) / kStages) & 1)) break;
+                    write_operand(sm + BL::sb + ((i + 1) & 1) * BL::sbuf,
+                                  exp2_fast(dec[s1 * (BL::decs / 4) + 128]), carry, carry_z);
+                }
                 mask_to_bf16(cP, false);
                 publish(&bars[B_PSDONE]);
             }
@@ -601,15 +824,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     }
 
     // ------------------------------------------------ suffix exchange (dS^, dz^)
-    if (warp < 8) publish_sums(cDS, n > 0 && ok, Xs, 0);
-    tc::tc_fence_before();
-    cluster.sync();
-    tc::tc_fence_after();
-    if (warp < 8) gather_sums(g + 1, P.G, nullptr, nullptr, carry, carry_z);
+    if (warp < 8) {
+        if constexpr (kDecay) {  // X from lanes 16-31, and the segment's log2 decay total
+            if (lane >= 16) {
+                const int xr = srow - 16;
+#pragma unroll
+                for (int x = 0; x < 32; ++x) Xs[xr * 64 + hf * 32 + x] = (n > 0 && ok) ? carry[x] : 0.f;
+                if (hf == 0) Xz[xr] = (kNorm && n > 0 && ok) ? carry_z : 0.f;
+            }
+            if (tid == 0) misc[2] = lf;
+        } else {
+            publish_sums(cDS, n > 0 && ok, Xs, 0);
+        }
+    }
     tc::tc_fence_before();
     cluster.sync();
     tc::tc_fence_after();
     if (warp < 8) {
+        if (kDecay) gather_suffix_decayed(carry, carry_z);
+        else gather_sums(g + 1, P.G, nullptr, nullptr, carry, carry_z);
+    }
+    tc::tc_fence_before();
+    cluster.sync();
+    tc::tc_fence_after();
+    if (warp < 8 && !kDecay) {  // (with decay the adjoint stays in registers, lanes 0-15)
         install_state(cDS, sm + BL::sb, carry, carry_z);
         tc::fence_proxy_async();
     }
@@ -648,7 +886,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 if (i >= 1) ok = wait_bar(&bars[B_DSBDONE], (i - 1) & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
-                mma_xt(tmem + cDS, qa, sbase + BL::ob, sbase + BL::ca, false);
+                mma_xt(tmem + cDS, qa, sbase + BL::ob, sbase + BL::ca, kDecay);
                 tc::mma_commit(&bars[B_DSFULL]);
                 // dK~ = [V | 1] [dS^ | dz^]^T + bf16(dA^T) q^ ;  dV = K^ dS^ + bf16(P^T) o^.
                 // The state terms go first, while the compute warps mask P^T and dA^T.
@@ -679,22 +917,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         __syncwarp();
     } else if (warp < 8) {
         // mask and (Zc, c) of a chunk's row, fetched one chunk ahead
-        auto fetch = [&](int cc, float& m_, float2& z_) {
+        auto fetch = [&](int cc, float& m_, float2& z_, float& gq_) {
+            const bool in = cc * kC + row < p.N;
             m_ = row_mask_at(cc, row);
-            z_ = (cc * kC + row < p.N) ? wsz[cc * kC + row] : make_float2(1.f, 0.f);
+            z_ = in ? wsz[cc * kC + row] : make_float2(1.f, 0.f);
+            if (want_dlg) gq_ = in ? wgq[cc * kC + row] : 0.f;
         };
-        float m_cur = 0.f;
+        float m_cur = 0.f, gq_cur = 0.f;
         float2 zcc_cur = make_float2(1.f, 0.f);
-        if (n > 0) fetch(c_begin + n - 1, m_cur, zcc_cur);
+        float dlg_carry = 0.f;  // d log(gamma) summed over this segment's later tokens
+        if (kDecay && n > 0) {  // the first (last in time) chunk's operand exp(b_end - b_m) [dS^ | dz^]
+            const int s0 = (nA + n) % kStages;
+            if (cwait(&bars[B_TDONE + s0], ((nA + n) / kStages) & 1)) {
+                const float* dc = dec + s0 * (BL::decs / 4);
+                write_operand(sm + BL::sb, exp2_fast(dc[129] - dc[128]), carry, carry_z);
+                tc::fence_proxy_async();
+            }
+        }
+        if (n > 0) fetch(c_begin + n - 1, m_cur, zcc_cur, gq_cur);
         for (int i = 0; i < n && ok; ++i) {
             const int j = nA + n + i, c = c_begin + n - 1 - i;
-            const float m = m_cur;
+            const float m = m_cur, gq = gq_cur;
             const float2 zcc = zcc_cur;
-            if (i + 1 < n) fetch(c - 1, m_cur, zcc_cur);
+            if (i + 1 < n) fetch(c - 1, m_cur, zcc_cur, gq_cur);
             // (1) o^ = m dO / Zc and the c atom, from the workspace
             {
                 const float inv = m / zcc.x;
                 if (!cwait(&bars[B_TDONE + j % kStages], (j / kStages) & 1)) break;  // dO, q^, k^ ready
+                if (kDecay && i >= 1) {  // this chunk's operand exp(b_end - b_m) G_c+1
+                    const float* dc = dec + (j % kStages) * (BL::decs / 4);
+                    write_operand(sm + BL::sb + (i & 1) * BL::sbuf, exp2_fast(dc[129] - dc[128]), carry, carry_z);
+                }
                 float go[32];
                 load_chunks<kFp16>(slot_ptr(j, BL::g), row, hf * 4, 4, go);
 #pragma unroll
@@ -721,11 +974,83 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             publish(&bars[B_CPDONE]);
             // (3) suffix refresh: bf16 [dS^ | dz^] into sb[(i + 1) % 2]
             if (!cwait(&bars[B_DSFULL], i & 1)) break;
-            refresh(cDS, sm + BL::sb + ((i + 1) & 1) * BL::sbuf);
+            if constexpr (kDecay) {
+                // G_c = exp(b_m) W'_c + exp(b_end) G_c+1 (the adjoint of the state before
+                // chunk c); the operand of chunk c-1, which carries that chunk's
+                // exp(b_end - b_m), is written in its step 1
+                const float* dc = dec + (j % kStages) * (BL::decs / 4);
+                const float fm = exp2_fast(dc[128]), fe = exp2_fast(dc[129]);
+                float ww[32];
+                tc::tmem_ld32(tmem + cDS + loff + hf * 32, ww);
+                const float wz = (kNorm && hf == 0) ? tmem_ld1(tmem + cDS + loff + 64) : 0.f;
+                if (lane < 16) {
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) carry[x] = fmaf(fm, ww[x], fe * carry[x]);
+                    carry_z = fmaf(fm, wz, fe * carry_z);
+                }
+            } else {
+                refresh(cDS, sm + BL::sb + ((i + 1) & 1) * BL::sbuf);
+            }
             publish(&bars[B_DSBDONE]);
             // (4) dk = s dK~ phi'(k) m over the (dead) dO tile, dv = s dV m over o^
             if (!cwait(&bars[B_KVFULL], i & 1)) break;
-            {
+            if constexpr (kDecay) {
+                // k' = m phi(k) g and dK~ = s g x (the accumulator), g = exp(b_m - b_tau);
+                // s k' . acc is the key part of d log(gamma_tau)
+                const float* dc = dec + (j % kStages) * (BL::decs / 4);
+                const float gt = exp2_fast(dc[128] - dc[row]), igt = exp2_fast(dc[row] - dc[128]);
+                const float sm_ = p.scale * m;
+                uint8_t* dst = slot_ptr(j, BL::g);
+                float gk = 0.f;
+                {
+                    float dk[32], kv[32];
+                    tc::tmem_ld32(tmem + cDK + loff + hf * 32, dk);
+                    load_chunks<kFp16>(slot_ptr(j, BL::k), row, hf * 4, 4, kv);
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) {
+                        gk = fmaf(kv[x], dk[x], gk);
+                        dk[x] *= sm_ * gt * min_nan(kv[x] * igt, 1.f);
+                    }
+#pragma unroll
+                    for (int x = 0; x < 4; ++x) store_chunk<kFp16>(dst, row, hf * 4 + x, dk + 8 * x);
+                }
+                {
+                    float dv[32];
+                    tc::tmem_ld32(tmem + cDV + loff + hf * 32, dv);
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) dv[x] *= sm_;
+#pragma unroll
+                    for (int x = 0; x < 4; ++x) store_chunk<kFp16>(sm + BL::ob, row, hf * 4 + x, dv + 8 * x);
+                }
+                if (want_dlg) dxs[hf * 128 + row] = gk;
+                tc::fence_proxy_async();
+                tc::tc_fence_before();
+                tc::bar_sync(kBarCompute, kComputeThreads);
+                if (tid == 0) {
+                    tc::mbar_arrive(&bars[B_KVDONE]);  // dK / dV columns read
+                    tc::tma_store_4d(&P.tm_dk, dst, 0, c * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dv, sm + BL::ob, 0, c * kC, h, b);
+                    tc::bulk_commit();
+                }
+                if (want_dlg) {
+                    // g_t = s q~.dQ~ - s k~.dK~; d log(gamma_t) = m_t sum_{t' >= t} g_t'
+                    // (reverse scan: lanes within the quad's 32 rows, then the quads, then
+                    // the later chunks of the segment; later segments are added at the end)
+                    float x = gq - p.scale * (dxs[row] + dxs[128 + row]);
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const float y = __shfl_down_sync(0xffffffffu, x, o);
+                        if (lane + o < 32) x += y;
+                    }
+                    const float qtot = __shfl_sync(0xffffffffu, x, 0);
+                    if (hf == 0 && lane == 0) misc[4 + quad] = qtot;
+                    tc::bar_sync(kBarCompute, kComputeThreads);
+                    float later = dlg_carry;
+                    for (int qq = quad + 1; qq < 4; ++qq) later += misc[4 + qq];
+                    if (hf == 0 && c * kC + row < p.N) p.dlg[(int64_t)bh * p.N + c * kC + row] = m * (x + later);
+                    dlg_carry += misc[4] + misc[5] + misc[6] + misc[7];
+                }
+            } else {
                 float dk[32], dv[32], kv[32];
                 tc::tmem_ld32(tmem + cDK + loff + hf * 32, dk);
                 tc::tmem_ld32(tmem + cDV + loff + hf * 32, dv);
@@ -768,16 +1093,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 }
                 tc::bulk_commit();
             }
+            if (want_dlg && hf == 0)  // and their d log(gamma) (masked tokens)
+                for (int d = nL + g; d < nC; d += P.G)
+                    if (d * kC + row < p.N) p.dlg[(int64_t)bh * p.N + d * kC + row] = 0.f;
         }
+        if (want_dlg && tid == 0) misc[3] = dlg_carry;
         if (tid == 0) tc::bulk_wait0();
     }
 
+    if (want_dlg) {
+        // d log(gamma) of this segment's live tokens takes the sum over the later
+        // segments' tokens (their totals, read over DSMEM)
+        tc::tc_fence_before();
+        cluster.sync();
+        float off = 0.f;
+        for (int r = g + 1; r < P.G; ++r) off += cluster.map_shared_rank(misc, r)[3];
+        cluster.sync();  // remote reads done
+        if (warp < 8 && n > 0 && ok && off != 0.f) {
+            float* dl = p.dlg + (int64_t)bh * p.N;
+            const int t1 = min(p.N, (c_begin + n) * kC);
+            for (int t = c_begin * kC + tid; t < t1; t += kComputeThreads)
+                if (row_mask_at(t / kC, t % kC) != 0.f) dl[t] += off;
+        }
+    }
     tc::tc_fence_before();
     __syncthreads();
     if (warp == kWarpMma) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
-template <bool kFp16, bool kNorm>
+template <bool kFp16, bool kNorm, bool kDecay>
 cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     BwdParams P;
     memset(&P, 0, sizeof(P));
@@ -796,7 +1140,7 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     if (!P.status) return cudaErrorInvalidDevice;
     P.G = pick_segments(p);
     P.cps = (nC + P.G - 1) / P.G;
-    const void* kern = reinterpret_cast<const void*>(&bwd_kernel<kFp16, kNorm>);
+    const void* kern = reinterpret_cast<const void*>(&bwd_kernel<kFp16, kNorm, kDecay>);
     void* args[] = {&P};
     return launch_cluster(kern, P.G, p.B * p.H, kBwdThreads, BL::total + 1024, st, args);
 }
@@ -804,8 +1148,12 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_bwd_v2(const ScanParams& p, int dtype, cudaStream_t st) {
-    if (dtype == SUBQ_FP16) return p.normalize ? launch<true, true>(p, st) : launch<true, false>(p, st);
-    return p.normalize ? launch<false, true>(p, st) : launch<false, false>(p, st);
+    if (p.decay_mode != SUBQ_DECAY_NONE) {  // bf16 only (the factorised decay needs its exponent range)
+        if (dtype != SUBQ_BF16 || !p.fallback) return cudaErrorInvalidValue;
+        return p.normalize ? launch<false, true, true>(p, st) : launch<false, false, true>(p, st);
+    }
+    if (dtype == SUBQ_FP16) return p.normalize ? launch<true, true, false>(p, st) : launch<true, false, false>(p, st);
+    return p.normalize ? launch<false, true, false>(p, st) : launch<false, false, false>(p, st);
 }
 
 }  // namespace tcs
