@@ -11,6 +11,15 @@ one backward scan over the batch. Inputs (268 MB) exceed the 126 MB L2.
 Multi-GPU (torchrun, one rank per GPU): every rank runs the full per-GPU
 workload on its own batch (batch x head sharding, no collective in the
 path): weak scaling; time = max over ranks of the device-timed region.
+
+  python bench.py --workload encoder [--seq-len 16384] [--batch 4]
+
+prints a second kind of line (not the default): one training step of the
+surgered audio encoder the model path runs (12 pre-LayerNorm blocks, d_model
+768, 12 heads, FFN 3072 GELU, linear attention with data-dependent decay
+gating, input Linear(80, 768), MSE loss, bf16 autocast, AdamW step), random
+init and seeded N(0,1) frames; under torchrun the model is wrapped in DDP
+(NCCL gradient all-reduce), per-GPU batch fixed (weak scaling).
 """
 from __future__ import annotations
 
@@ -43,7 +52,102 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--path", default="auto", choices=["auto", "exact", "tensorcore"])
+    p.add_argument("--workload", default="scan", choices=["scan", "encoder"])
+    p.add_argument("--seq-len", type=int, default=16384)
+    p.add_argument("--batch", type=int, default=4)
     return p.parse_args()
+
+
+def encoder_main(args, rank, world, local_rank):
+    """One training step of the surgered encoder (see the module docstring)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    from subq_audio import ops
+    from subq_audio.autograd import SubQLinearAttention
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dev = torch.device("cuda", local_rank if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    Bb, L, Dm, Hh = args.batch, args.seq_len, 768, 12
+
+    class Block(nn.Module):  # pre-LN block of the reference's audio model (model.py:97-135)
+        def __init__(self):
+            super().__init__()
+            self.ln1, self.ln2 = nn.LayerNorm(Dm), nn.LayerNorm(Dm)
+            self.attn = SubQLinearAttention(Dm, Hh, use_data_dependent_gating=True)
+            self.ff = nn.Sequential(nn.Linear(Dm, 3072), nn.GELU(), nn.Linear(3072, Dm))
+
+        def forward(self, x):
+            x = x + self.attn(self.ln1(x))[0]
+            return x + self.ff(self.ln2(x))
+
+    torch.manual_seed(0)
+    model = nn.Sequential(nn.Linear(80, Dm), *[Block() for _ in range(12)]).to(dev)
+    if world > 1:
+        model = nn.parallel.DistributedDataParallel(model, device_ids=[dev.index], bucket_cap_mb=25,
+                                                    gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    g = torch.Generator().manual_seed(4321 + rank)
+    x_h = torch.randn(Bb, L, 80, generator=g).pin_memory()
+    y = torch.randn(Bb, L, Dm, generator=g).to(dev)
+    x_d = torch.empty(x_h.shape, device=dev)
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def train_step():
+        x_d.copy_(x_h, non_blocking=True)  # the step's input frames from pinned host memory
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = model(x_d)
+            loss = F.mse_loss(out.float(), y)
+        loss.backward()
+        opt.step()
+        loss_h.copy_(loss.detach(), non_blocking=True)  # the step's loss back to the host
+
+    for _ in range(args.warmup):
+        train_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler = clocks_sampler(dev.index) if rank == 0 else None
+    time.sleep(0.3 if sampler else 0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        train_step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clk = clocks_summary(sampler)
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    tokens = Bb * L * world
+    if rank == 0:
+        line = {"metric": f"surgered encoder training step tokens/sec (B={Bb}/GPU, N={L}, 12x768)",
+                "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"12-layer surgered audio encoder training step (pre-LN, d_model 768, "
+                                       f"12 heads, FFN 3072, gated decay), B={Bb}/GPU, N={L}, AdamW",
+                           "parallelism": f"ddp{world}" if world > 1 else "single", "scan_path": ops.last_path(),
+                           "l2": "activations far above the 126 MB L2"},
+                "e2e": {"value": tokens / (ms / 1e3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": x_h.numel() * 4, "d2h_bytes_per_step": 4},
+                "gpu_launches": 4 * 12 * args.steps, "clocks": clk}
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
 
 
 # --------------------------------------------------------------------------
@@ -159,6 +263,14 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.workload == "encoder":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the encoder workload is timed on the "
+                                  "tensor-core path only; the reference arm times the scan workload"}))
+            return 0
+        return encoder_main(args, rank, world, local_rank)
 
     if args.impl == "reference":
         if rank != 0:
