@@ -3,6 +3,11 @@
 // device status word. The kernels live in scan_tc_fwd.cu / scan_tc_bwd.cu.
 #include "tc_common.cuh"
 
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
+
 namespace subq {
 
 // First error code raised by a bounded device-side wait of the tensor-core
@@ -50,17 +55,6 @@ bool strides_ok(int64_t sb, int64_t sh, int64_t sn, const void* ptr) {
            sn * 2 < ((int64_t)1 << 40) && sh * 2 < ((int64_t)1 << 40) && sb * 2 < ((int64_t)1 << 40);
 }
 
-int num_sms() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 }  // namespace
 
 // [B, H, N, 64] 16-bit tensor, box of 64 x 128 tokens, 128-byte swizzle.
@@ -79,14 +73,48 @@ bool make_map(CUtensorMap* m, const void* base, int dtype, int N, int H, int B, 
     return r == CUDA_SUCCESS;
 }
 
-// Segments (CTAs of one cluster) per sequence: grow while the grid stays
-// within one wave of SMs and each segment keeps at least one chunk.
-int pick_segments(const ScanParams& p) {
+// Clusters of G CTAs of `kern` that the device holds at once (cached per
+// device, kernel and G; a cluster must fit in one GPC, so this is below
+// SMs / G when G does not divide a GPC's SM count).
+static int max_active_clusters(const void* kern, int G, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, const void*, int>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_tuple(dev, kern, G);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess) {
+        cudaLaunchConfig_t cfg;
+        memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3(G, 1, 1);
+        cfg.blockDim = dim3(threads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = G;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();  // a failed query leaves no sticky error behind
+    cache[key] = n;
+    return n;
+}
+
+// Segments (CTAs of one cluster) per sequence: the largest G <= 8 (and <= the
+// chunk count) for which every sequence's cluster is resident at once, so the
+// grid runs in one wave; G = 1 when even single CTAs need more than one wave.
+int pick_segments(const ScanParams& p, const void* kern, int threads, size_t smem) {
     const int nC = (p.N + kC - 1) / kC;
     const int bh = p.B * p.H;
-    int G = 1;
-    while (G < 8 && bh * G * 2 <= num_sms() && G * 2 <= nC) G *= 2;
-    return G;
+    for (int G = std::min(8, nC); G > 1; --G)
+        if (bh <= max_active_clusters(kern, G, threads, smem)) return G;
+    return 1;
 }
 
 cudaError_t launch_cluster(const void* kern, int G, int BH, int threads, size_t smem, cudaStream_t st, void** args) {

@@ -1138,9 +1138,9 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     const int nC = (p.N + kC - 1) / kC;
     P.status = status_ptr();
     if (!P.status) return cudaErrorInvalidDevice;
-    P.G = pick_segments(p);
-    P.cps = (nC + P.G - 1) / P.G;
     const void* kern = reinterpret_cast<const void*>(&bwd_kernel<kFp16, kNorm, kDecay>);
+    P.G = pick_segments(p, kern, kBwdThreads, BL::total + 1024);
+    P.cps = (nC + P.G - 1) / P.G;
     void* args[] = {&P};
     return launch_cluster(kern, P.G, p.B * p.H, kBwdThreads, BL::total + 1024, st, args);
 }

@@ -370,7 +370,7 @@ __device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
 // Launch plumbing (scan_tc.cu).
 struct Maps;
 bool make_map(CUtensorMap* m, const void* base, int dtype, int N, int H, int B, int64_t sn, int64_t sh, int64_t sb);
-int pick_segments(const ScanParams& p);
+int pick_segments(const ScanParams& p, const void* kern, int threads, size_t smem);
 int* status_ptr();  // device address of the status word (current device)
 cudaError_t launch_cluster(const void* kern, int G, int BH, int threads, size_t smem, cudaStream_t st, void** args);
 
