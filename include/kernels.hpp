@@ -74,7 +74,10 @@ typedef enum subq_decay_mode {
 } subq_decay_mode;
 
 /* Which kernel family a call may use. AUTO picks the tensor-core path when
- * the shape allows it and the exact float32 path otherwise. */
+ * the shape allows it (bf16/fp16, d = e = 64; with per-token decay bf16
+ * only) and the exact float32 path otherwise; calls of at most 16 tokens
+ * (streaming decode steps) take the exact, token-recurrent path, which is
+ * faster there. */
 typedef enum subq_kernel_path {
     SUBQ_PATH_AUTO = 0,
     SUBQ_PATH_EXACT = 1,      /* SIMT float32 sequential scan, any d, e <= 256 */

@@ -76,8 +76,16 @@ int check_tensor(const subq_tensor4& t, const char* name, int dtype, bool empty)
     return SUBQ_OK;
 }
 
+// Calls of at most this many tokens (streaming decode steps) run on the
+// token-recurrent kernel under SUBQ_PATH_AUTO: a single-token step takes
+// about 3.7 us there against about 13 us for one chunk of the tensor-core
+// kernel (measured on B200 at B*H <= 48, CUDA-graph replay); the two meet
+// near 16 tokens.
+constexpr int kRecurrentMaxTokens = 16;
+
 bool use_tc(const subq::ScanParams& p, int dtype, int path) {
     if (path == SUBQ_PATH_EXACT || dtype == SUBQ_FP64) return false;
+    if (path == SUBQ_PATH_AUTO && p.N <= kRecurrentMaxTokens) return false;
     return subq::tc_supported(p, dtype);
 }
 

@@ -185,6 +185,63 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
     return dq, dk, dv, dlg
 
 
+class DecodeStep:
+    """Streaming decode over preallocated device buffers: the serving loop of
+    the scan, with the float32 state carried on the device and updated in
+    place (the C3 streaming case at its finest grain, one call per new token
+    or a few tokens).
+
+    ``q, k`` [B, H, T, d], ``v`` [B, H, T, e] and ``out`` [B, H, T, e] hold the
+    step's T new tokens (usually T = 1); ``S`` [B, H, d, e] and, for the
+    normalised form, ``z`` [B, H, d] are contiguous float32 state buffers.
+    ``log_gamma`` is None, a float, a float32 [H] tensor or a contiguous
+    float32 [B, H, T] tensor; ``mask`` a contiguous bool/uint8 [B, T] tensor.
+    ``step()`` enqueues one scan call on the current stream: out = the scan of
+    the new tokens from (S, z), then (S, z) <- the state after them. It
+    allocates nothing and does not synchronise, so a CUDA graph can capture
+    it; refill q, k, v (and log_gamma, mask) in place between steps.
+    Short steps run on the token-recurrent kernel (see ``subq_fwd``'s path
+    choice).
+    """
+
+    def __init__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, S: torch.Tensor,
+                 z: Optional[torch.Tensor] = None, *, log_gamma: LogGamma = None, mask: Optional[torch.Tensor] = None,
+                 normalize: bool = True, scale: Optional[float] = None, clamp_min: float = 1e-5, path: str = "auto"):
+        _require_cuda(q, k, v, out, S)
+        B, H, T, d = q.shape
+        e = v.shape[-1]
+        for name, t, shape in (("k", k, (B, H, T, d)), ("v", v, (B, H, T, e)), ("out", out, (B, H, T, e))):
+            if tuple(t.shape) != shape or t.dtype != q.dtype or t.stride(-1) != 1:
+                raise ValueError(f"{name} must be {shape} of {q.dtype} with a contiguous last dimension")
+        if q.stride(-1) != 1:
+            raise ValueError("q must have a contiguous last dimension")
+        if S.dtype != torch.float32 or tuple(S.shape) != (B, H, d, e) or not S.is_contiguous():
+            raise ValueError(f"S must be a contiguous float32 [{B}, {H}, {d}, {e}] tensor")
+        if normalize and (z is None or z.dtype != torch.float32 or tuple(z.shape) != (B, H, d)
+                          or not z.is_contiguous()):
+            raise ValueError(f"z must be a contiguous float32 [{B}, {H}, {d}] tensor for the normalised form")
+        self._keep: list = [q, k, v, out, S, z]
+        a = _capi.FwdArgs()
+        a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, False, path, self._keep)
+        # the step must read the caller's buffers, not copies made at set-up
+        if isinstance(log_gamma, torch.Tensor) and a.desc.log_gamma != log_gamma.data_ptr():
+            raise ValueError("log_gamma must be a contiguous float32 [H] or [B, H, T] tensor")
+        if mask is not None and a.desc.mask != mask.data_ptr():
+            raise ValueError("mask must be a contiguous bool or uint8 [B, T] tensor")
+        a.q, a.k, a.v, a.o = _t4(q), _t4(k), _t4(v), _t4(out)
+        a.state_in = a.state_out = S.data_ptr()
+        if normalize:
+            a.norm_in = a.norm_out = z.data_ptr()
+        self.device = q.device
+        with torch.cuda.device(q.device):
+            a.workspace, a.workspace_bytes = _workspace(_capi.fwd_workspace_bytes(a), q.device, self._keep)
+        self._args = a
+
+    def step(self) -> None:
+        self._args.stream = torch.cuda.current_stream(self.device).cuda_stream
+        _capi.fwd(self._args)
+
+
 def feature_map_(x: torch.Tensor) -> torch.Tensor:
     """In-place phi(x) = ELU(x) + 1 on a contiguous CUDA tensor (run_feature_map)."""
     _require_cuda(x)
