@@ -20,6 +20,14 @@ surgered audio encoder the model path runs (12 pre-LayerNorm blocks, d_model
 gating, input Linear(80, 768), MSE loss, bf16 autocast, AdamW step), random
 init and seeded N(0,1) frames; under torchrun the model is wrapped in DDP
 (NCCL gradient all-reduce), per-GPU batch fixed (weak scaling).
+
+  python bench.py --workload stream   long-context streaming inference: B=1, H=4,
+      d=64, N=131072 fp16 fed as 32 calls of 4096 tokens with the float32
+      state carried between calls (one step = the whole stream)
+  python bench.py --workload engine   the C++ engine's forward (SubQEngine): B=1,
+      N=1024, D=256 float32 U[0,1), decay 0.99, through the numpy API (host
+      buffers) and forward_raw (device buffers); --impl reference times the
+      reference's own C++ engine (CPU build) on the same call
 """
 from __future__ import annotations
 
@@ -52,10 +60,134 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--path", default="auto", choices=["auto", "exact", "tensorcore"])
-    p.add_argument("--workload", default="scan", choices=["scan", "encoder"])
+    p.add_argument("--workload", default="scan", choices=["scan", "encoder", "stream", "engine"])
     p.add_argument("--seq-len", type=int, default=16384)
     p.add_argument("--batch", type=int, default=4)
     return p.parse_args()
+
+
+def _device_timer(fn, steps, warmup):
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = clocks_sampler(torch.cuda.current_device())
+    time.sleep(0.3)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, clocks_summary(sampler)
+
+
+def stream_main(args):
+    """Long-context streaming inference (see the module docstring)."""
+    import torch
+
+    from subq_audio import ops
+
+    Bs, Hs, Ns, Ls = 1, 4, 131072, 4096
+    g = torch.Generator().manual_seed(77)
+    hq, hk, hv = (torch.randn(Bs, Hs, Ns, D, generator=g).to(torch.float16).pin_memory() for _ in range(3))
+    q, k, v = (x.cuda() for x in (hq, hk, hv))
+    o = torch.empty_like(q)
+    ho = torch.empty_like(hq).pin_memory()
+
+    def run(qq, kk, vv):
+        st = None
+        for s0 in range(0, Ns, Ls):
+            _, st = ops.scan_forward(qq[:, :, s0:s0 + Ls], kk[:, :, s0:s0 + Ls], vv[:, :, s0:s0 + Ls], state=st,
+                                     return_state=True, out=o[:, :, s0:s0 + Ls])
+        return st
+
+    ms, clk = _device_timer(lambda: run(q, k, v), args.steps, args.warmup)
+    path = ops.last_path()
+
+    def e2e():  # inputs from pinned host memory, outputs back to it, every step
+        q.copy_(hq, non_blocking=True), k.copy_(hk, non_blocking=True), v.copy_(hv, non_blocking=True)
+        run(q, k, v)
+        ho.copy_(o, non_blocking=True)
+
+    e2e_ms, _ = _device_timer(e2e, max(3, args.steps // 2), 1)
+    tokens = Bs * Ns
+    line = {"metric": "streaming linear-attn forward tokens/sec (B=1,H=4,N=131072 as 32x4096 calls, d=64)",
+            "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "ms_per_call": ms / (Ns // Ls), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "causal ELU+1 linear attention forward, B=1 H=4 d=64, N=131072 fed as 32 "
+                                   "calls of 4096 tokens with the float32 (S, z) state carried", "path": path,
+                       "l2": "inputs 201 MB > 126 MB L2"},
+            "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 3 * hq.numel() * 2, "d2h_bytes_per_step": ho.numel() * 2},
+            "gpu_launches": (Ns // Ls) * args.steps, "clocks": clk}
+    print(json.dumps(line))
+    return 0
+
+
+def engine_main(args):
+    """The C++ engine's forward at B=1, N=1024, D=256 float32 (see the module docstring)."""
+    import numpy as np
+
+    Be, Ne, De = 1, 1024, 256
+    rng = np.random.default_rng(0)
+    q, k, v = (rng.random((Be, Ne, De), dtype=np.float32) for _ in range(3))
+    reps = max(3, args.steps)
+    if args.impl == "reference":
+        sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))
+        try:
+            import _C as ref_C  # the reference engine built from its sources (CPU)
+        except ImportError as exc:
+            print(json.dumps({"impl": "reference", "unavailable": f"reference engine not built: {exc}"}))
+            return 0
+        eng = ref_C.SubQEngine(256 * 1024 * 1024)
+        eng.forward(q, k, v, 0.99)
+        t0 = time.perf_counter()
+        n = 0
+        while n < reps and (n == 0 or time.perf_counter() - t0 < 20.0):
+            eng.forward(q, k, v, 0.99)
+            n += 1
+        ms = (time.perf_counter() - t0) / n * 1e3
+        val = Be * Ne / (ms / 1e3)
+        print(json.dumps({"impl": "reference", "metric": "engine forward tokens/sec (B=1,N=1024,D=256 fp32)",
+                          "value": val, "unit": "tokens/s", "n_gpus": 0, "steps": n, "warmup": 1,
+                          "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "f32", "data": "synthetic",
+                          "config": {"workload": "SubQEngine.forward B=1 N=1024 D=256 decay 0.99"},
+                          "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                                           "sample": "the whole call (the engine's forward is single-threaded)"},
+                          "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return 0
+    import torch
+
+    from subq_audio import SubQEngine
+
+    eng = SubQEngine(256 * 1024 * 1024)
+    # through the numpy API: host buffers, copies inside each call
+    for _ in range(args.warmup):
+        eng.forward(q, k, v, decay_factor=0.99)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        eng.forward(q, k, v, decay_factor=0.99)
+    e2e_ms = (time.perf_counter() - t0) / reps * 1e3
+    # forward_raw on device buffers (the engine's state stays in its arena)
+    dq, dk, dv = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    do = torch.empty_like(dq)
+    raw = lambda: eng.forward_raw(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), do.data_ptr(), Be, Ne, De, 0.99)  # noqa: E731
+    ms, clk = _device_timer(raw, reps, args.warmup)
+    line = {"metric": "engine forward tokens/sec (B=1,N=1024,D=256 fp32)", "value": Be * Ne / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": reps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "SubQEngine.forward_raw B=1 N=1024 D=256 decay 0.99 (exact recurrent kernel)",
+                       "l2": "3 MB of inputs fit in L2: a latency-bound single-sequence scan"},
+            "e2e": {"value": Be * Ne / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 3 * q.nbytes,
+                    "d2h_bytes_per_step": q.nbytes},
+            "gpu_launches": reps, "clocks": clk}
+    print(json.dumps(line))
+    return 0
 
 
 def encoder_main(args, rank, world, local_rank):
@@ -264,6 +396,15 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
 
+    if args.workload == "engine":
+        return engine_main(args) if rank == 0 else 0
+    if args.workload == "stream":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the streaming workload is timed on the "
+                                  "GPU path only; the reference arm times the scan and engine workloads"}))
+            return 0
+        return stream_main(args) if rank == 0 else 0
     if args.workload == "encoder":
         if args.impl == "reference":
             if rank == 0:

@@ -358,64 +358,78 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         }
         if (lane < 16) {
 #pragma unroll
-            for (int x = 0; x < 32; ++x) X[srow * 64 + hf * 32 + x] = v[x];
+            for (int x = 0; x < 32; ++x) X[xch(srow, hf, x)] = v[x];
         }
         if (hf == 0) {
             const float zv = (kNorm && have) ? tmem_ld1(tmem + tcol + loff + 64) : 0.f;
             if (lane < 16) Xz[piece * 64 + srow] = zv;
         }
     };
-    // S_in plus the partial segment sums of the segments before this CTA's
-    auto gather_prefix = [&](float* v, float& z) {
+    // Exchange gathers (compute warps): every lane ends with the sum for row
+    // quad * 16 + (lane & 15); lanes 16-31 are then cleared (the M = 64 rows
+    // live in lanes 0-15, and with decay lanes 16-31 start the adjoint sum at 0).
+    auto clear_upper = [&](float* v, float& z) {
+        if (lane >= 16) {
 #pragma unroll
-        for (int x = 0; x < 32; ++x) v[x] = 0.f;
-        z = 0.f;
-        if (lane < 16) {
-            if (p.S_in) {
-                const float* src = p.S_in + ((int64_t)bh * kD + srow) * kD + hf * 32;
-#pragma unroll
-                for (int x = 0; x < 32; ++x) v[x] = src[x];
-            }
-            if (kNorm && hf == 0) z = p.z_in ? p.z_in[(int64_t)bh * kD + srow] : 0.f;
-            for (int r = 0; r < P.G; ++r) {
-                const PrefixShare sr = prefix_share(r, P.G, nL, cps);
-#pragma unroll
-                for (int piece = 0; piece < 2; ++piece) {
-                    const bool used = piece == 0 ? (min(sr.b, sr.x) > sr.a && sr.seg < g)
-                                                 : (sr.b > sr.x && sr.seg + 1 < g);
-                    if (!used) continue;
-                    const float* rx = cluster.map_shared_rank(piece == 0 ? Xs : Xs2, r) + srow * 64 + hf * 32;
-                    // decayed: the state so far decays over the piece, then takes its sum
-                    const float f = kDecay ? exp2_fast(cluster.map_shared_rank(misc, r)[piece]) : 1.f;
-#pragma unroll
-                    for (int x = 0; x < 32; ++x) v[x] = fmaf(f, v[x], rx[x]);
-                    if (kNorm && hf == 0) z = fmaf(f, z, cluster.map_shared_rank(Xz, r)[piece * 64 + srow]);
-                }
-            }
+            for (int x = 0; x < 32; ++x) v[x] = 0.f;
+            z = 0.f;
         }
     };
-    // sum of the exchanged values of CTAs [r0, r1) (+ an optional fp32 base)
-    // -> registers v (this thread's 32 columns of row srow) and z
-    auto gather_sums = [&](int r0, int r1, const float* base_S, const float* base_z, float* v, float& z) {
+    // S_in plus the partial segment sums of the segments before this CTA's
+    // (decayed: S_in decays over all the pieces and each piece over the ones
+    // after it, the Horner chain written as one weighted sum)
+    auto gather_prefix = [&](float* v, float& z) {
+        const int row = quad * 16 + (lane & 15);
 #pragma unroll
         for (int x = 0; x < 32; ++x) v[x] = 0.f;
         z = 0.f;
-        if (lane < 16) {
-            if (base_S) {
-                const float* src = base_S + ((int64_t)bh * kD + srow) * kD + hf * 32;
-#pragma unroll
-                for (int x = 0; x < 32; ++x) v[x] = src[x];
-            }
-            for (int r = r0; r < r1; ++r) {
-                const float* rx = cluster.map_shared_rank(Xs, r) + srow * 64 + hf * 32;
-#pragma unroll
-                for (int x = 0; x < 32; ++x) v[x] += rx[x];
-            }
-            if (kNorm && hf == 0) {
-                z = base_z ? base_z[(int64_t)bh * kD + srow] : 0.f;
-                for (int r = r0; r < r1; ++r) z += cluster.map_shared_rank(Xz, r)[srow];
-            }
+        int pr[16], pb[16], np = 0;
+        for (int r = 0; r < P.G; ++r) {
+            const PrefixShare sr = prefix_share(r, P.G, nL, cps);
+            if (min(sr.b, sr.x) > sr.a && sr.seg < g) pr[np] = r, pb[np++] = 0;
+            if (sr.b > sr.x && sr.seg + 1 < g) pr[np] = r, pb[np++] = 1;
         }
+        float wl = 1.f, w_in = 1.f;
+        if (kDecay) {
+            const float lam = lane < np ? cluster.map_shared_rank(misc, pr[lane])[pb[lane]] : 0.f;
+            float total;
+            wl = exp2_fast(piece_exponent(lam, lane, true, total));
+            w_in = exp2_fast(total);
+        }
+        if (lane < 16) {
+            if (p.S_in) {
+                const float* src = p.S_in + ((int64_t)bh * kD + row) * kD + hf * 32;
+#pragma unroll
+                for (int x = 0; x < 32; ++x) v[x] = w_in * src[x];
+            }
+            if (kNorm && hf == 0) z = p.z_in ? w_in * p.z_in[(int64_t)bh * kD + row] : 0.f;
+        }
+        gather_pieces(
+            np, pr, pb, wl, row, hf, lane,
+            [&](int r, int pc) { return cluster.map_shared_rank(pc == 0 ? Xs : Xs2, r); },
+            [&](int r, int pc) { return cluster.map_shared_rank(Xz, r) + pc * 64; }, kNorm && hf == 0, v, z);
+        clear_upper(v, z);
+    };
+    // the adjoint at this segment's end: the later segments' sums X_r (each at
+    // its segment's start); decayed, X_r takes the decay of the segments
+    // between (G = X_g+1 + exp(Lambda_g+1) (X_g+2 + ...), as one weighted sum)
+    auto gather_suffix = [&](float* v, float& z) {
+        const int row = quad * 16 + (lane & 15);
+#pragma unroll
+        for (int x = 0; x < 32; ++x) v[x] = 0.f;
+        z = 0.f;
+        int pr[8], pb[8], np = 0;
+        for (int r = g + 1; r < P.G; ++r) pr[np] = r, pb[np++] = 0;
+        float wl = 1.f;
+        if (kDecay) {
+            const float lam = lane < np ? cluster.map_shared_rank(misc, pr[lane])[2] : 0.f;
+            float total;
+            wl = exp2_fast(piece_exponent(lam, lane, false, total));
+        }
+        gather_pieces(
+            np, pr, pb, wl, row, hf, lane, [&](int r, int) { return cluster.map_shared_rank(Xs, r); },
+            [&](int r, int) { return cluster.map_shared_rank(Xz, r); }, kNorm && hf == 0, v, z);
+        clear_upper(v, z);
     };
     // registers -> TMEM accumulator (M = 64 layout) and bf16 copy in `dst`
     auto install_state = [&](uint32_t tcol, uint8_t* dst, const float* v, float z) {
@@ -456,23 +470,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             }
         }
     };
-    // decay: the adjoint at this segment's end, Horner over the later segments
-    // r = G-1 .. g+1: G = X_r + exp(Lambda_r) G (X_r at segment r's start)
-    auto gather_suffix_decayed = [&](float* v, float& z) {
-#pragma unroll
-        for (int x = 0; x < 32; ++x) v[x] = 0.f;
-        z = 0.f;
-        if (lane < 16) {
-            for (int r = P.G - 1; r > g; --r) {
-                const float f = exp2_fast(cluster.map_shared_rank(misc, r)[2]);
-                const float* rx = cluster.map_shared_rank(Xs, r) + srow * 64 + hf * 32;
-#pragma unroll
-                for (int x = 0; x < 32; ++x) v[x] = fmaf(f, v[x], rx[x]);
-                if (kNorm && hf == 0) z = fmaf(f, z, cluster.map_shared_rank(Xz, r)[srow]);
-            }
-        }
-    };
-
     // ============================================================ phase A
     if (warp == kWarpProducer) {
         if (lane == 0) {
@@ -525,7 +522,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             float* dst = pc == 0 ? Xs : Xs2;
             if (lane < 16) {
 #pragma unroll
-                for (int x = 0; x < 32; ++x) dst[srow * 64 + hf * 32 + x] = X[x];
+                for (int x = 0; x < 32; ++x) dst[xch(srow, hf, x)] = X[x];
                 if (hf == 0) Xz[pc * 64 + srow] = xz;
             }
         };
@@ -829,7 +826,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             if (lane >= 16) {
                 const int xr = srow - 16;
 #pragma unroll
-                for (int x = 0; x < 32; ++x) Xs[xr * 64 + hf * 32 + x] = (n > 0 && ok) ? carry[x] : 0.f;
+                for (int x = 0; x < 32; ++x) Xs[xch(xr, hf, x)] = (n > 0 && ok) ? carry[x] : 0.f;
                 if (hf == 0) Xz[xr] = (kNorm && n > 0 && ok) ? carry_z : 0.f;
             }
             if (tid == 0) misc[2] = lf;
@@ -841,8 +838,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     cluster.sync();
     tc::tc_fence_after();
     if (warp < 8) {
-        if (kDecay) gather_suffix_decayed(carry, carry_z);
-        else gather_sums(g + 1, P.G, nullptr, nullptr, carry, carry_z);
+        gather_suffix(carry, carry_z);
     }
     tc::tc_fence_before();
     cluster.sync();

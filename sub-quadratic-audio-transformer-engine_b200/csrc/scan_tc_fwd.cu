@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             float* dst = pc == 0 ? Xs1 : Xs2;
             if (lane < 16) {
 #pragma unroll
-                for (int x = 0; x < 32; ++x) dst[srow * 64 + hf * 32 + x] = X[x];
+                for (int x = 0; x < 32; ++x) dst[xch(srow, hf, x)] = X[x];
                 if (hf == 0) Xz[pc * 64 + srow] = xz;
             }
         };
@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             }
             if (lane < 16) {
 #pragma unroll
-                for (int x = 0; x < 32; ++x) X[srow * 64 + hf * 32 + x] = v[x];
+                for (int x = 0; x < 32; ++x) X[xch(srow, hf, x)] = v[x];
             }
             if (hf == 0) {
                 const float zv = (kNorm && have) ? tmem_ld1(tmem + col + loff + 64) : 0.f;
@@ -373,33 +373,42 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
 
     // ------------------------------------------------------ segment prefix
     // S_in plus every partial sum of a segment before this CTA's, read over DSMEM
+    // (decayed: S_in decays over all the pieces and each piece over the ones after
+    // it, the Horner chain written as one weighted sum)
     float v[32], z = 0.f;
 #pragma unroll
     for (int x = 0; x < 32; ++x) v[x] = 0.f;
     if (warp < 8) {
-        const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
+        const int quad = warp & 3, hf = warp >> 2, row = quad * 16 + (lane & 15);
+        int pr[16], pb[16], np = 0;  // the pieces of the segments before this one, in order
+        for (int r = 0; r < P.G; ++r) {
+            const PrefixShare sr = prefix_share(r, P.G, nL, cps);
+            if (min(sr.b, sr.x) > sr.a && sr.seg < g) pr[np] = r, pb[np++] = 0;
+            if (sr.b > sr.x && sr.seg + 1 < g) pr[np] = r, pb[np++] = 1;
+        }
+        float wl = 1.f, w_in = 1.f;
+        if (kDecay) {
+            const float lam = lane < np ? cluster.map_shared_rank(Lam, pr[lane])[pb[lane]] : 0.f;
+            float total;
+            wl = exp2_fast(piece_exponent(lam, lane, true, total));
+            w_in = exp2_fast(total);
+        }
         if (lane < 16) {
             if (p.S_in) {
-                const float* src = p.S_in + ((int64_t)bh * kD + srow) * kD + hf * 32;
+                const float* src = p.S_in + ((int64_t)bh * kD + row) * kD + hf * 32;
 #pragma unroll
-                for (int x = 0; x < 32; ++x) v[x] = src[x];
+                for (int x = 0; x < 32; ++x) v[x] = w_in * src[x];
             }
-            if (kNorm && hf == 0) z = p.z_in ? p.z_in[(int64_t)bh * kD + srow] : 0.f;
-            for (int r = 0; r < P.G; ++r) {
-                const PrefixShare sr = prefix_share(r, P.G, nL, cps);
+            if (kNorm && hf == 0) z = p.z_in ? w_in * p.z_in[(int64_t)bh * kD + row] : 0.f;
+        }
+        gather_pieces(
+            np, pr, pb, wl, row, hf, lane,
+            [&](int r, int pc) { return cluster.map_shared_rank(pc == 0 ? Xs1 : Xs2, r); },
+            [&](int r, int pc) { return cluster.map_shared_rank(Xz, r) + pc * 64; }, kNorm && hf == 0, v, z);
+        if (lane >= 16) {  // lanes 16-31 keep zeros (the M = 64 state rows live in lanes 0-15)
 #pragma unroll
-                for (int piece = 0; piece < 2; ++piece) {
-                    const bool used = piece == 0 ? (min(sr.b, sr.x) > sr.a && sr.seg < g)
-                                                 : (sr.b > sr.x && sr.seg + 1 < g);
-                    if (!used) continue;
-                    const float* rx = cluster.map_shared_rank(piece == 0 ? Xs1 : Xs2, r) + srow * 64 + hf * 32;
-                    // decayed: the state so far decays over the piece, then takes its sum
-                    const float f = kDecay ? exp2_fast(cluster.map_shared_rank(Lam, r)[piece]) : 1.f;
-#pragma unroll
-                    for (int x = 0; x < 32; ++x) v[x] = fmaf(f, v[x], rx[x]);
-                    if (kNorm && hf == 0) z = fmaf(f, z, cluster.map_shared_rank(Xz, r)[piece * 64 + srow]);
-                }
-            }
+            for (int x = 0; x < 32; ++x) v[x] = 0.f;
+            z = 0.f;
         }
     }
     tc::tc_fence_before();

@@ -146,6 +146,53 @@ __device__ __forceinline__ PrefixShare prefix_share(int r, int G, int nL, int cp
     return s;
 }
 
+// Exchange layout of a 64 x 64 float32 partial sum read by the other CTAs of
+// a cluster over DSMEM: element (row, 32 hf + x) at x * 128 + 64 hf + row, so
+// that the 16 rows a warp reads for one x are 64 contiguous bytes (one
+// coalesced remote access per load instruction instead of 16 scattered ones).
+__device__ __forceinline__ int xch(int row, int hf, int x) { return x * 128 + hf * 64 + row; }
+
+// Exponents of the weights of an ordered list of exchange pieces under decay:
+// lane i holds lam_i, the log2 decay across piece i (0 past the list). Returns
+// in lane i the sum of lam over the pieces after i (after = true) or before i
+// (after = false), and in `total` the sum over all of them.
+__device__ __forceinline__ float piece_exponent(float lam, int lane, bool after, float& total) {
+    float t = lam;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = after ? __shfl_down_sync(0xffffffffu, t, o) : __shfl_up_sync(0xffffffffu, t, o);
+        if (after ? (lane + o < 32) : (lane >= o)) t += y;
+    }
+    total = __shfl_sync(0xffffffffu, t, after ? 0 : 31);
+    return t - lam;
+}
+
+// v (this thread's 32 values of exchange row `row`, column half hf) and z (the
+// normaliser column, `with_z` threads) += sum_i w_i X_i over `np` pieces of
+// other CTAs' exchange buffers, piece i at px(pr[i], pb[i]) and pz(pr[i],
+// pb[i]) with its weight in lane i of `wl`. The two lane halves of the warp
+// read alternate pieces (their remote loads overlap) and the halves' sums are
+// combined, so every lane ends with the row's total; callers start half 1
+// (lanes 16-31) from zero.
+template <typename PX, typename PZ>
+__device__ __forceinline__ void gather_pieces(int np, const int* pr, const int* pb, float wl, int row, int hf,
+                                              int lane, PX px, PZ pz, bool with_z, float* v, float& z) {
+    const int half = lane >> 4;
+    for (int i = 0; i < np; i += 2) {
+        const int my = i + half;
+        const float w = __shfl_sync(0xffffffffu, wl, my & 31);
+        if (my < np) {
+            const float* rx = px(pr[my], pb[my]) + xch(row, hf, 0);
+#pragma unroll
+            for (int x = 0; x < 32; ++x) v[x] = fmaf(w, rx[x * 128], v[x]);
+            if (with_z) z = fmaf(w, pz(pr[my], pb[my])[row], z);
+        }
+    }
+#pragma unroll
+    for (int x = 0; x < 32; ++x) v[x] += __shfl_xor_sync(0xffffffffu, v[x], 16);
+    z += __shfl_xor_sync(0xffffffffu, z, 16);
+}
+
 // Bounded mbarrier wait; on expiry records SUBQ_ERR_TIMEOUT in *status (the
 // library's device status word) and returns false.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* status) {
