@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define SUBQ_ABI_VERSION 1
+#define SUBQ_ABI_VERSION 2
 
 typedef enum subq_status {
     SUBQ_OK = 0,
@@ -102,6 +102,13 @@ typedef struct subq_scan_desc {
     int64_t mask_stride_b;
     int32_t flush_subnormal; /* flush |S| < FLT_MIN to 0 after every update   */
     int32_t path;            /* subq_kernel_path                              */
+    /* Grouped K/V (GQA, python/subq_audio/autograd.py:746-748): 0 or `heads`
+     * = one K/V head per query head; else a divisor of `heads`, and query
+     * head h reads K/V head h / (heads / kv_heads). k, v (and dk, dv) then
+     * have kv_heads heads; the backward's dk, dv sum over each group, as the
+     * reference's repeat_interleave does under autograd. The state S, z and
+     * log gamma stay per query head. */
+    int64_t kv_heads;
 } subq_scan_desc;
 
 typedef struct subq_fwd_args {

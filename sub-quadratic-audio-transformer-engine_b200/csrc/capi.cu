@@ -51,6 +51,8 @@ int check_desc(const subq_scan_desc& d, subq::ScanParams& p) {
         return fail(SUBQ_ERR_INVALID_ARGUMENT, "unknown kernel path");
     if (!(d.clamp_min >= 0.f))
         return fail(SUBQ_ERR_INVALID_ARGUMENT, "clamp_min must be >= 0");
+    if (d.kv_heads < 0 || (d.kv_heads > 0 && d.heads % d.kv_heads != 0))
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "kv_heads must be 0 or a divisor of heads");
     memset(&p, 0, sizeof(p));
     p.B = (int)d.batch; p.H = (int)d.heads; p.N = (int)d.seq_len;
     p.d = (int)d.head_dim; p.e = (int)d.value_dim;
@@ -63,6 +65,7 @@ int check_desc(const subq_scan_desc& d, subq::ScanParams& p) {
     p.mask = d.mask;
     p.mask_sb = d.mask ? d.mask_stride_b : 0;
     p.flush = d.flush_subnormal ? 1 : 0;
+    p.kvg = (d.kv_heads > 0 && d.heads > 0) ? (int)(d.heads / d.kv_heads) : 1;
     return SUBQ_OK;
 }
 
@@ -148,6 +151,21 @@ size_t exact_bwd_ws(const subq::ScanParams& p, int dtype) {
     return align_up(elem_size(dtype == SUBQ_FP64 ? SUBQ_FP64 : SUBQ_FP32) * 3 * (size_t)p.B * p.H * (size_t)p.N);
 }
 
+// Grouped K/V: the scan kernels write dk [B, H, N, d] and dv [B, H, N, e] per
+// query head into contiguous buffers after the kernels' own workspace; group
+// sums then write the caller's [B, kv_heads, N, *] gradients.
+size_t gqa_dk_bytes(const subq::ScanParams& p, int dtype) {
+    return align_up(elem_size(dtype) * (size_t)p.B * p.H * (size_t)p.N * (size_t)p.d);
+}
+size_t gqa_bytes(const subq::ScanParams& p, int dtype) {
+    if (p.kvg <= 1) return 0;
+    return gqa_dk_bytes(p, dtype) + align_up(elem_size(dtype) * (size_t)p.B * p.H * (size_t)p.N * (size_t)p.e);
+}
+
+size_t scan_bwd_ws(const subq::ScanParams& p, int dtype, bool tc) {
+    return tc ? subq::tc_bwd_workspace_bytes(p) : exact_bwd_ws(p, dtype);
+}
+
 int check_workspace(void* ws, size_t have, size_t need) {
     if (need == 0) return SUBQ_OK;
     if (!ws) return fail(SUBQ_ERR_WORKSPACE, "workspace required: " + std::to_string(need) + " bytes");
@@ -190,8 +208,7 @@ size_t subq_fwd_workspace_bytes(const subq_fwd_args* a) {
 size_t subq_bwd_workspace_bytes(const subq_bwd_args* a) {
     subq::ScanParams p;
     if (fill_bwd(a, p) != SUBQ_OK) return 0;
-    if (use_tc_bwd(p, a->desc.dtype, a->desc.path)) return subq::tc_bwd_workspace_bytes(p);
-    return exact_bwd_ws(p, a->desc.dtype);
+    return scan_bwd_ws(p, a->desc.dtype, use_tc_bwd(p, a->desc.dtype, a->desc.path)) + gqa_bytes(p, a->desc.dtype);
 }
 
 int subq_fwd(const subq_fwd_args* a) {
@@ -241,14 +258,31 @@ int subq_bwd(const subq_bwd_args* a) {
     cudaStream_t st = static_cast<cudaStream_t>(a->stream);
     cudaError_t err;
     int launches = 0;
-    const size_t need = tc ? subq::tc_bwd_workspace_bytes(p) : exact_bwd_ws(p, a->desc.dtype);
+    const size_t scan_need = scan_bwd_ws(p, a->desc.dtype, tc);
+    const size_t need = scan_need + gqa_bytes(p, a->desc.dtype);
     if ((rc = check_workspace(a->workspace, a->workspace_bytes, need))) return rc;
     p.ws = static_cast<float*>(a->workspace);
+    if (p.kvg > 1) {  // per-query-head dk, dv into the workspace; summed per group below
+        char* base = static_cast<char*>(a->workspace) + scan_need;
+        p.dk = base;
+        p.dk_sn = p.d, p.dk_sh = (int64_t)p.N * p.d, p.dk_sb = p.dk_sh * p.H;
+        p.dv = base + gqa_dk_bytes(p, a->desc.dtype);
+        p.dv_sn = p.e, p.dv_sh = (int64_t)p.N * p.e, p.dv_sb = p.dv_sh * p.H;
+    }
     if (tc) {
         err = subq::launch_bwd_tc(p, a->desc.dtype, st, &launches);
     } else {
         err = subq::launch_bwd_exact(p, a->desc.dtype, st);
         launches = 1;
+    }
+    if (err == cudaSuccess && p.kvg > 1) {
+        const int Hkv = p.H / p.kvg;
+        err = subq::launch_group_sum(p.dk, a->dk.data, a->desc.dtype, p.B, Hkv, p.kvg, p.N, p.d, a->dk.stride_b,
+                                     a->dk.stride_h, a->dk.stride_n, st);
+        if (err == cudaSuccess)
+            err = subq::launch_group_sum(p.dv, a->dv.data, a->desc.dtype, p.B, Hkv, p.kvg, p.N, p.e, a->dv.stride_b,
+                                         a->dv.stride_h, a->dv.stride_n, st);
+        launches += 2;
     }
     if (err != cudaSuccess) return fail_cuda(err, "subq_bwd launch");
     g_last_path = tc ? SUBQ_PATH_TENSORCORE : SUBQ_PATH_EXACT;

@@ -38,6 +38,10 @@ struct ScanParams {
     // the exact kernels, given the array, then compute only the flagged
     // sequences (null: every sequence).
     int* fallback;
+    // K/V group size (GQA): query head h reads K/V head h / kvg; 1 = one K/V
+    // head per query head. dk, dv are then written per query head (the caller
+    // sums each group).
+    int kvg;
 };
 
 // phi(x) = ELU(x) + 1 and its derivative (reference python/subq_audio/autograd.py:15-28).

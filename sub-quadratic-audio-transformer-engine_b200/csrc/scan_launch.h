@@ -13,6 +13,9 @@ size_t exact_bwd_smem_bytes(int d, int e, int normalize, size_t acc_bytes);
 cudaError_t launch_fwd_exact(const ScanParams& p, int dtype, cudaStream_t st);
 cudaError_t launch_bwd_exact(const ScanParams& p, int dtype, cudaStream_t st);
 cudaError_t launch_feature_map(void* x, int64_t n, int dtype, cudaStream_t st);
+// dst[b, hk] = sum of src[b, hk * G .. hk * G + G) (grouped K/V gradients)
+cudaError_t launch_group_sum(const void* src, void* dst, int dtype, int B, int Hkv, int G, int N, int e,
+                             int64_t dsb, int64_t dsh, int64_t dsn, cudaStream_t st);
 
 // Tensor-core path (scan_tc.cu).
 bool tc_supported(const ScanParams& p, int dtype);

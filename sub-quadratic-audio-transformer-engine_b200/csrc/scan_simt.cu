@@ -9,6 +9,8 @@
 // sequential one, so float32 results stay within ~1e-6 of a float64 scan.
 #include <float.h>
 
+#include <algorithm>
+
 #include "scan_common.cuh"
 #include "scan_launch.h"
 
@@ -48,8 +50,8 @@ __global__ void __launch_bounds__(288) scan_fwd_exact_kernel(ScanParams p, int E
 
     const int64_t bh = (int64_t)b * p.H + h;
     const T* qb = (const T*)p.q + b * p.q_sb + h * p.q_sh;
-    const T* kb = (const T*)p.k + b * p.k_sb + h * p.k_sh;
-    const T* vb = (const T*)p.v + b * p.v_sb + h * p.v_sh;
+    const T* kb = (const T*)p.k + b * p.k_sb + (h / p.kvg) * p.k_sh;
+    const T* vb = (const T*)p.v + b * p.v_sb + (h / p.kvg) * p.v_sh;
     T* ob = (T*)p.o + b * p.o_sb + h * p.o_sh;
 
     A s[RPT];
@@ -183,8 +185,8 @@ __global__ void __launch_bounds__(256) scan_bwd_exact_kernel(ScanParams p) {
     A* red = ov + LD;        // [33]
 
     const T* qb = (const T*)p.q + b * p.q_sb + h * p.q_sh;
-    const T* kb = (const T*)p.k + b * p.k_sb + h * p.k_sh;
-    const T* vb = (const T*)p.v + b * p.v_sb + h * p.v_sh;
+    const T* kb = (const T*)p.k + b * p.k_sb + (h / p.kvg) * p.k_sh;
+    const T* vb = (const T*)p.v + b * p.v_sb + (h / p.kvg) * p.v_sh;
     const T* gb = (const T*)p.g + b * p.g_sb + h * p.g_sh;
     T* dqb = (T*)p.o + b * p.o_sb + h * p.o_sh;
     T* dkb = (T*)p.dk + b * p.dk_sb + h * p.dk_sh;
@@ -361,6 +363,48 @@ cudaError_t launch_bwd_exact(const ScanParams& p, int dtype, cudaStream_t st) {
         case SUBQ_FP16: return launch_bwd_t<__half, float>(p, st);
         case SUBQ_FP64: return launch_bwd_t<double, double>(p, st);
         default: return launch_bwd_t<__nv_bfloat16, float>(p, st);
+    }
+}
+
+// Grouped K/V: dst[b, hk, n, :] = sum over the group's query heads of
+// src[b, hk * G + g, n, :] (src contiguous [B, Hkv * G, N, e]; dst strided),
+// accumulated in A. The reduction autograd applies to the reference's
+// repeat_interleave of K and V (python/subq_audio/autograd.py:746-748).
+template <typename T, typename A>
+__global__ void __launch_bounds__(256) group_sum_kernel(const T* src, T* dst, int B, int Hkv, int G, int N, int e,
+                                                        int64_t dsb, int64_t dsh, int64_t dsn) {
+    const int64_t total = (int64_t)B * Hkv * N * e;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % e);
+        int64_t r = i / e;
+        const int n = (int)(r % N);
+        r /= N;
+        const int hk = (int)(r % Hkv);
+        const int b = (int)(r / Hkv);
+        const T* s = src + (((int64_t)b * Hkv * G + (int64_t)hk * G) * N + n) * e + c;
+        A acc = 0;
+        for (int g = 0; g < G; ++g) acc += load_a<A>(s[(int64_t)g * N * e]);
+        dst[b * dsb + hk * dsh + (int64_t)n * dsn + c] = store_a<T, A>(acc);
+    }
+}
+
+template <typename T, typename A>
+cudaError_t launch_group_sum_t(const void* src, void* dst, int B, int Hkv, int G, int N, int e, int64_t dsb,
+                               int64_t dsh, int64_t dsn, cudaStream_t st) {
+    const int64_t total = (int64_t)B * Hkv * N * e;
+    if (total == 0) return cudaSuccess;
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    group_sum_kernel<T, A><<<blocks, 256, 0, st>>>((const T*)src, (T*)dst, B, Hkv, G, N, e, dsb, dsh, dsn);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_group_sum(const void* src, void* dst, int dtype, int B, int Hkv, int G, int N, int e,
+                             int64_t dsb, int64_t dsh, int64_t dsn, cudaStream_t st) {
+    switch (dtype) {
+        case SUBQ_FP32: return launch_group_sum_t<float, float>(src, dst, B, Hkv, G, N, e, dsb, dsh, dsn, st);
+        case SUBQ_FP16: return launch_group_sum_t<__half, float>(src, dst, B, Hkv, G, N, e, dsb, dsh, dsn, st);
+        case SUBQ_FP64: return launch_group_sum_t<double, double>(src, dst, B, Hkv, G, N, e, dsb, dsh, dsn, st);
+        default: return launch_group_sum_t<__nv_bfloat16, float>(src, dst, B, Hkv, G, N, e, dsb, dsh, dsn, st);
     }
 }
 

@@ -156,8 +156,9 @@ bool tc_bwd_supported(const ScanParams& p, int) {
     using namespace tcs;
     // d log(gamma) comes with the decayed kernels only (without decay it is not defined)
     if (p.dlg != nullptr && p.decay_mode == SUBQ_DECAY_NONE) return false;
+    // (with grouped K/V the kernel writes dk, dv into contiguous workspace buffers)
     return strides_ok(p.g_sb, p.g_sh, p.g_sn, p.g) &&
-           strides_ok(p.dk_sb, p.dk_sh, p.dk_sn, p.dk) && strides_ok(p.dv_sb, p.dv_sh, p.dv_sn, p.dv);
+           (p.kvg > 1 || (strides_ok(p.dk_sb, p.dk_sh, p.dk_sn, p.dk) && strides_ok(p.dv_sb, p.dv_sh, p.dv_sn, p.dv)));
 }
 
 static size_t align256(size_t x) { return (x + 255) / 256 * 256; }

@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     const int g = (int)cluster.block_rank();
     const int bh = blockIdx.y;
     const int b = bh / p.H, h = bh - b * p.H;
+    const int hk = h / p.kvg;  // K/V head (grouped K/V: shared by kvg query heads)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nC = (p.N + kC - 1) / kC;
 
@@ -219,8 +220,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 tc::tma_load_4d(base + BL::q, &P.tm_q, 0, chunk * kC, h, b, &bars[B_FULL + s]);
                 tc::tma_load_4d(base + BL::g, &P.tm_g, 0, chunk * kC, h, b, &bars[B_FULL + s]);
             }
-            tc::tma_load_4d(base + BL::k, &P.tm_k, 0, chunk * kC, h, b, &bars[B_FULL + s]);
-            tc::tma_load_4d(base + BL::v, &P.tm_v, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + BL::k, &P.tm_k, 0, chunk * kC, hk, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + BL::v, &P.tm_v, 0, chunk * kC, hk, b, &bars[B_FULL + s]);
         }
     };
     auto transform = [&](int jlo, int jhi) {
@@ -1124,8 +1125,8 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     P.p = p;
     const int dt = kFp16 ? SUBQ_FP16 : SUBQ_BF16;
     if (!make_map(&P.tm_q, p.q, dt, p.N, p.H, p.B, p.q_sn, p.q_sh, p.q_sb) ||
-        !make_map(&P.tm_k, p.k, dt, p.N, p.H, p.B, p.k_sn, p.k_sh, p.k_sb) ||
-        !make_map(&P.tm_v, p.v, dt, p.N, p.H, p.B, p.v_sn, p.v_sh, p.v_sb) ||
+        !make_map(&P.tm_k, p.k, dt, p.N, p.H / p.kvg, p.B, p.k_sn, p.k_sh, p.k_sb) ||
+        !make_map(&P.tm_v, p.v, dt, p.N, p.H / p.kvg, p.B, p.v_sn, p.v_sh, p.v_sb) ||
         !make_map(&P.tm_g, p.g, dt, p.N, p.H, p.B, p.g_sn, p.g_sh, p.g_sb) ||
         !make_map(&P.tm_dq, p.o, dt, p.N, p.H, p.B, p.o_sn, p.o_sh, p.o_sb) ||
         !make_map(&P.tm_dk, p.dk, dt, p.N, p.H, p.B, p.dk_sn, p.dk_sh, p.dk_sb) ||

@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     const int g = (int)cluster.block_rank();
     const int bh = blockIdx.y;
     const int b = bh / p.H, h = bh - b * p.H;
+    const int hk = h / p.kvg;  // K/V head (grouped K/V: shared by kvg query heads)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nC = (p.N + kC - 1) / kC;
 
@@ -196,8 +197,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             uint8_t* base = sm + s * L::stage;
             tc::mbar_arrive_expect_tx(&bars[B_FULL + s], (ph2 ? 3u : 2u) * kTile);
             if (ph2) tc::tma_load_4d(base + L::q, &P.tm_q, 0, chunk * kC, h, b, &bars[B_FULL + s]);
-            tc::tma_load_4d(base + L::k, &P.tm_k, 0, chunk * kC, h, b, &bars[B_FULL + s]);
-            tc::tma_load_4d(base + L::v, &P.tm_v, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + L::k, &P.tm_k, 0, chunk * kC, hk, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + L::v, &P.tm_v, 0, chunk * kC, hk, b, &bars[B_FULL + s]);
         }
     };
     auto transform = [&](int jlo, int jhi) {
@@ -711,8 +712,8 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     P.p = p;
     const int dt = kFp16 ? SUBQ_FP16 : SUBQ_BF16;
     if (!make_map(&P.tm_q, p.q, dt, p.N, p.H, p.B, p.q_sn, p.q_sh, p.q_sb) ||
-        !make_map(&P.tm_k, p.k, dt, p.N, p.H, p.B, p.k_sn, p.k_sh, p.k_sb) ||
-        !make_map(&P.tm_v, p.v, dt, p.N, p.H, p.B, p.v_sn, p.v_sh, p.v_sb) ||
+        !make_map(&P.tm_k, p.k, dt, p.N, p.H / p.kvg, p.B, p.k_sn, p.k_sh, p.k_sb) ||
+        !make_map(&P.tm_v, p.v, dt, p.N, p.H / p.kvg, p.B, p.v_sn, p.v_sh, p.v_sb) ||
         !make_map(&P.tm_o, p.o, dt, p.N, p.H, p.B, p.o_sn, p.o_sh, p.o_sb))
         return cudaErrorInvalidValue;
     const int nC = (p.N + kC - 1) / kC;

@@ -214,7 +214,8 @@ def chunkwise_flash_linear_attention(q: torch.Tensor, k: torch.Tensor, v: torch.
         w_rev = torch.flip(decay_w, dims=[-1]) if isinstance(decay_w, torch.Tensor) and decay_w.ndim >= 2 else decay_w
         vm_rev = torch.flip(valid_mask, dims=[2]) if valid_mask is not None else None
         out_b, _, _ = _single_direction(flip(q), flip(k), flip(v), w_rev, None, vm_rev, False)
-        diag = v if valid_mask is None else v * valid_mask.expand_as(v)
+        vq = v if v.shape[1] == q.shape[1] else v.repeat_interleave(q.shape[1] // v.shape[1], dim=1)
+        diag = vq if valid_mask is None else vq * valid_mask.expand_as(vq)
         out = out + flip(out_b) - diag
         if valid_mask is not None:
             out = out * valid_mask.expand_as(out)
@@ -362,9 +363,9 @@ class SubQLinearAttention(nn.Module):
         if position_embeddings is not None:
             cos, sin = position_embeddings
             Q, K = apply_rotary_pos_emb(Q, K, cos, sin)
-        if self.num_key_value_groups > 1:
-            K = K.repeat_interleave(self.num_key_value_groups, dim=1)
-            V = V.repeat_interleave(self.num_key_value_groups, dim=1)
+        # grouped K/V (num_key_value_groups > 1) go to the kernels as they are:
+        # query head h reads K/V head h // groups, and the backward sums dK, dV
+        # over each group (the reference's repeat_interleave, autograd.py:746-748)
         if self.use_data_dependent_gating and self.gate_proj is not None:
             gate = self.gate_proj(hidden_states).transpose(1, 2)
             decay_w = self.raw_decay.view(1, self.num_heads, 1) + gate

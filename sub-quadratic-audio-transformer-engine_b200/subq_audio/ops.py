@@ -44,12 +44,21 @@ def _inner_contig(t: torch.Tensor) -> torch.Tensor:
     return t if (t.shape[-1] <= 1 or t.stride(-1) == 1) else t.contiguous()
 
 
+def _check_kv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    """k [B, Hkv, N, d] and v [B, Hkv, N, e] with Hkv a divisor of q's H (grouped K/V)."""
+    B, H, N, d = q.shape
+    if (k.dim() != 4 or v.dim() != 4 or k.shape[0] != B or k.shape[2] != N or k.shape[3] != d
+            or v.shape[:3] != k.shape[:3] or k.shape[1] < 1 or H % k.shape[1] != 0):
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}")
+
+
 def _desc(q: torch.Tensor, v: torch.Tensor, log_gamma: LogGamma, mask: Optional[torch.Tensor],
           normalize: bool, scale: Optional[float], clamp_min: float, flush_subnormal: bool,
           path: str, keep: list) -> _capi.ScanDesc:
     B, H, N, d = q.shape
     desc = _capi.ScanDesc()
     desc.batch, desc.heads, desc.seq_len, desc.head_dim, desc.value_dim = B, H, N, d, v.shape[-1]
+    desc.kv_heads = v.shape[1] if v.shape[1] != H else 0  # grouped K/V (GQA)
     if q.dtype not in _DTYPES:
         raise TypeError(f"unsupported dtype {q.dtype}; use float32, float16, bfloat16 or float64")
     desc.dtype = _DTYPES[q.dtype]
@@ -108,11 +117,13 @@ def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma
                  clamp_min: float = 1e-5, state: Optional[Tuple[torch.Tensor, Optional[torch.Tensor]]] = None,
                  return_state: bool = False, flush_subnormal: bool = False, path: str = "auto",
                  out: Optional[torch.Tensor] = None):
-    """Causal scan. Returns ``(o, (S, z) | None)``; S [B,H,d,e] and z [B,H,d] are float32."""
+    """Causal scan. Returns ``(o, (S, z) | None)``; S [B,H,d,e] and z [B,H,d] are float32.
+    ``k`` and ``v`` may have fewer heads than ``q`` (a divisor of H: grouped K/V,
+    query head h reading K/V head h // (H // Hkv)); the backward then returns
+    dk, dv summed over each group."""
     _require_cuda(q, k, v)
     q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
-    if k.shape != q.shape or v.shape[:3] != q.shape[:3]:
-        raise ValueError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}")
+    _check_kv(q, k, v)
     if k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError("q, k and v must share one dtype")
     B, H, N, d = q.shape
@@ -154,6 +165,7 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
     dlog_gamma is float32 [B,H,N] (d loss / d log gamma_t per token)."""
     _require_cuda(q, k, v, dout)
     q, k, v, dout = _inner_contig(q), _inner_contig(k), _inner_contig(v), _inner_contig(dout)
+    _check_kv(q, k, v)
     if dout.dtype != q.dtype:
         dout = dout.to(q.dtype)
     B, H, N, d = q.shape
@@ -161,8 +173,8 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
     keep: list = []
     with torch.cuda.device(q.device):
         dq = torch.empty((B, H, N, d), dtype=q.dtype, device=q.device)
-        dk = torch.empty((B, H, N, d), dtype=q.dtype, device=q.device)
-        dv = torch.empty((B, H, N, e), dtype=q.dtype, device=q.device)
+        dk = torch.empty(k.shape, dtype=q.dtype, device=q.device)  # [B, Hkv, N, d]: summed per K/V group
+        dv = torch.empty(v.shape, dtype=q.dtype, device=q.device)
         a = _capi.BwdArgs()
         a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep)
         a.q, a.k, a.v, a.dout = _t4(q), _t4(k), _t4(v), _t4(dout)
@@ -210,7 +222,9 @@ class DecodeStep:
         _require_cuda(q, k, v, out, S)
         B, H, T, d = q.shape
         e = v.shape[-1]
-        for name, t, shape in (("k", k, (B, H, T, d)), ("v", v, (B, H, T, e)), ("out", out, (B, H, T, e))):
+        _check_kv(q, k, v)
+        Hkv = k.shape[1]
+        for name, t, shape in (("k", k, (B, Hkv, T, d)), ("v", v, (B, Hkv, T, e)), ("out", out, (B, H, T, e))):
             if tuple(t.shape) != shape or t.dtype != q.dtype or t.stride(-1) != 1:
                 raise ValueError(f"{name} must be {shape} of {q.dtype} with a contiguous last dimension")
         if q.stride(-1) != 1:
