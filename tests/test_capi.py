@@ -84,6 +84,39 @@ def test_forward_rejects_bad_descriptions(field, value, code):
     assert _capi.load().subq_fwd(ctypes.byref(a)) == code
 
 
+def test_grouped_kv_heads_must_divide_heads():
+    lib = _capi.load()
+    a = _fwd_args(H=4)
+    a.desc.kv_heads = 3
+    assert lib.subq_fwd(ctypes.byref(a)) == _capi.SUBQ_ERR_INVALID_ARGUMENT
+    assert b"kv_heads" in lib.subq_last_error()
+    a.desc.kv_heads = -1
+    assert lib.subq_fwd(ctypes.byref(a)) == _capi.SUBQ_ERR_INVALID_ARGUMENT
+
+
+def test_grouped_kv_backward_workspace_holds_per_head_gradients():
+    """With kv_heads < heads the backward needs room for dk, dv per query head
+    (summed per group afterwards): the workspace grows by 2 x B x H x N x d
+    elements over the same call without grouping (exact path, float32)."""
+    lib = _capi.load()
+    B, H, N, d = 2, 4, 16, 8
+
+    def bwd_args(kv):
+        a = _capi.BwdArgs()
+        a.desc.batch, a.desc.heads, a.desc.seq_len, a.desc.head_dim, a.desc.value_dim = B, H, N, d, d
+        a.desc.dtype, a.desc.scale, a.desc.clamp_min, a.desc.path = _capi.SUBQ_FP32, 1.0, 1e-5, 1
+        a.desc.kv_heads = kv
+        for i, name in enumerate(("q", "k", "v", "dout", "dq", "dk", "dv")):
+            t = getattr(a, name)
+            t.data = 0x10000 * (i + 1)
+            t.stride_b, t.stride_h, t.stride_n = H * N * d, N * d, d
+        return a
+
+    plain = lib.subq_bwd_workspace_bytes(ctypes.byref(bwd_args(0)))
+    grouped = lib.subq_bwd_workspace_bytes(ctypes.byref(bwd_args(2)))
+    assert plain > 0 and grouped - plain >= 2 * B * H * N * d * 4
+
+
 def test_forward_rejects_null_and_misaligned_tensors():
     lib = _capi.load()
     a = _fwd_args()
