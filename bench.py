@@ -11,6 +11,9 @@ one backward scan over the batch. Inputs (268 MB) exceed the 126 MB L2.
 Multi-GPU (torchrun, one rank per GPU): every rank runs the full per-GPU
 workload on its own batch (batch x head sharding, no collective in the
 path): weak scaling; time = max over ranks of the device-timed region.
+--scaling strong splits the one B=8 batch over the ranks instead (rank r
+takes its slice; with 8 ranks one sequence of H=8 heads each, which the
+kernels spread over clusters of up to 8 CTAs per head).
 
   python bench.py --workload encoder [--seq-len 16384] [--batch 4]
 
@@ -61,6 +64,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--path", default="auto", choices=["auto", "exact", "tensorcore"])
     p.add_argument("--workload", default="scan", choices=["scan", "encoder", "stream", "engine"])
+    p.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                   help="scan workload: weak = the full batch on every rank; strong = the B=8 batch split "
+                        "over the ranks (one slice each)")
     p.add_argument("--seq-len", type=int, default=16384)
     p.add_argument("--batch", type=int, default=4)
     return p.parse_args()
@@ -454,9 +460,16 @@ def main():
     torch.cuda.set_device(dev)
     from subq_audio import ops
 
-    g = torch.Generator(device="cpu").manual_seed(1234 + rank)
+    strong = args.scaling == "strong"
+    if strong and B % world:
+        raise SystemExit(f"--scaling strong needs a rank count dividing B={B}")
+    Bl = B // world if strong else B  # this rank's sequences
+    g = torch.Generator(device="cpu").manual_seed(1234 if strong else 1234 + rank)
     q, k, v, do = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16) for _ in range(4))
     lens = torch.randint(N // 2, N + 1, (B,), generator=g)
+    if strong:  # one slice of the shared batch per rank
+        sl = slice(rank * Bl, (rank + 1) * Bl)
+        q, k, v, do, lens = (x[sl].contiguous() for x in (q, k, v, do, lens))
     mask = torch.arange(N)[None, :] < lens[:, None]
     qd, kd, vd, dod, md = (x.to(dev) for x in (q, k, v, do, mask))
     stream = torch.cuda.current_stream(dev)
@@ -495,7 +508,7 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    tokens = B * N * world
+    tokens = B * N * (1 if strong else world)
     value = tokens / (ms_max / 1e3)
 
     # ---- per-kernel launch timing (forward and backward separately) ----
@@ -524,7 +537,7 @@ def main():
     # last output copy.
     hq, hk, hv, hdo, hm = (x.pin_memory() for x in (q, k, v, do, mask))
     h_in = (hq, hk, hv, hdo, hm)
-    outs_h = [[torch.empty((B, H, N, D), dtype=torch.bfloat16).pin_memory() for _ in range(4)] for _ in range(2)]
+    outs_h = [[torch.empty((Bl, H, N, D), dtype=torch.bfloat16).pin_memory() for _ in range(4)] for _ in range(2)]
     h2d = sum(x.numel() * x.element_size() for x in h_in)
     d2h = sum(x.numel() * x.element_size() for x in outs_h[0])
     s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
@@ -572,23 +585,24 @@ def main():
         hbm, tflops, src = peaks()
         valid = float(lens.sum())  # live tokens per head across the batch
         # algorithmic bytes (bf16, d=64): backward reads q,k,v,dO of live tokens and writes dq,dk,dv of all
-        bwd_bytes = H * (valid * 4 * D * 2 + B * N * 3 * D * 2)
-        fwd_bytes = H * (valid * 3 * D * 2 + B * N * D * 2)
+        bwd_bytes = H * (valid * 4 * D * 2 + Bl * N * 3 * D * 2)
+        fwd_bytes = H * (valid * 3 * D * 2 + Bl * N * D * 2)
         dom = "bwd" if bwd_ms >= fwd_ms else "fwd"
         dom_bytes, dom_ms = (bwd_bytes, bwd_ms) if dom == "bwd" else (fwd_bytes, fwd_ms)
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9
         tr = profile_traffic().get(f"{path_used}_{dom}")
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": {**CONFIG, "kernel_path": path_used},
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": args.scaling,
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {**CONFIG, "kernel_path": path_used, "batch_this_gpu": Bl},
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "peak_source": src,
                          "traffic": (tr * 1.0 if tr is not None else None),
                          "algorithmic_bytes": dom_bytes, "launch_ms": dom_ms},
             "kernels_ms": {"fwd": fwd_ms, "bwd": bwd_ms},
-            "tc_frac": (12 * D * D * B * H * N) / (ms_max / 1e3) / (tflops * 1e12),
+            "tc_frac": (12 * D * D * Bl * H * N) / (ms_max / 1e3) / (tflops * 1e12),
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "clocks": clk,
         }
