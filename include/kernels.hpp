@@ -109,6 +109,12 @@ typedef struct subq_scan_desc {
      * reference's repeat_interleave does under autograd. The state S, z and
      * log gamma stay per query head. */
     int64_t kv_heads;
+    /* 1: reverse time - token t sees itself and the later tokens, with the
+     * decay of tokens t..tau-1 between key tau and query t: the second
+     * direction of the bidirectional scan (python/subq_audio/autograd.py:
+     * 407-433, which runs it on time-flipped copies). The caller combines the
+     * two directions. The state runs from the end of the sequence. */
+    int32_t reverse;
 } subq_scan_desc;
 
 typedef struct subq_fwd_args {

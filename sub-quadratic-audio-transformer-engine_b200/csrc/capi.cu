@@ -53,6 +53,7 @@ int check_desc(const subq_scan_desc& d, subq::ScanParams& p) {
         return fail(SUBQ_ERR_INVALID_ARGUMENT, "clamp_min must be >= 0");
     if (d.kv_heads < 0 || (d.kv_heads > 0 && d.heads % d.kv_heads != 0))
         return fail(SUBQ_ERR_INVALID_ARGUMENT, "kv_heads must be 0 or a divisor of heads");
+    if (d.reverse != 0 && d.reverse != 1) return fail(SUBQ_ERR_INVALID_ARGUMENT, "reverse must be 0 or 1");
     memset(&p, 0, sizeof(p));
     p.B = (int)d.batch; p.H = (int)d.heads; p.N = (int)d.seq_len;
     p.d = (int)d.head_dim; p.e = (int)d.value_dim;
@@ -66,6 +67,7 @@ int check_desc(const subq_scan_desc& d, subq::ScanParams& p) {
     p.mask_sb = d.mask ? d.mask_stride_b : 0;
     p.flush = d.flush_subnormal ? 1 : 0;
     p.kvg = (d.kv_heads > 0 && d.heads > 0) ? (int)(d.heads / d.kv_heads) : 1;
+    p.reverse = d.reverse;
     return SUBQ_OK;
 }
 

@@ -42,6 +42,9 @@ struct ScanParams {
     // head per query head. dk, dv are then written per query head (the caller
     // sums each group).
     int kvg;
+    // 1: reverse time (token t sees itself and the later tokens; the
+    // backward direction of the bidirectional scan), tensor-core path only
+    int reverse;
 };
 
 // phi(x) = ELU(x) + 1 and its derivative (reference python/subq_audio/autograd.py:15-28).
@@ -84,6 +87,10 @@ __device__ __forceinline__ float token_log_gamma(const ScanParams& p, int b, int
         default: return 0.f;
     }
 }
+
+// Token in memory at processing position u (reverse time walks the sequence
+// from its end; the recurrence itself is the same).
+__device__ __forceinline__ int tok_at(const ScanParams& p, int u) { return p.reverse ? p.N - 1 - u : u; }
 
 template <typename A>
 __device__ __forceinline__ A flush_small(A s, int flush) {

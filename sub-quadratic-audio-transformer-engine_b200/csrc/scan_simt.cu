@@ -74,21 +74,24 @@ __global__ void __launch_bounds__(288) scan_fwd_exact_kernel(ScanParams p, int E
         __syncthreads();  // the previous step's results have been written out
         for (int x = threadIdx.x; x < nt * d; x += blockDim.x) {
             const int tt = x / d, i = x - tt * d;
-            const A m = token_mask(p, b, t0 + tt);
-            qs[x] = phi_f(load_a<A>(qb[(int64_t)(t0 + tt) * p.q_sn + i])) * (A)p.scale;
-            ks[x] = phi_f(load_a<A>(kb[(int64_t)(t0 + tt) * p.k_sn + i])) * m;
+            const int t = tok_at(p, t0 + tt);
+            const A m = token_mask(p, b, t);
+            qs[x] = phi_f(load_a<A>(qb[(int64_t)t * p.q_sn + i])) * (A)p.scale;
+            ks[x] = phi_f(load_a<A>(kb[(int64_t)t * p.k_sn + i])) * m;
         }
         for (int x = threadIdx.x; x < nt * VW; x += blockDim.x) {
             const int tt = x / VW, c = x - tt * VW;
-            const A m = token_mask(p, b, t0 + tt);
+            const int t = tok_at(p, t0 + tt);
+            const A m = token_mask(p, b, t);
             A val = 0;
-            if (c < ncols) val = load_a<A>(vb[(int64_t)(t0 + tt) * p.v_sn + j0 + c]) * m;
+            if (c < ncols) val = load_a<A>(vb[(int64_t)t * p.v_sn + j0 + c]) * m;
             else if (c == ncols) val = m;
             vs[x] = val;
         }
         for (int tt = threadIdx.x; tt < nt; tt += blockDim.x) {
-            const A m = token_mask(p, b, t0 + tt);
-            gs[tt] = m > 0 ? exp_a((A)token_log_gamma(p, b, h, t0 + tt)) : (A)1;
+            const int t = tok_at(p, t0 + tt);
+            const A m = token_mask(p, b, t);
+            gs[tt] = m > 0 ? exp_a((A)token_log_gamma(p, b, h, t)) : (A)1;
             ms[tt] = m;
         }
         __syncthreads();
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(288) scan_fwd_exact_kernel(ScanParams p, int E
             const A num = os[tt * VW + c];
             const A m = ms[tt];
             const A out = p.normalize ? num / fmax(os[tt * VW + ncols], (A)p.clamp_min) * m : num * m;
-            ob[(int64_t)(t0 + tt) * p.o_sn + j0 + c] = store_a<T, A>(out);
+            ob[(int64_t)tok_at(p, t0 + tt) * p.o_sn + j0 + c] = store_a<T, A>(out);
         }
     }
     // Final state. Every CTA read its initial state before its first barrier,
@@ -204,7 +207,8 @@ __global__ void __launch_bounds__(256) scan_bwd_exact_kernel(ScanParams p) {
     }
 
     // ---------------- pass F ----------------
-    for (int t = 0; t < p.N; ++t) {
+    for (int u = 0; u < p.N; ++u) {
+        const int t = tok_at(p, u);
         const A m = token_mask(p, b, t);
         const A g = m > 0 ? exp_a((A)token_log_gamma(p, b, h, t)) : (A)1;
         for (int i = threadIdx.x; i < d; i += blockDim.x) {
@@ -258,7 +262,8 @@ __global__ void __launch_bounds__(256) scan_bwd_exact_kernel(ScanParams p) {
     // ---------------- pass R ----------------
     for (int x = threadIdx.x; x < d * LD; x += blockDim.x) Sm[x] = 0;
     A g_next = 1, run = 0;
-    for (int t = p.N - 1; t >= 0; --t) {
+    for (int u = p.N - 1; u >= 0; --u) {
+        const int t = tok_at(p, u);
         const A m = token_mask(p, b, t);
         const A g = m > 0 ? exp_a((A)token_log_gamma(p, b, h, t)) : (A)1;
         const A zc = wzc[t];

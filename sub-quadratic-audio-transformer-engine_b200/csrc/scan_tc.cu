@@ -143,6 +143,7 @@ bool tc_supported(const ScanParams& p, int dtype) {
     if (dtype != SUBQ_BF16 && dtype != SUBQ_FP16) return false;
     if (p.d != kD || p.e != kD || p.N < 1) return false;
     if (p.flush) return false;
+    if (p.reverse && !p.normalize) return false;  // reverse time: the normalised form (the module's)
     // per-token decay runs factorised through the chunk midpoint, which needs
     // bf16's exponent range (fp16 decayed scans take the exact path)
     if (p.decay_mode != SUBQ_DECAY_NONE && dtype != SUBQ_BF16) return false;

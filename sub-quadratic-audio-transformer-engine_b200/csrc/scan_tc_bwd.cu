@@ -108,7 +108,7 @@ struct BwdParams {
     int* status;
 };
 
-template <bool kFp16, bool kNorm, bool kDecay>
+template <bool kFp16, bool kNorm, bool kDecay, bool kRev>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_constant__ BwdParams P) {
     const ScanParams& p = P.p;
     extern __shared__ uint8_t smem_raw[];
@@ -179,8 +179,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     constexpr uint32_t idKM64 = tc::idesc_f16<kFp16>(128, 64, false, true);
     constexpr uint32_t idST = tc::idesc_f16<kFp16>(64, kNorm ? kNX : 64, true, true);  // X^T [Y | 1]
 
+    // Chunks are numbered in processing order; reverse time processes the live
+    // chunks from the last one down (act maps to the chunk's place in memory),
+    // and each chunk's rows from 127 down (masks, decay scan and the d log(gamma)
+    // scan follow). Every global index below is the token's place in memory.
+    auto act = [&](int c) { return kRev ? nL - 1 - c : c; };
     auto row_mask_at = [&](int chunk, int r) -> float {
-        const int t = chunk * kC + r;
+        const int t = act(chunk) * kC + r;
         if (t >= p.N) return 0.f;
         return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
     };
@@ -217,30 +222,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
             uint8_t* base = sm + s * BL::stage;
             tc::mbar_arrive_expect_tx(&bars[B_FULL + s], (full ? 4u : 2u) * kTile);
             if (full) {
-                tc::tma_load_4d(base + BL::q, &P.tm_q, 0, chunk * kC, h, b, &bars[B_FULL + s]);
-                tc::tma_load_4d(base + BL::g, &P.tm_g, 0, chunk * kC, h, b, &bars[B_FULL + s]);
+                tc::tma_load_4d(base + BL::q, &P.tm_q, 0, act(chunk) * kC, h, b, &bars[B_FULL + s]);
+                tc::tma_load_4d(base + BL::g, &P.tm_g, 0, act(chunk) * kC, h, b, &bars[B_FULL + s]);
             }
-            tc::tma_load_4d(base + BL::k, &P.tm_k, 0, chunk * kC, hk, b, &bars[B_FULL + s]);
-            tc::tma_load_4d(base + BL::v, &P.tm_v, 0, chunk * kC, hk, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + BL::k, &P.tm_k, 0, act(chunk) * kC, hk, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + BL::v, &P.tm_v, 0, act(chunk) * kC, hk, b, &bars[B_FULL + s]);
         }
     };
     auto transform = [&](int jlo, int jhi) {
         const int r = tid - 256;
         float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
-        float a_next = (kDecay && jlo < jhi) ? decay_log2_at(p, b, h, chunk_of(jlo) * kC + r, m_next) : 0.f;
+        float a_next = (kDecay && jlo < jhi) ? decay_log2_at(p, b, h, act(chunk_of(jlo)) * kC + r, m_next) : 0.f;
         for (int j = jlo; j < jhi && ok; ++j) {
             const int s = j % kStages, u = j / kStages;
             const float m = m_next, a = a_next;
             if (j + 1 < jhi) {
                 m_next = row_mask_at(chunk_of(j + 1), r);
-                if (kDecay) a_next = decay_log2_at(p, b, h, chunk_of(j + 1) * kC + r, m_next);
+                if (kDecay) a_next = decay_log2_at(p, b, h, act(chunk_of(j + 1)) * kC + r, m_next);
             }
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
             uint8_t* base = sm + s * BL::stage;
             if constexpr (kDecay) {
                 float b63, b127;
-                const float br = decay_scan128(a, r, reinterpret_cast<float*>(sm + BL::wt), kBarTransform, b63, b127);
+                float* wt = reinterpret_cast<float*>(sm + BL::wt);
+                const float br = kRev ? decay_scan128_rev(a, r, wt, kBarTransform, b63, b127)
+                                      : decay_scan128(a, r, wt, kBarTransform, b63, b127);
                 float* dc = dec + s * (BL::decs / 4);
                 dc[r] = br;
                 if (r == 0) {
@@ -270,6 +277,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     // columns (this thread's half of its row), after every thread's fp32 reads.
     // keep_upper: keep col >= row (key-major tiles), else col <= row (query-major).
     auto mask_to_bf16 = [&](uint32_t tcol, bool keep_upper) {
+        keep_upper = keep_upper != kRev;  // reverse time: the other triangle
         uint32_t packed[32];
         const bool zero = keep_upper ? (hf == 0 && quad >= 2) : (hf == 1 && quad < 2);
         if (zero) {
@@ -742,7 +750,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                     float c8[8] = {ct, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                     store_chunk<kFp16>(sm + BL::ca, row, 0, c8);
                 }
-                if (c * kC + row < p.N) wsz[c * kC + row] = make_float2(zc, ct);
+                if (act(c) * kC + row < p.N) wsz[act(c) * kC + row] = make_float2(zc, ct);
             }
             publish(&bars[B_OCDONE]);  // also: every thread has read dxs, [N | Z] and dO
             // (3) dA: causal mask, bf16 in place
@@ -779,10 +787,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 tc::bar_sync(kBarCompute, kComputeThreads);
                 if (tid == 0) {
                     tc::mbar_arrive(&bars[B_DQDONE]);  // dQ~ columns read
-                    tc::tma_store_4d(&P.tm_dq, dst, 0, c * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dq, dst, 0, act(c) * kC, h, b);
                     tc::bulk_commit();
                 }
-                if (want_dlg && hf == 0 && c * kC + row < p.N) wgq[c * kC + row] = p.scale * (dxs[row] + dxs[128 + row]);
+                if (want_dlg && hf == 0 && act(c) * kC + row < p.N)
+                    wgq[act(c) * kC + row] = p.scale * (dxs[row] + dxs[128 + row]);
             }
             if constexpr (kDecay) {
                 // X += exp(B_c - B_seg) exp(b_m) W'_c, W'_c = q'^T [o^ | c] of this chunk
@@ -915,10 +924,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     } else if (warp < 8) {
         // mask and (Zc, c) of a chunk's row, fetched one chunk ahead
         auto fetch = [&](int cc, float& m_, float2& z_, float& gq_) {
-            const bool in = cc * kC + row < p.N;
+            const int t = act(cc) * kC + row;
+            const bool in = t < p.N;
             m_ = row_mask_at(cc, row);
-            z_ = in ? wsz[cc * kC + row] : make_float2(1.f, 0.f);
-            if (want_dlg) gq_ = in ? wgq[cc * kC + row] : 0.f;
+            z_ = in ? wsz[t] : make_float2(1.f, 0.f);
+            if (want_dlg) gq_ = in ? wgq[t] : 0.f;
         };
         float m_cur = 0.f, gq_cur = 0.f;
         float2 zcc_cur = make_float2(1.f, 0.f);
@@ -1025,26 +1035,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 tc::bar_sync(kBarCompute, kComputeThreads);
                 if (tid == 0) {
                     tc::mbar_arrive(&bars[B_KVDONE]);  // dK / dV columns read
-                    tc::tma_store_4d(&P.tm_dk, dst, 0, c * kC, h, b);
-                    tc::tma_store_4d(&P.tm_dv, sm + BL::ob, 0, c * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dk, dst, 0, act(c) * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dv, sm + BL::ob, 0, act(c) * kC, h, b);
                     tc::bulk_commit();
                 }
                 if (want_dlg) {
                     // g_t = s q~.dQ~ - s k~.dK~; d log(gamma_t) = m_t sum_{t' >= t} g_t'
                     // (reverse scan: lanes within the quad's 32 rows, then the quads, then
                     // the later chunks of the segment; later segments are added at the end)
+                    // (reverse time: the rows after t in processing order are the rows
+                    // before it in the chunk, so the scan runs the other way)
                     float x = gq - p.scale * (dxs[row] + dxs[128 + row]);
 #pragma unroll
                     for (int o = 1; o < 32; o <<= 1) {
-                        const float y = __shfl_down_sync(0xffffffffu, x, o);
-                        if (lane + o < 32) x += y;
+                        const float y = kRev ? __shfl_up_sync(0xffffffffu, x, o) : __shfl_down_sync(0xffffffffu, x, o);
+                        if (kRev ? lane >= o : lane + o < 32) x += y;
                     }
-                    const float qtot = __shfl_sync(0xffffffffu, x, 0);
+                    const float qtot = __shfl_sync(0xffffffffu, x, kRev ? 31 : 0);
                     if (hf == 0 && lane == 0) misc[4 + quad] = qtot;
                     tc::bar_sync(kBarCompute, kComputeThreads);
                     float later = dlg_carry;
-                    for (int qq = quad + 1; qq < 4; ++qq) later += misc[4 + qq];
-                    if (hf == 0 && c * kC + row < p.N) p.dlg[(int64_t)bh * p.N + c * kC + row] = m * (x + later);
+                    for (int qq = kRev ? 0 : quad + 1; qq < (kRev ? quad : 4); ++qq) later += misc[4 + qq];
+                    const int t = act(c) * kC + row;
+                    if (hf == 0 && t < p.N) p.dlg[(int64_t)bh * p.N + t] = m * (x + later);
                     dlg_carry += misc[4] + misc[5] + misc[6] + misc[7];
                 }
             } else {
@@ -1069,8 +1082,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 tc::bar_sync(kBarCompute, kComputeThreads);
                 if (tid == 0) {
                     tc::mbar_arrive(&bars[B_KVDONE]);  // dK / dV columns read
-                    tc::tma_store_4d(&P.tm_dk, dst, 0, c * kC, h, b);
-                    tc::tma_store_4d(&P.tm_dv, sm + BL::ob, 0, c * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dk, dst, 0, act(c) * kC, h, b);
+                    tc::tma_store_4d(&P.tm_dv, sm + BL::ob, 0, act(c) * kC, h, b);
                     tc::bulk_commit();
                 }
             }
@@ -1108,9 +1121,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
         cluster.sync();  // remote reads done
         if (warp < 8 && n > 0 && ok && off != 0.f) {
             float* dl = p.dlg + (int64_t)bh * p.N;
-            const int t1 = min(p.N, (c_begin + n) * kC);
-            for (int t = c_begin * kC + tid; t < t1; t += kComputeThreads)
-                if (row_mask_at(t / kC, t % kC) != 0.f) dl[t] += off;
+            const int c0 = kRev ? nL - c_begin - n : c_begin;  // the segment's chunks in memory
+            const int t1 = min(p.N, (c0 + n) * kC);
+            for (int t = c0 * kC + tid; t < t1; t += kComputeThreads)
+                if (!p.mask || p.mask[(int64_t)b * p.mask_sb + t]) dl[t] += off;
         }
     }
     tc::tc_fence_before();
@@ -1118,7 +1132,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     if (warp == kWarpMma) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
-template <bool kFp16, bool kNorm, bool kDecay>
+template <bool kFp16, bool kNorm, bool kDecay, bool kRev = false>
 cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     BwdParams P;
     memset(&P, 0, sizeof(P));
@@ -1135,7 +1149,7 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     const int nC = (p.N + kC - 1) / kC;
     P.status = status_ptr();
     if (!P.status) return cudaErrorInvalidDevice;
-    const void* kern = reinterpret_cast<const void*>(&bwd_kernel<kFp16, kNorm, kDecay>);
+    const void* kern = reinterpret_cast<const void*>(&bwd_kernel<kFp16, kNorm, kDecay, kRev>);
     P.G = pick_segments(p, kern, kBwdThreads, BL::total + 1024);
     P.cps = (nC + P.G - 1) / P.G;
     void* args[] = {&P};
@@ -1145,6 +1159,14 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_bwd_v2(const ScanParams& p, int dtype, cudaStream_t st) {
+    if (p.reverse) {  // reverse time: normalised form only
+        if (!p.normalize) return cudaErrorInvalidValue;
+        if (p.decay_mode != SUBQ_DECAY_NONE) {
+            if (dtype != SUBQ_BF16 || !p.fallback) return cudaErrorInvalidValue;
+            return launch<false, true, true, true>(p, st);
+        }
+        return dtype == SUBQ_FP16 ? launch<true, true, false, true>(p, st) : launch<false, true, false, true>(p, st);
+    }
     if (p.decay_mode != SUBQ_DECAY_NONE) {  // bf16 only (the factorised decay needs its exponent range)
         if (dtype != SUBQ_BF16 || !p.fallback) return cudaErrorInvalidValue;
         return p.normalize ? launch<false, true, true>(p, st) : launch<false, false, true>(p, st);

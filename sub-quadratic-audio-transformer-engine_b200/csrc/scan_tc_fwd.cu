@@ -102,7 +102,7 @@ struct FwdParams {
     int* status;
 };
 
-template <bool kFp16, bool kNorm, bool kDecay>
+template <bool kFp16, bool kNorm, bool kDecay, bool kRev>
 __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_constant__ FwdParams P) {
     const ScanParams& p = P.p;
     extern __shared__ uint8_t smem_raw[];
@@ -158,8 +158,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     constexpr uint32_t idO = tc::idesc_f16<kFp16>(128, 64, false, true);    // P V
     constexpr uint32_t idSX = tc::idesc_f16<kFp16>(64, kNX, true, true);    // phi~(K)^T [V | 1]
 
+    // Chunks are numbered in processing order; reverse time processes the live
+    // chunks from the last one down (act maps to the chunk's place in memory),
+    // and each chunk's rows from 127 down (the mask and decay scan follow).
+    auto act = [&](int c) { return kRev ? nL - 1 - c : c; };
     auto row_mask_at = [&](int chunk, int r) -> float {
-        const int t = chunk * kC + r;
+        const int t = act(chunk) * kC + r;
         if (t >= p.N) return 0.f;
         return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
     };
@@ -196,29 +200,31 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             if (!ok) break;
             uint8_t* base = sm + s * L::stage;
             tc::mbar_arrive_expect_tx(&bars[B_FULL + s], (ph2 ? 3u : 2u) * kTile);
-            if (ph2) tc::tma_load_4d(base + L::q, &P.tm_q, 0, chunk * kC, h, b, &bars[B_FULL + s]);
-            tc::tma_load_4d(base + L::k, &P.tm_k, 0, chunk * kC, hk, b, &bars[B_FULL + s]);
-            tc::tma_load_4d(base + L::v, &P.tm_v, 0, chunk * kC, hk, b, &bars[B_FULL + s]);
+            if (ph2) tc::tma_load_4d(base + L::q, &P.tm_q, 0, act(chunk) * kC, h, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + L::k, &P.tm_k, 0, act(chunk) * kC, hk, b, &bars[B_FULL + s]);
+            tc::tma_load_4d(base + L::v, &P.tm_v, 0, act(chunk) * kC, hk, b, &bars[B_FULL + s]);
         }
     };
     auto transform = [&](int jlo, int jhi) {
         const int r = tid - 256;
         float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
-        float a_next = (kDecay && jlo < jhi) ? decay_log2_at(p, b, h, chunk_of(jlo) * kC + r, m_next) : 0.f;
+        float a_next = (kDecay && jlo < jhi) ? decay_log2_at(p, b, h, act(chunk_of(jlo)) * kC + r, m_next) : 0.f;
         for (int j = jlo; j < jhi && ok; ++j) {
             const bool ph2 = j >= n1;
             const int s = j % kStages, u = j / kStages;
             const float m = m_next, a = a_next;
             if (j + 1 < jhi) {  // in flight during the wait
                 m_next = row_mask_at(chunk_of(j + 1), r);
-                if (kDecay) a_next = decay_log2_at(p, b, h, chunk_of(j + 1) * kC + r, m_next);
+                if (kDecay) a_next = decay_log2_at(p, b, h, act(chunk_of(j + 1)) * kC + r, m_next);
             }
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
             uint8_t* base = sm + s * L::stage;
             if constexpr (kDecay) {
                 float b63, b127;
-                const float br = decay_scan128(a, r, reinterpret_cast<float*>(sm + L::wt), kBarTransform, b63, b127);
+                float* wt = reinterpret_cast<float*>(sm + L::wt);
+                const float br = kRev ? decay_scan128_rev(a, r, wt, kBarTransform, b63, b127)
+                                      : decay_scan128(a, r, wt, kBarTransform, b63, b127);
                 if (r == 0) {
                     dec[2 * s] = b63;
                     dec[2 * s + 1] = b127;
@@ -513,7 +519,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             tc::tc_fence_after();
             using E = Elem<kFp16>;
             uint32_t packed[32];
-            if (hf == 1 && quad < 2) {
+            // causal: keep tau <= t (the block right of the diagonal blocks is zero);
+            // reverse: keep tau >= t (the block left of them is zero)
+            if (kRev ? (hf == 0 && quad >= 2) : (hf == 1 && quad < 2)) {
 #pragma unroll
                 for (int x = 0; x < 32; ++x) packed[x] = 0u;
             } else if (kDecay) {  // 32 columns at a time: the decayed state occupies 33 registers
@@ -524,7 +532,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                     tc::tmem_ld32(tmem + cP + bf * 128 + loff + hf * 64 + part * 32, v);
 #pragma unroll
                     for (int x = 0; x < 32; ++x)
-                        if (diag && (hf * 64 + part * 32 + x) > row) v[x] = 0.f;
+                        if (diag && (kRev ? (hf * 64 + part * 32 + x) < row : (hf * 64 + part * 32 + x) > row)) v[x] = 0.f;
 #pragma unroll
                     for (int x = 0; x < 16; ++x) {
                         typename E::T2 h2 = E::from2(v[2 * x], v[2 * x + 1]);
@@ -538,7 +546,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 tc::tmem_ld32(tmem + cP + bf * 128 + loff + hf * 64 + 32, v + 32);
 #pragma unroll
                 for (int x = 0; x < 64; ++x)
-                    if (diag && (hf * 64 + x) > row) v[x] = 0.f;
+                    if (diag && (kRev ? (hf * 64 + x) < row : (hf * 64 + x) > row)) v[x] = 0.f;
 #pragma unroll
                 for (int x = 0; x < 32; ++x) {
                     typename E::T2 h2 = E::from2(v[2 * x], v[2 * x + 1]);
@@ -663,7 +671,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             tc::fence_proxy_async();
             tc::bar_sync(kBarCompute, kComputeThreads);
             if (tid == 0) {
-                tc::tma_store_4d(&P.tm_o, sm + L::os, 0, c * kC, h, b);
+                tc::tma_store_4d(&P.tm_o, sm + L::os, 0, act(c) * kC, h, b);
                 tc::bulk_commit();
             }
         }
@@ -705,7 +713,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     if (warp == kWarpMma) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
-template <bool kFp16, bool kNorm, bool kDecay>
+template <bool kFp16, bool kNorm, bool kDecay, bool kRev = false>
 cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     FwdParams P;
     memset(&P, 0, sizeof(P));
@@ -719,7 +727,7 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     const int nC = (p.N + kC - 1) / kC;
     P.status = status_ptr();
     if (!P.status) return cudaErrorInvalidDevice;
-    const void* kern = reinterpret_cast<const void*>(&fwd_kernel<kFp16, kNorm, kDecay>);
+    const void* kern = reinterpret_cast<const void*>(&fwd_kernel<kFp16, kNorm, kDecay, kRev>);
     P.G = pick_segments(p, kern, kFwdThreads, L::total + 1024);
     P.cps = (nC + P.G - 1) / P.G;
     void* args[] = {&P};
@@ -729,6 +737,14 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_fwd_v2(const ScanParams& p, int dtype, cudaStream_t st) {
+    if (p.reverse) {  // reverse time: normalised form only
+        if (!p.normalize) return cudaErrorInvalidValue;
+        if (p.decay_mode != SUBQ_DECAY_NONE) {
+            if (dtype != SUBQ_BF16 || !p.fallback) return cudaErrorInvalidValue;
+            return launch<false, true, true, true>(p, st);
+        }
+        return dtype == SUBQ_FP16 ? launch<true, true, false, true>(p, st) : launch<false, true, false, true>(p, st);
+    }
     if (p.decay_mode != SUBQ_DECAY_NONE) {  // bf16 only (the factorised decay needs its exponent range)
         if (dtype != SUBQ_BF16 || !p.fallback) return cudaErrorInvalidValue;
         return p.normalize ? launch<false, true, true>(p, st) : launch<false, false, true>(p, st);

@@ -305,6 +305,28 @@ __device__ __forceinline__ float decay_scan128(float a, int r, float* wt, int ba
     return w == 0 ? x : x + pre;
 }
 
+// Reverse-time counterpart: the tokens are processed from row 127 down to
+// row 0, so the prefix in processing order is B'_r = sum over rows r' >= r.
+// bmid = B'_64 (the midpoint in processing order) and bend = B'_0 are summed
+// in the same order as rows 64 and 0 reproduce them.
+__device__ __forceinline__ float decay_scan128_rev(float a, int r, float* wt, int bar_id, float& bmid, float& bend) {
+    const int lane = r & 31, w = r >> 5;
+    float x = a;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_down_sync(0xffffffffu, x, o);
+        if (lane + o < 32) x += y;
+    }
+    if (lane == 0) wt[w] = x;
+    tc::bar_sync(bar_id, 128);
+    const float w1 = wt[1], w2 = wt[2], w3 = wt[3];
+    const float s23 = w2 + w3, s123 = w1 + s23;
+    bmid = s23;
+    bend = wt[0] + s123;
+    const float pre = w == 3 ? 0.f : w == 2 ? w3 : w == 1 ? s23 : s123;
+    return w == 3 ? x : x + pre;
+}
+
 // Whether both halves of a chunk stay within the factorisation's range (NaN
 // decay passes and propagates like the reference's).
 __device__ __forceinline__ bool decay_in_range(float b63, float b127) {

@@ -47,7 +47,7 @@ class ScanDesc(ctypes.Structure):
         ("decay_mode", ctypes.c_int32), ("log_gamma_scalar", ctypes.c_float),
         ("log_gamma", ctypes.c_void_p), ("mask", ctypes.c_void_p), ("mask_stride_b", ctypes.c_int64),
         ("flush_subnormal", ctypes.c_int32), ("path", ctypes.c_int32),
-        ("kv_heads", ctypes.c_int64),
+        ("kv_heads", ctypes.c_int64), ("reverse", ctypes.c_int32),
     ]
 
 

@@ -136,12 +136,15 @@ def _split_state(past_state: StateLike):
 
 
 class _CausalScan(torch.autograd.Function):
-    """One causal scan direction on the kernels; differentiable in q, k, v, log_gamma."""
+    """One scan direction on the kernels (causal, or reverse time for the
+    second direction of the bidirectional scan); differentiable in q, k, v,
+    log_gamma."""
 
     @staticmethod
-    def forward(ctx, q, k, v, lg, mask_u8, state, want_state):
+    def forward(ctx, q, k, v, lg, mask_u8, state, want_state, reverse=False):
         o, st = ops.scan_forward(q, k, v, log_gamma=lg, mask=mask_u8, normalize=True, state=state,
-                                 return_state=want_state)
+                                 return_state=want_state, reverse=reverse)
+        ctx.reverse = reverse
         ctx.save_for_backward(q, k, v, lg if isinstance(lg, torch.Tensor) else None, mask_u8)
         ctx.lg_is_tensor = isinstance(lg, torch.Tensor)
         ctx.state = state
@@ -155,7 +158,8 @@ class _CausalScan(torch.autograd.Function):
         q, k, v, lg, mask_u8 = ctx.saved_tensors
         need_lg = ctx.lg_is_tensor and ctx.needs_input_grad[3]
         dq, dk, dv, dlg = ops.scan_backward(q, k, v, do.contiguous(), log_gamma=lg, mask=mask_u8,
-                                            normalize=True, state=ctx.state, need_dlog_gamma=need_lg)
+                                            normalize=True, state=ctx.state, need_dlog_gamma=need_lg,
+                                            reverse=ctx.reverse)
         glg = None
         if need_lg:
             glg = dlg.to(lg.dtype)
@@ -163,7 +167,7 @@ class _CausalScan(torch.autograd.Function):
                 glg = glg.sum()
             elif lg.dim() == 1:
                 glg = glg.sum(dim=(0, 2))
-        return dq, dk, dv, glg, None, None, None
+        return dq, dk, dv, glg, None, None, None, None
 
 
 def _to_device_inputs(q, k, v):
@@ -175,7 +179,7 @@ def _to_device_inputs(q, k, v):
     return q.to(dev), k.to(dev), v.to(dev), q.device
 
 
-def _single_direction(q, k, v, decay_w, past_state, valid_mask, want_state):
+def _single_direction(q, k, v, decay_w, past_state, valid_mask, want_state, reverse=False):
     B, H, T, D = q.shape
     lg = _log_gamma(decay_w, B, H, T, q.device)
     mask_u8 = _token_mask(valid_mask, B, T, q.device)
@@ -185,7 +189,7 @@ def _single_direction(q, k, v, decay_w, past_state, valid_mask, want_state):
         S = S.to(device=q.device, dtype=torch.float32)
         Z = None if Z is None else Z.to(device=q.device, dtype=torch.float32).reshape(B, H, D)
         st = (S, Z)
-    o, S_next, z_next = _CausalScan.apply(q, k, v, lg, mask_u8, st, want_state)
+    o, S_next, z_next = _CausalScan.apply(q, k, v, lg, mask_u8, st, want_state, reverse)
     return o, S_next, z_next
 
 
@@ -208,15 +212,14 @@ def chunkwise_flash_linear_attention(q: torch.Tensor, k: torch.Tensor, v: torch.
         attention_mask.to(q.device) if attention_mask is not None else None, q.dtype, T)
     out, S_next, z_next = _single_direction(q, k, v, decay_w, past_state, valid_mask, True)
     if not is_causal:
-        # Bidirectional: add the reversed-time scan and remove the double-counted
-        # diagonal (in normalised linear attention the self term is v).
-        flip = lambda x: torch.flip(x, dims=[2])  # noqa: E731
-        w_rev = torch.flip(decay_w, dims=[-1]) if isinstance(decay_w, torch.Tensor) and decay_w.ndim >= 2 else decay_w
-        vm_rev = torch.flip(valid_mask, dims=[2]) if valid_mask is not None else None
-        out_b, _, _ = _single_direction(flip(q), flip(k), flip(v), w_rev, None, vm_rev, False)
+        # Bidirectional: add the reverse-time scan and remove the double-counted
+        # diagonal (in normalised linear attention the self term is v). The
+        # kernels run the reverse direction in place of the reference's scan of
+        # time-flipped copies (the same decay between tokens, no copies).
+        out_b, _, _ = _single_direction(q, k, v, decay_w, None, valid_mask, False, reverse=True)
         vq = v if v.shape[1] == q.shape[1] else v.repeat_interleave(q.shape[1] // v.shape[1], dim=1)
         diag = vq if valid_mask is None else vq * valid_mask.expand_as(vq)
-        out = out + flip(out_b) - diag
+        out = out + out_b - diag
         if valid_mask is not None:
             out = out * valid_mask.expand_as(out)
     S_next = S_next.to(q.device)
@@ -246,12 +249,12 @@ def _reduce_dw(dlg: torch.Tensor, w: torch.Tensor, B: int, H: int, T: int) -> to
     return dlg.sum()
 
 
-def _direction_grads(q, k, v, w, do, valid_mask):
+def _direction_grads(q, k, v, w, do, valid_mask, reverse=False):
     B, H, T, D = q.shape
     lg = None if w is None else _log_gamma(w.detach(), B, H, T, q.device)
     mask_u8 = _token_mask(valid_mask, B, T, q.device)
     dq, dk, dv, dlg = ops.scan_backward(q, k, v, do.contiguous(), log_gamma=lg, mask=mask_u8, normalize=True,
-                                        need_dlog_gamma=w is not None)
+                                        need_dlog_gamma=w is not None, reverse=reverse)
     dw = None if w is None else _reduce_dw(dlg, w, B, H, T)
     return dq, dk, dv, dw
 
@@ -298,17 +301,14 @@ class SubQAttentionFunction(torch.autograd.Function):
         w_dev = None if ctx.decay_none else w.to(q4.device)
         vm = ctx.valid_mask.to(q4.device) if ctx.valid_mask is not None else None
         dQ, dK, dV, dw = _direction_grads(q4, k4, v4, w_dev, g4, vm)
-        if not ctx.is_causal:
-            flip = lambda x: torch.flip(x, dims=[2])  # noqa: E731
-            w_rev = (torch.flip(w_dev, dims=[-1]) if w_dev is not None and w_dev.ndim >= 2 else w_dev)
-            vm_rev = flip(vm) if vm is not None else None
-            dQb, dKb, dVb, dwb = _direction_grads(flip(q4), flip(k4), flip(v4), w_rev, flip(g4), vm_rev)
+        if not ctx.is_causal:  # the reverse-time direction (reference: on time-flipped copies)
+            dQb, dKb, dVb, dwb = _direction_grads(q4, k4, v4, w_dev, g4, vm, reverse=True)
             g_m = g4 if vm is None else g4 * vm.expand_as(g4)
-            dQ = dQ + flip(dQb)
-            dK = dK + flip(dKb)
-            dV = dV + flip(dVb) - g_m
+            dQ = dQ + dQb
+            dK = dK + dKb
+            dV = dV + dVb - g_m
             if dw is not None:
-                dw = dw + (torch.flip(dwb, dims=[-1]) if w_dev.ndim >= 2 else dwb)
+                dw = dw + dwb
         if ctx.is_3d:
             dQ, dK, dV = dQ.squeeze(1), dK.squeeze(1), dV.squeeze(1)
         dw_out = None if dw is None else dw.to(w.dtype).reshape(w.shape)

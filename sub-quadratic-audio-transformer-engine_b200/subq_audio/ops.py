@@ -54,11 +54,12 @@ def _check_kv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
 
 def _desc(q: torch.Tensor, v: torch.Tensor, log_gamma: LogGamma, mask: Optional[torch.Tensor],
           normalize: bool, scale: Optional[float], clamp_min: float, flush_subnormal: bool,
-          path: str, keep: list) -> _capi.ScanDesc:
+          path: str, keep: list, reverse: bool = False) -> _capi.ScanDesc:
     B, H, N, d = q.shape
     desc = _capi.ScanDesc()
     desc.batch, desc.heads, desc.seq_len, desc.head_dim, desc.value_dim = B, H, N, d, v.shape[-1]
     desc.kv_heads = v.shape[1] if v.shape[1] != H else 0  # grouped K/V (GQA)
+    desc.reverse = 1 if reverse else 0
     if q.dtype not in _DTYPES:
         raise TypeError(f"unsupported dtype {q.dtype}; use float32, float16, bfloat16 or float64")
     desc.dtype = _DTYPES[q.dtype]
@@ -116,11 +117,12 @@ def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma
                  mask: Optional[torch.Tensor] = None, normalize: bool = True, scale: Optional[float] = None,
                  clamp_min: float = 1e-5, state: Optional[Tuple[torch.Tensor, Optional[torch.Tensor]]] = None,
                  return_state: bool = False, flush_subnormal: bool = False, path: str = "auto",
-                 out: Optional[torch.Tensor] = None):
+                 out: Optional[torch.Tensor] = None, reverse: bool = False):
     """Causal scan. Returns ``(o, (S, z) | None)``; S [B,H,d,e] and z [B,H,d] are float32.
     ``k`` and ``v`` may have fewer heads than ``q`` (a divisor of H: grouped K/V,
     query head h reading K/V head h // (H // Hkv)); the backward then returns
-    dk, dv summed over each group."""
+    dk, dv summed over each group. ``reverse=True`` scans in reverse time
+    (token t sees itself and the later tokens; the state runs from the end)."""
     _require_cuda(q, k, v)
     q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
     _check_kv(q, k, v)
@@ -132,7 +134,7 @@ def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma
     with torch.cuda.device(q.device):
         o = out if out is not None else torch.empty((B, H, N, e), dtype=q.dtype, device=q.device)
         a = _capi.FwdArgs()
-        a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep)
+        a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep, reverse)
         a.q, a.k, a.v, a.o = _t4(q), _t4(k), _t4(v), _t4(o)
         S_out = z_out = None
         if state is not None:
@@ -160,7 +162,8 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
                   log_gamma: LogGamma = None, mask: Optional[torch.Tensor] = None, normalize: bool = True,
                   scale: Optional[float] = None, clamp_min: float = 1e-5,
                   state: Optional[Tuple[torch.Tensor, Optional[torch.Tensor]]] = None,
-                  need_dlog_gamma: bool = False, flush_subnormal: bool = False, path: str = "auto"):
+                  need_dlog_gamma: bool = False, flush_subnormal: bool = False, path: str = "auto",
+                  reverse: bool = False):
     """Gradients of ``scan_forward``. Returns ``(dq, dk, dv, dlog_gamma | None)``;
     dlog_gamma is float32 [B,H,N] (d loss / d log gamma_t per token)."""
     _require_cuda(q, k, v, dout)
@@ -176,7 +179,7 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
         dk = torch.empty(k.shape, dtype=q.dtype, device=q.device)  # [B, Hkv, N, d]: summed per K/V group
         dv = torch.empty(v.shape, dtype=q.dtype, device=q.device)
         a = _capi.BwdArgs()
-        a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep)
+        a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep, reverse)
         a.q, a.k, a.v, a.dout = _t4(q), _t4(k), _t4(v), _t4(dout)
         a.dq, a.dk, a.dv = _t4(dq), _t4(dk), _t4(dv)
         if state is not None:
