@@ -325,13 +325,17 @@ int subq_device_info(int device, char* arch, size_t arch_len, size_t* memory_byt
 // scratch buffer that is part of this library's static device memory, placed
 // when the module loads, so the call itself allocates nothing.
 //
-//  * Capacity: kNoAllocScratchBytes = 8 MiB, enough for 1,048,576 token-heads
-//    (B x H x N) on the tensor-core path (8 bytes each) and 699,050 on the
-//    float32 exact path (12 bytes each). A larger call is rejected with
+//  * Capacity: kNoAllocScratchBytes = 8 MiB against subq_bwd_workspace_bytes:
+//    1,048,576 token-heads (B x H x N) on the tensor-core path (8 bytes each),
+//    about 699,000 with per-token decay (12 bytes each plus a flag per
+//    sequence) and on the float32 exact path (12 bytes each); grouped K/V adds
+//    dK and dV per query head. A larger call is rejected with
 //    SUBQ_ERR_WORKSPACE before anything is launched.
-//  * Nothing in the scratch has to start at zero: every call writes each
-//    per-token entry it later reads (the clamped normaliser and the quotient
-//    coefficient, or the exact path's per-token values) before reading it.
+//  * Nothing in the scratch has to start at zero when the call begins: every
+//    call writes each per-token entry it later reads (the clamped normaliser
+//    and the quotient coefficient, or the exact path's per-token values)
+//    before reading it, and the decayed path clears its per-sequence fallback
+//    flags itself (a memset on the call's stream, not an allocation).
 //  * One buffer per device: calls that overlap in time on one device (two
 //    streams, or host threads without ordering between them) race on it, so
 //    such callers must serialise their calls.

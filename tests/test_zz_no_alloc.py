@@ -22,19 +22,24 @@ def _case(B, H, N, d, dtype, seed):
     return q, k, v, do, mask
 
 
-def _noalloc_backward(q, k, v, do, mask):
-    """One subq_bwd_noalloc call: the caller provides inputs and outputs only."""
+def _noalloc_backward(q, k, v, do, mask, log_gamma=None):
+    """One subq_bwd_noalloc call: the caller provides inputs and outputs only
+    (with a per-token decay also the d log(gamma) output, returned last)."""
     B, H, N, d = q.shape
     keep = []
     dq, dk, dv = (torch.empty_like(q) for _ in range(3))
     a = _capi.BwdArgs()
-    a.desc = ops._desc(q, v, None, mask, True, None, 1e-5, False, "auto", keep)
+    a.desc = ops._desc(q, v, log_gamma, mask, True, None, 1e-5, False, "auto", keep)
+    dlg = None
+    if log_gamma is not None:
+        dlg = torch.empty(B, H, N, dtype=torch.float32, device=q.device)
+        a.dlog_gamma = dlg.data_ptr()
     a.q, a.k, a.v, a.dout = ops._t4(q), ops._t4(k), ops._t4(v), ops._t4(do)
     a.dq, a.dk, a.dv = ops._t4(dq), ops._t4(dk), ops._t4(dv)
     a.stream = torch.cuda.current_stream().cuda_stream
     a.workspace, a.workspace_bytes = None, 0
     _capi.bwd_noalloc(a)
-    return dq, dk, dv
+    return (dq, dk, dv) if log_gamma is None else (dq, dk, dv, dlg)
 
 
 @pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 64), (torch.float32, 16)])
@@ -46,6 +51,25 @@ def test_noalloc_backward_equals_subq_bwd_twice(dtype, d):
         got = _noalloc_backward(q, k, v, do, mask)
         torch.cuda.synchronize()
         assert ops.last_path() == path
+        for x, y in zip(got, ref):
+            assert torch.equal(x, y)
+
+
+def test_noalloc_backward_with_decay_equals_subq_bwd_twice():
+    """Per-token decay on the tensor-core path keeps its per-sequence fallback
+    flags in the same static scratch (cleared by each call); one sequence
+    decays strongly enough to take the exact fallback."""
+    q, k, v, do, mask = _case(2, 3, 1200, 64, torch.bfloat16, seed=29)
+    g = torch.Generator().manual_seed(30)
+    lg = -torch.nn.functional.softplus(-(torch.randn(2, 3, 1200, generator=g) + 3.0))
+    lg[1, 0, 200:700] = math.log(0.1)
+    lg = lg.cuda()
+    ref = ops.scan_backward(q, k, v, do, mask=mask, log_gamma=lg, need_dlog_gamma=True)
+    assert ops.last_path() == "tensorcore"
+    for _ in range(2):
+        got = _noalloc_backward(q, k, v, do, mask, log_gamma=lg)
+        torch.cuda.synchronize()
+        assert ops.last_path() == "tensorcore"
         for x, y in zip(got, ref):
             assert torch.equal(x, y)
 
