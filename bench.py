@@ -4,7 +4,9 @@ Workload (per GPU): B=8, H=8, N=8192, d_head=64, bfloat16 inputs with float32
 accumulation; Q, K, V, dO ~ N(0,1) from a seed; a key-padding mask with
 per-sequence valid lengths drawn uniform in [N/2, N]; gamma == 1 (the plain
 normaliser form phi(q)S/(phi(q)z), clamp 1e-5). One step = one forward and
-one backward scan over the batch. Inputs (268 MB) exceed the 126 MB L2.
+one backward scan over the batch, the forward handing its segment-start
+states to the backward as a training step does. Inputs (268 MB) exceed the
+126 MB L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -482,9 +484,11 @@ def main():
     stream = torch.cuda.current_stream(dev)
 
     def step(qq, kk, vv, dd, mm):
-        o, _ = ops.scan_forward(qq, kk, vv, mask=mm, normalize=True, path=args.path)
+        # as in training: the forward hands its segment-start states to the backward
+        seg = ops.SegmentStates()
+        o, _ = ops.scan_forward(qq, kk, vv, mask=mm, normalize=True, path=args.path, segments=seg)
         n_f = ops.last_launches()
-        dq, dk, dv, _ = ops.scan_backward(qq, kk, vv, dd, mask=mm, normalize=True, path=args.path)
+        dq, dk, dv, _ = ops.scan_backward(qq, kk, vv, dd, mask=mm, normalize=True, path=args.path, segments=seg)
         return (o, dq, dk, dv), n_f + ops.last_launches()
 
     def barrier():
@@ -524,11 +528,12 @@ def main():
     fe = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     reps = max(3, min(args.steps, 10))
     fe[0].record(stream)
+    seg = ops.SegmentStates()
     for _ in range(reps):
-        ops.scan_forward(qd, kd, vd, mask=md, normalize=True, path=args.path)
+        ops.scan_forward(qd, kd, vd, mask=md, normalize=True, path=args.path, segments=seg)
     fe[1].record(stream)
     for _ in range(reps):
-        ops.scan_backward(qd, kd, vd, dod, mask=md, normalize=True, path=args.path)
+        ops.scan_backward(qd, kd, vd, dod, mask=md, normalize=True, path=args.path, segments=seg)
     fe[2].record(stream)
     torch.cuda.synchronize(dev)
     fwd_ms = fe[0].elapsed_time(fe[1]) / reps

@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define SUBQ_ABI_VERSION 2
+#define SUBQ_ABI_VERSION 3
 
 typedef enum subq_status {
     SUBQ_OK = 0,
@@ -127,6 +127,12 @@ typedef struct subq_fwd_args {
     void* workspace;
     size_t workspace_bytes;
     void* stream;           /* cudaStream_t */
+    /* Optional (NULL = not wanted): receives the state at the start of each
+     * segment of each sequence as the tensor-core forward computes it,
+     * subq_segment_states_bytes(args) bytes. Passing the same buffer to the
+     * backward of the same call spares it recomputing those states (the
+     * reference's backward recomputes them, autograd.py:207-222). */
+    float* segment_states;
 } subq_fwd_args;
 
 typedef struct subq_bwd_args {
@@ -139,6 +145,9 @@ typedef struct subq_bwd_args {
     void* workspace;
     size_t workspace_bytes;
     void* stream;
+    /* Optional: the segment_states buffer the forward of the same inputs
+     * filled; used when it matches this call's segment split, else ignored. */
+    const float* segment_states;
 } subq_bwd_args;
 
 /* Forward scan. Replaces run_attention_forward / the torch chunked forward. */
@@ -151,6 +160,9 @@ int subq_bwd(const subq_bwd_args* args);
 /* Bytes of `workspace` the call needs (0 is possible). */
 size_t subq_fwd_workspace_bytes(const subq_fwd_args* args);
 size_t subq_bwd_workspace_bytes(const subq_bwd_args* args);
+/* Bytes of the forward's optional segment_states buffer (0: the call would
+ * not fill one, e.g. on the exact path). */
+size_t subq_segment_states_bytes(const subq_fwd_args* args);
 
 /* In-place phi(x) = ELU(x) + 1 over n contiguous elements (run_feature_map). */
 int subq_feature_map(void* x, int64_t n, int32_t dtype, void* stream);

@@ -113,6 +113,7 @@ int fill_fwd(const subq_fwd_args* a, subq::ScanParams& p) {
     p.o = a->o.data; p.o_sb = a->o.stride_b; p.o_sh = a->o.stride_h; p.o_sn = a->o.stride_n;
     p.S_in = a->state_in; p.z_in = a->norm_in;
     p.S_out = a->state_out; p.z_out = a->norm_out;
+    p.seg_out = a->segment_states;
     return SUBQ_OK;
 }
 
@@ -146,6 +147,7 @@ int fill_bwd(const subq_bwd_args* a, subq::ScanParams& p) {
     p.dv = a->dv.data; p.dv_sb = a->dv.stride_b; p.dv_sh = a->dv.stride_h; p.dv_sn = a->dv.stride_n;
     p.S_in = a->state_in; p.z_in = a->norm_in;
     p.dlg = a->dlog_gamma;
+    p.seg_in = a->segment_states;
     return SUBQ_OK;
 }
 
@@ -207,6 +209,12 @@ size_t subq_fwd_workspace_bytes(const subq_fwd_args* a) {
     return 0;
 }
 
+size_t subq_segment_states_bytes(const subq_fwd_args* a) {
+    subq::ScanParams p;
+    if (fill_fwd(a, p) != SUBQ_OK || p.B == 0 || p.H == 0) return 0;
+    return use_tc(p, a->desc.dtype, a->desc.path) ? subq::tc_segment_states_bytes(p) : 0;
+}
+
 size_t subq_bwd_workspace_bytes(const subq_bwd_args* a) {
     subq::ScanParams p;
     if (fill_bwd(a, p) != SUBQ_OK) return 0;
@@ -228,6 +236,11 @@ int subq_fwd(const subq_fwd_args* a) {
     cudaStream_t st = static_cast<cudaStream_t>(a->stream);
     cudaError_t err;
     int launches = 0;
+    if (p.seg_out) {  // "not written" until the tensor-core kernel stamps its segment count
+        err = cudaMemsetAsync(p.seg_out, 0, 256, st);
+        if (err != cudaSuccess) return fail_cuda(err, "subq_fwd segment_states header");
+        if (!tc) p.seg_out = nullptr;
+    }
     if (tc) {
         const size_t need = subq::tc_fwd_workspace_bytes(p);
         if ((rc = check_workspace(a->workspace, a->workspace_bytes, need))) return rc;

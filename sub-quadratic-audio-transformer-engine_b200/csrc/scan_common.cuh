@@ -45,6 +45,13 @@ struct ScanParams {
     // 1: reverse time (token t sees itself and the later tokens; the
     // backward direction of the bidirectional scan), tensor-core path only
     int reverse;
+    // Segment-start states of the tensor-core scans: a 256-byte header (int 0:
+    // the segment count G it was written with; 0 = not written) and then, per
+    // sequence and segment, the fp32 state [S | z] (64 rows of 65). The
+    // forward writes them (seg_out); the backward reads them (seg_in) when
+    // their G is its own, in place of recomputing them.
+    float* seg_out;
+    const float* seg_in;
 };
 
 // phi(x) = ELU(x) + 1 and its derivative (reference python/subq_audio/autograd.py:15-28).

@@ -22,6 +22,7 @@ bool tc_supported(const ScanParams& p, int dtype);
 bool tc_bwd_supported(const ScanParams& p, int dtype);
 size_t tc_fwd_workspace_bytes(const ScanParams& p);
 size_t tc_bwd_workspace_bytes(const ScanParams& p);
+size_t tc_segment_states_bytes(const ScanParams& p);
 // Returns the number of kernel launches issued through *launches.
 cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches);
 cudaError_t launch_bwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches);

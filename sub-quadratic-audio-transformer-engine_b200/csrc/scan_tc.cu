@@ -29,6 +29,7 @@ int* status_ptr() {
 }
 
 cudaError_t launch_fwd_v2(const ScanParams& p, int dtype, cudaStream_t st);
+int fwd_segment_count(const ScanParams& p);
 cudaError_t launch_bwd_v2(const ScanParams& p, int dtype, cudaStream_t st);
 
 namespace {
@@ -181,6 +182,12 @@ static size_t tc_bwd_token_bytes(const ScanParams& p) {
 size_t tc_bwd_workspace_bytes(const ScanParams& p) {
     const size_t flags = p.decay_mode == SUBQ_DECAY_NONE ? 0 : align256((size_t)p.B * p.H * sizeof(int));
     return tc_bwd_token_bytes(p) + flags;
+}
+
+// Header (256 bytes) + per sequence and segment the fp32 [S | z] state, 64 x 65.
+size_t tc_segment_states_bytes(const ScanParams& p) {
+    const size_t G = (size_t)tcs::fwd_segment_count(p);
+    return 256 + (size_t)p.B * p.H * G * tcs::kD * (tcs::kD + 1) * sizeof(float);
 }
 
 cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches) {

@@ -168,7 +168,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     const int c_begin = min(nL, g * cps);
     const int n = min(nL, c_begin + cps) - c_begin;
     const PrefixShare share = prefix_share(g, P.G, nL, cps);
-    const int nA = share.b - share.a;  // phase-A chunks: this CTA's share of the segment sums
+    // The forward of the same call may hand over the segment-start states
+    // (written with the same segment count): phase A and the prefix exchange
+    // are then skipped.
+    const bool use_seg = p.seg_in != nullptr && *reinterpret_cast<const int*>(p.seg_in) == P.G;
+    const int nA = use_seg ? 0 : share.b - share.a;  // phase-A chunks: this CTA's share of the segment sums
     // pipeline slots: [0, nA) phase A, [nA, nA + n) phase B, [nA + n, nA + 2n) phase C
     const int nslots = nA + 2 * n;
 
@@ -582,7 +586,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     tc::tc_fence_after();
     float carry[32], carry_z = 0.f;  // prefix (phase B) / suffix (phase C) state rows, compute warps
     float lf = 0.f;                  // decay: log2 decay total of the segment's chunks (phase B)
-    if (warp < 8) gather_prefix(carry, carry_z);
+    if (warp < 8) {
+        if (use_seg) {  // this segment's start state from the forward (rows in lanes 0-15)
+#pragma unroll
+            for (int x = 0; x < 32; ++x) carry[x] = 0.f;
+            carry_z = 0.f;
+            if (lane < 16) {
+                const float* src = p.seg_in + 64 + ((int64_t)(bh * P.G + g) * kD + srow) * (kD + 1);
+#pragma unroll
+                for (int x = 0; x < 32; ++x) carry[x] = src[hf * 32 + x];
+                if (kNorm && hf == 0) carry_z = src[kD];
+            }
+        } else {
+            gather_prefix(carry, carry_z);
+        }
+    }
     tc::tc_fence_before();
     cluster.sync();  // remote reads done before the exchange tile is reused
     tc::tc_fence_after();

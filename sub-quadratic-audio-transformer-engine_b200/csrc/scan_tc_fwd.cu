@@ -424,6 +424,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     if (warp < 8) {
         const int quad = warp & 3, hf = warp >> 2, srow = quad * 16 + lane;
         const uint32_t loff = (uint32_t)(quad * 32) << 16;
+        // the segment's start state for the backward of the same call (lanes
+        // 0-15 hold rows srow), and the header with the segment count
+        if (p.seg_out && lane < 16) {
+            float* dst = p.seg_out + 64 + ((int64_t)(bh * P.G + g) * kD + srow) * (kD + 1);
+#pragma unroll
+            for (int x = 0; x < 32; ++x) dst[hf * 32 + x] = v[x];
+            if (hf == 0) dst[kD] = kNorm ? z : 0.f;
+        }
+        if (p.seg_out && bh == 0 && g == 0 && tid == 0) *reinterpret_cast<int*>(p.seg_out) = P.G;
         // (with decay the state stays in these registers and the first chunk's
         // operand is written at the start of phase 2, scaled by its exp(b_m))
         if (!kDecay && lane < 16) {
@@ -735,6 +744,13 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
 }
 
 }  // namespace
+
+// Segment count the forward launches with (every instantiation has the same
+// block size and shared memory, so one of them answers for all).
+int fwd_segment_count(const ScanParams& p) {
+    const void* kern = reinterpret_cast<const void*>(&fwd_kernel<false, true, false, false>);
+    return pick_segments(p, kern, kFwdThreads, L::total + 1024);
+}
 
 cudaError_t launch_fwd_v2(const ScanParams& p, int dtype, cudaStream_t st) {
     if (p.reverse) {  // reverse time: normalised form only

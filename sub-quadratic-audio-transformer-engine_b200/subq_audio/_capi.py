@@ -30,6 +30,7 @@ EXPORTED = (
     "subq_fwd", "subq_bwd", "subq_fwd_workspace_bytes", "subq_bwd_workspace_bytes",
     "subq_feature_map", "subq_last_path", "subq_last_launches", "subq_last_error",
     "subq_abi_version", "subq_device_info", "subq_device_status", "subq_bwd_noalloc",
+    "subq_segment_states_bytes",
 )
 
 
@@ -57,7 +58,7 @@ class FwdArgs(ctypes.Structure):
         ("state_in", ctypes.c_void_p), ("norm_in", ctypes.c_void_p),
         ("state_out", ctypes.c_void_p), ("norm_out", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
-        ("stream", ctypes.c_void_p),
+        ("stream", ctypes.c_void_p), ("segment_states", ctypes.c_void_p),
     ]
 
 
@@ -68,7 +69,7 @@ class BwdArgs(ctypes.Structure):
         ("state_in", ctypes.c_void_p), ("norm_in", ctypes.c_void_p),
         ("dlog_gamma", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
-        ("stream", ctypes.c_void_p),
+        ("stream", ctypes.c_void_p), ("segment_states", ctypes.c_void_p),
     ]
 
 
@@ -106,6 +107,8 @@ def load() -> ctypes.CDLL:
             lib.subq_fwd_workspace_bytes.restype = ctypes.c_size_t
             lib.subq_bwd_workspace_bytes.argtypes = [ctypes.POINTER(BwdArgs)]
             lib.subq_bwd_workspace_bytes.restype = ctypes.c_size_t
+            lib.subq_segment_states_bytes.argtypes = [ctypes.POINTER(FwdArgs)]
+            lib.subq_segment_states_bytes.restype = ctypes.c_size_t
             lib.subq_feature_map.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p]
             lib.subq_feature_map.restype = ctypes.c_int
             lib.subq_last_path.restype = ctypes.c_int
@@ -148,6 +151,10 @@ def fwd_workspace_bytes(args: FwdArgs) -> int:
 
 def bwd_workspace_bytes(args: BwdArgs) -> int:
     return int(load().subq_bwd_workspace_bytes(ctypes.byref(args)))
+
+
+def segment_states_bytes(args: FwdArgs) -> int:
+    return int(load().subq_segment_states_bytes(ctypes.byref(args)))
 
 
 def device_status(stream: int = 0) -> int:

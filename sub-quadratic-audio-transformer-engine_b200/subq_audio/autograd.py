@@ -142,9 +142,11 @@ class _CausalScan(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, lg, mask_u8, state, want_state, reverse=False):
+        seg = ops.SegmentStates()  # handed to the backward, which then skips recomputing them
         o, st = ops.scan_forward(q, k, v, log_gamma=lg, mask=mask_u8, normalize=True, state=state,
-                                 return_state=want_state, reverse=reverse)
+                                 return_state=want_state, reverse=reverse, segments=seg)
         ctx.reverse = reverse
+        ctx.seg = seg
         ctx.save_for_backward(q, k, v, lg if isinstance(lg, torch.Tensor) else None, mask_u8)
         ctx.lg_is_tensor = isinstance(lg, torch.Tensor)
         ctx.state = state
@@ -159,7 +161,7 @@ class _CausalScan(torch.autograd.Function):
         need_lg = ctx.lg_is_tensor and ctx.needs_input_grad[3]
         dq, dk, dv, dlg = ops.scan_backward(q, k, v, do.contiguous(), log_gamma=lg, mask=mask_u8,
                                             normalize=True, state=ctx.state, need_dlog_gamma=need_lg,
-                                            reverse=ctx.reverse)
+                                            reverse=ctx.reverse, segments=ctx.seg)
         glg = None
         if need_lg:
             glg = dlg.to(lg.dtype)

@@ -113,11 +113,23 @@ def _workspace(nbytes: int, device: torch.device, keep: list) -> Tuple[int, int]
     return (ptr + 255) // 256 * 256, nbytes
 
 
+class SegmentStates:
+    """Carrier of the segment-start states from a forward to the backward of
+    the same inputs: pass one instance as ``segments=`` to ``scan_forward``
+    (which fills it on the tensor-core path) and then to ``scan_backward``
+    (which then skips recomputing those states). An empty or mismatched
+    carrier is ignored by the backward."""
+
+    def __init__(self) -> None:
+        self.buf: Optional[torch.Tensor] = None
+
+
 def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma: LogGamma = None,
                  mask: Optional[torch.Tensor] = None, normalize: bool = True, scale: Optional[float] = None,
                  clamp_min: float = 1e-5, state: Optional[Tuple[torch.Tensor, Optional[torch.Tensor]]] = None,
                  return_state: bool = False, flush_subnormal: bool = False, path: str = "auto",
-                 out: Optional[torch.Tensor] = None, reverse: bool = False):
+                 out: Optional[torch.Tensor] = None, reverse: bool = False,
+                 segments: Optional[SegmentStates] = None):
     """Causal scan. Returns ``(o, (S, z) | None)``; S [B,H,d,e] and z [B,H,d] are float32.
     ``k`` and ``v`` may have fewer heads than ``q`` (a divisor of H: grouped K/V,
     query head h reading K/V head h // (H // Hkv)); the backward then returns
@@ -154,6 +166,11 @@ def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma
                 a.norm_out = z_out.data_ptr()
         a.stream = torch.cuda.current_stream(q.device).cuda_stream
         a.workspace, a.workspace_bytes = _workspace(_capi.fwd_workspace_bytes(a), q.device, keep)
+        if segments is not None:
+            nbytes = _capi.segment_states_bytes(a)
+            segments.buf = torch.empty(nbytes, dtype=torch.uint8, device=q.device) if nbytes else None
+            if segments.buf is not None:
+                a.segment_states = segments.buf.data_ptr()
         _capi.fwd(a)
     return o, ((S_out, z_out) if return_state else None)
 
@@ -163,7 +180,7 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
                   scale: Optional[float] = None, clamp_min: float = 1e-5,
                   state: Optional[Tuple[torch.Tensor, Optional[torch.Tensor]]] = None,
                   need_dlog_gamma: bool = False, flush_subnormal: bool = False, path: str = "auto",
-                  reverse: bool = False):
+                  reverse: bool = False, segments: Optional[SegmentStates] = None):
     """Gradients of ``scan_forward``. Returns ``(dq, dk, dv, dlog_gamma | None)``;
     dlog_gamma is float32 [B,H,N] (d loss / d log gamma_t per token)."""
     _require_cuda(q, k, v, dout)
@@ -196,6 +213,8 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
             a.dlog_gamma = dlg.data_ptr()
         a.stream = torch.cuda.current_stream(q.device).cuda_stream
         a.workspace, a.workspace_bytes = _workspace(_capi.bwd_workspace_bytes(a), q.device, keep)
+        if segments is not None and segments.buf is not None and segments.buf.device == q.device:
+            a.segment_states = segments.buf.data_ptr()
         _capi.bwd(a)
     return dq, dk, dv, dlg
 

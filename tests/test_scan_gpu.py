@@ -316,3 +316,25 @@ def test_feature_map_known_answers():
     ops.feature_map_(x)
     ref = torch.tensor([0.367879, 3.0, 1.0, 0.135335], device="cuda")
     assert torch.allclose(x, ref, atol=1e-4)
+
+
+@pytest.mark.parametrize("decay,H,N", [(None, 8, 4000), ("token", 1, 3000), (None, 2, 700)])
+def test_backward_with_forward_segment_states_is_unchanged(decay, H, N):
+    """The backward given the forward's segment-start states (skipping its own
+    recomputation of them) returns the same gradients as without them."""
+    B = 2
+    q, k, v, do, lg, m, st = make_case(B, H, N, 64, 64, torch.bfloat16, seed=61 + N, decay=decay, mask=True,
+                                       state=True)
+    args = [to_dev(x) for x in (q, k, v, do)]
+    seg = ops.SegmentStates()
+    ops.scan_forward(*args[:3], log_gamma=to_dev(lg), mask=to_dev(m), state=to_dev(st), segments=seg)
+    assert seg.buf is not None
+    got = ops.scan_backward(*args, log_gamma=to_dev(lg), mask=to_dev(m), state=to_dev(st),
+                            need_dlog_gamma=lg is not None, segments=seg)
+    ref = ops.scan_backward(*args, log_gamma=to_dev(lg), mask=to_dev(m), state=to_dev(st),
+                            need_dlog_gamma=lg is not None)
+    torch.cuda.synchronize()
+    assert ops.last_path() == "tensorcore"
+    for x, y in zip(got, ref):
+        if y is not None:
+            assert rel_err(x, y.double().cpu().numpy()) < 1e-3
