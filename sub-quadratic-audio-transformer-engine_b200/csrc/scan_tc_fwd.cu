@@ -595,8 +595,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             tc::fence_proxy_async();
         }
         if (n > 0 && ok) ok = mask_p(0);
+        // the output rows' mask values, loaded one chunk ahead (off the epilogue's path)
+        float m_next = n > 0 ? row_mask_at(c_begin, row) : 0.f;
         for (int i = 0; i < n && ok; ++i) {
             const int c = c_begin + i, bf = i & 1, pu = i >> 1;
+            const float m_row = m_next;
+            if (i + 1 < n) m_next = row_mask_at(c + 1, row);
             // state refresh: bf16 [S | z]_c+1 into sb[(i + 1) % 2], the next chunk's operand
             ok = tc::bar_and(kBarCompute, kComputeThreads,
                              wait_bar(&bars[B_SFULL], sfull_count & 1, P.status)) && ok;
@@ -669,8 +673,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             if (tid == 0) tc::mbar_arrive(&bars[B_ODONE + bf]);  // every thread has read O'[bf]
             {
                 // O' and its normaliser column carry phi(q) unscaled: o = s O' / max(s Z', clamp)
-                const float m = row_mask_at(c, row);
-                float inv = m * p.scale;
+                float inv = m_row * p.scale;
                 if (kNorm) inv = inv / max_nan(p.scale * zi, p.clamp_min);
 #pragma unroll
                 for (int x = 0; x < 32; ++x) o[x] *= inv;
