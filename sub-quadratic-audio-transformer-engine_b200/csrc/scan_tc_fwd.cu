@@ -173,9 +173,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         const uint32_t ka = sbase + s * L::stage + L::k, va = sbase + s * L::stage + L::v;
         const uint32_t lbo = L::ones - (s * L::stage + L::v);  // V atom -> ones atom
         const uint32_t n80 = kNorm ? idSX : tc::idesc_f16<kFp16>(64, 64, true, true);
-        for (int kk = 0; kk < 8; ++kk)
-            tc::mma_f16(tmem + col, tc::sdesc_sw128(ka + kk * 2048, kTile, 1024),
-                        tc::sdesc_sw128(va + kk * 2048, lbo, 1024), n80, (first && kk == 0) ? 0u : 1u);
+        const uint64_t da = tc::sdesc_sw128(ka, kTile, 1024), db = tc::sdesc_sw128(va, lbo, 1024);
+        for (int kk = 0; kk < 8; ++kk)  // a K-step of 16 tokens is 2048 bytes on (a descriptor step of 128)
+            tc::mma_f16(tmem + col, da + kk * 128, db + kk * 128, n80, (first && kk == 0) ? 0u : 1u);
     };
 
     // Chunk of pipeline slot j: phase-1 slots (j < n1) visit the share in an
@@ -475,10 +475,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 if (!wait_bar(&bars[B_TDONE + s], u & 1, P.status)) return false;
                 if (i >= 2 && !wait_bar(&bars[B_PSDONE + bf], ((i >> 1) - 1) & 1, P.status)) return false;
                 tc::tc_fence_after();
-                const uint32_t qa = sbase + s * L::stage + L::q, ka = sbase + s * L::stage + L::k;
-                for (int kk = 0; kk < 4; ++kk)
-                    tc::mma_f16(tmem + cP + bf * 128, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(ka + kk * 32, 16, 1024), idP, kk > 0);
+                const uint64_t dq = tc::sdesc_sw128(sbase + s * L::stage + L::q, 16, 1024);
+                const uint64_t dk = tc::sdesc_sw128(sbase + s * L::stage + L::k, 16, 1024);
+                for (int kk = 0; kk < 4; ++kk)  // 16 features are 32 bytes on (a descriptor step of 2)
+                    tc::mma_f16(tmem + cP + bf * 128, dq + kk * 2, dk + kk * 2, idP, kk > 0);
                 tc::mma_commit(&bars[B_PFULL + bf]);
                 return true;
             };
@@ -498,18 +498,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 if (ok && i >= 2) ok = wait_bar(&bars[B_ODONE + bf], (pu - 1) & 1, P.status);
                 if (!ok) break;
                 tc::tc_fence_after();
-                const uint32_t qa = sbase + s * L::stage + L::q, va = sbase + s * L::stage + L::v;
                 const uint32_t tOb = tmem + cO + bf * kNX;
-                const uint32_t sba = sbase + L::sb + (i & 1) * L::sbuf;
+                const uint64_t dq = tc::sdesc_sw128(sbase + s * L::stage + L::q, 16, 1024);
+                const uint64_t dsb = tc::sdesc_sw128(sbase + L::sb + (i & 1) * L::sbuf, kD * kD * 2, 1024);
                 for (int kk = 0; kk < 4; ++kk)  // [O | Zi] = phi~(Q) [S_c | z_c]
-                    tc::mma_f16(tOb, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(sba + kk * 2048, kD * kD * 2, 1024), kNorm ? idOX : idO, kk > 0);
+                    tc::mma_f16(tOb, dq + kk * 2, dsb + kk * 128, kNorm ? idOX : idO, kk > 0);
                 // [O | Zi] += P [V | 1]: bf16 P read from TMEM (8 columns per 16 tokens);
                 // the ones column adds the causal row sums to the normaliser
                 const uint32_t lbo = kNorm ? L::ones - (s * L::stage + L::v) : kTile;
+                const uint64_t dv = tc::sdesc_sw128(sbase + s * L::stage + L::v, lbo, 1024);
                 for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts(tOb, tmem + cP + bf * 128 + kk * 8, tc::sdesc_sw128(va + kk * 2048, lbo, 1024),
-                                   kNorm ? idOX : idO, 1u);
+                    tc::mma_f16_ts(tOb, tmem + cP + bf * 128 + kk * 8, dv + kk * 128, kNorm ? idOX : idO, 1u);
                 tc::mma_commit(&bars[B_OFULL + bf]);
                 tc::mma_commit(&bars[B_EMPTY + s]);
             }
