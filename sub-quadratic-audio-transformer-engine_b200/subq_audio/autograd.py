@@ -159,7 +159,8 @@ class _CausalScan(torch.autograd.Function):
     def backward(ctx, do, _dS=None, _dz=None):
         q, k, v, lg, mask_u8 = ctx.saved_tensors
         need_lg = ctx.lg_is_tensor and ctx.needs_input_grad[3]
-        dq, dk, dv, dlg = ops.scan_backward(q, k, v, do.contiguous(), log_gamma=lg, mask=mask_u8,
+        # dO in any layout with a contiguous last dimension (the kernels take strides)
+        dq, dk, dv, dlg = ops.scan_backward(q, k, v, do, log_gamma=lg, mask=mask_u8,
                                             normalize=True, state=ctx.state, need_dlog_gamma=need_lg,
                                             reverse=ctx.reverse, segments=ctx.seg)
         glg = None
@@ -205,6 +206,14 @@ def chunkwise_flash_linear_attention(q: torch.Tensor, k: torch.Tensor, v: torch.
     (gamma = sigmoid(w)) as a scalar, [H], [B,T], [B,H] or [B,H,T], or None
     for gamma == 1. Returns ``(out, S_next)`` with ``S_next.Z`` attached.
     """
+    out, S_next = _chunkwise(q, k, v, decay_w, past_state, attention_mask, is_causal)
+    return out.contiguous(), S_next
+
+
+def _chunkwise(q, k, v, decay_w, past_state, attention_mask, is_causal):
+    """chunkwise_flash_linear_attention with ``out`` in q's memory order (a
+    [B, H, T, D] view of a [B, T, H, D] buffer when q is a view of a
+    projection's output), for callers that transpose it back."""
     is_3d = q.ndim == 3
     if is_3d:
         q, k, v = q.unsqueeze(1), k.unsqueeze(1), v.unsqueeze(1)
@@ -230,7 +239,7 @@ def chunkwise_flash_linear_attention(q: torch.Tensor, k: torch.Tensor, v: torch.
         out = out.squeeze(1)
     if home is not None:
         out = out.to(home)
-    return out.contiguous(), S_next
+    return out, S_next
 
 
 def _reduce_dw(dlg: torch.Tensor, w: torch.Tensor, B: int, H: int, T: int) -> torch.Tensor:
@@ -373,10 +382,16 @@ class SubQLinearAttention(nn.Module):
             decay_w = self.raw_decay.view(1, self.num_heads, 1) + gate
         else:
             decay_w = self.raw_decay
-        out, next_state = chunkwise_flash_linear_attention(Q, K, V, decay_w, past_state=past_state,
-                                                           attention_mask=attention_mask, is_causal=self.is_causal)
+        # the scan writes out in Q's memory order ([B, L, H, D] under the [B, H, L, D]
+        # view), so the transpose back below needs no copy
+        out, next_state = _chunkwise(Q, K, V, decay_w, past_state, attention_mask, self.is_causal)
         if self.head_norm is not None:
-            out = self.head_norm(out)
+            # with the weight in the activations' dtype torch runs its fused RMSNorm
+            # kernel (an fp32 weight on bf16 activations takes an unfused path)
+            w = self.head_norm.weight
+            if w is not None and w.dtype != out.dtype:
+                w = w.to(out.dtype)
+            out = F.rms_norm(out, self.head_norm.normalized_shape, w, self.head_norm.eps)
         else:
             out = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + 1e-5)
         out = out.transpose(1, 2).contiguous().view(B, L, self.hidden_size)

@@ -44,6 +44,19 @@ def _inner_contig(t: torch.Tensor) -> torch.Tensor:
     return t if (t.shape[-1] <= 1 or t.stride(-1) == 1) else t.contiguous()
 
 
+def _empty_in_order(ref: torch.Tensor, shape, dtype: torch.dtype) -> torch.Tensor:
+    """An empty [B, H, N, x] tensor whose memory runs over B, H and N in the
+    same order as ``ref``'s. For q, k, v that are [B, H, N, x] views of a
+    projection's [B, N, H * x] output, the results are views of a [B, N, H, x]
+    buffer, so the transpose back to [B, N, H * x] needs no copy."""
+    st = ref.stride()
+    order = sorted(range(3), key=lambda i: (-st[i], i))  # outermost first
+    if order == [0, 1, 2]:
+        return torch.empty(shape, dtype=dtype, device=ref.device)
+    buf = torch.empty([shape[i] for i in order] + [shape[3]], dtype=dtype, device=ref.device)
+    return buf.permute(*([order.index(i) for i in range(3)] + [3]))
+
+
 def _check_kv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
     """k [B, Hkv, N, d] and v [B, Hkv, N, e] with Hkv a divisor of q's H (grouped K/V)."""
     B, H, N, d = q.shape
@@ -144,7 +157,7 @@ def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma
     e = v.shape[-1]
     keep: list = []
     with torch.cuda.device(q.device):
-        o = out if out is not None else torch.empty((B, H, N, e), dtype=q.dtype, device=q.device)
+        o = out if out is not None else _empty_in_order(q, (B, H, N, e), q.dtype)
         a = _capi.FwdArgs()
         a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep, reverse)
         a.q, a.k, a.v, a.o = _t4(q), _t4(k), _t4(v), _t4(o)
@@ -192,9 +205,9 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
     e = v.shape[-1]
     keep: list = []
     with torch.cuda.device(q.device):
-        dq = torch.empty((B, H, N, d), dtype=q.dtype, device=q.device)
-        dk = torch.empty(k.shape, dtype=q.dtype, device=q.device)  # [B, Hkv, N, d]: summed per K/V group
-        dv = torch.empty(v.shape, dtype=q.dtype, device=q.device)
+        dq = _empty_in_order(q, (B, H, N, d), q.dtype)
+        dk = _empty_in_order(k, tuple(k.shape), q.dtype)  # [B, Hkv, N, d]: summed per K/V group
+        dv = _empty_in_order(v, tuple(v.shape), q.dtype)
         a = _capi.BwdArgs()
         a.desc = _desc(q, v, log_gamma, mask, normalize, scale, clamp_min, flush_subnormal, path, keep, reverse)
         a.q, a.k, a.v, a.dout = _t4(q), _t4(k), _t4(v), _t4(dout)
