@@ -87,6 +87,47 @@ def test_decode_step_replays_in_a_cuda_graph():
     assert torch.equal(S, S2) and torch.equal(z, z2)
 
 
+def test_stream_of_tensor_core_calls_replays_in_a_cuda_graph():
+    """The C3 serving form: a stream of 4096-token calls (tensor-core scans,
+    cluster launches) sharing one in-place state, captured once as a CUDA graph
+    (state reset included); replays equal the eager calls bit for bit."""
+    B, H, N, L = 1, 4, 4 * 4096, 4096
+    q, k, v, _ = _seq(B, H, N, torch.float16, seed=12)
+    o_eager, o_graph = torch.empty_like(q), torch.empty_like(q)
+    S, z = torch.zeros(B, H, 64, 64, device="cuda"), torch.zeros(B, H, 64, device="cuda")
+
+    def calls(o):
+        return [ops.DecodeStep(q[:, :, s:s + L], k[:, :, s:s + L], v[:, :, s:s + L], o[:, :, s:s + L], S, z)
+                for s in range(0, N, L)]
+
+    def run(steps):
+        S.zero_(), z.zero_()
+        for c in steps:
+            c.step()
+
+    eager, graphed = calls(o_eager), calls(o_graph)
+    run(eager)
+    torch.cuda.synchronize()
+    assert ops.last_path() == "tensorcore"
+    S_eager, z_eager = S.clone(), z.clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run(graphed)  # warm-up outside the capture
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run(graphed)
+    o_graph.zero_()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(o_graph, o_eager)
+    assert torch.equal(S, S_eager) and torch.equal(z, z_eager)
+    full = ops.scan_forward(q, k, v)[0]
+    assert rel_err(o_graph, full.double().cpu().numpy()) < 2e-2
+
+
 def test_decode_step_rejects_buffers_it_would_copy():
     B, H = 1, 2
     qb, kb, vb, ob = (torch.empty(B, H, 1, 64, dtype=torch.bfloat16, device="cuda") for _ in range(4))
