@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     auto mma_xt = [&](uint32_t dst, uint32_t xa, uint32_t ya, uint32_t extra, bool first) {
         const uint32_t lbo = kNorm ? extra - ya : kTile;
         for (int kk = 0; kk < 8; ++kk)
-            tc::mma_f16(dst, tc::sdesc_sw128(xa + kk * 2048, kTile, 1024), tc::sdesc_sw128(ya + kk * 2048, lbo, 1024),
+            tc::mma_f16(dst, (tc::sdesc_sw128(xa, kTile, 1024) + kk * 128), (tc::sdesc_sw128(ya, lbo, 1024) + kk * 128),
                         idST, (first && kk == 0) ? 0u : 1u);
     };
 
@@ -626,8 +626,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 tc::tc_fence_after();
                 const uint32_t qa = slot_addr(j, BL::q), ka = slot_addr(j, BL::k);
                 for (int kk = 0; kk < 4; ++kk)
-                    tc::mma_f16(tmem + cP, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(ka + kk * 32, 16, 1024), idPP, kk > 0);
+                    tc::mma_f16(tmem + cP, (tc::sdesc_sw128(qa, 16, 1024) + kk * 2),
+                                (tc::sdesc_sw128(ka, 16, 1024) + kk * 2), idPP, kk > 0);
                 tc::mma_commit(&bars[B_PFULL]);
                 return true;
             };
@@ -649,10 +649,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 if (!ok) break;
                 tc::tc_fence_after();
                 for (int kk = 0; kk < 4; ++kk)
-                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(qa + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(sba + kk * 2048, kD * kD * 2, 1024), idNZ, kk > 0);
+                    tc::mma_f16(tmem + cNZ, (tc::sdesc_sw128(qa, 16, 1024) + kk * 2),
+                                (tc::sdesc_sw128(sba, kD * kD * 2, 1024) + kk * 128), idNZ, kk > 0);
                 for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts(tmem + cNZ, tmem + cP + kk * 8, tc::sdesc_sw128(va + kk * 2048, lbo_v1, 1024),
+                    tc::mma_f16_ts(tmem + cNZ, tmem + cP + kk * 8, (tc::sdesc_sw128(va, lbo_v1, 1024) + kk * 128),
                                    idNZ, 1u);
                 tc::mma_commit(&bars[B_NZFULL]);
                 // P of the next chunk now when its feature map is already done (the
@@ -665,8 +665,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 if (!ok) break;
                 tc::tc_fence_after();
                 for (int kk = 0; kk < 4; ++kk)
-                    tc::mma_f16(tmem + cDA, tc::sdesc_sw128(sbase + BL::ob + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(va + kk * 32, 16, 1024), idPP, kk > 0);
+                    tc::mma_f16(tmem + cDA, (tc::sdesc_sw128(sbase + BL::ob, 16, 1024) + kk * 2),
+                                (tc::sdesc_sw128(va, 16, 1024) + kk * 2), idPP, kk > 0);
                 if (kNorm)
                     tc::mma_f16(tmem + cDA, tc::sdesc_sw128(sbase + BL::ca, 16, 1024),
                                 tc::sdesc_sw128(sbase + BL::ones, 16, 1024), idPP, 1u);
@@ -675,8 +675,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 // dQ~ = [o^ | c] [S_c | z_c]^T (issued while the compute warps mask dA)
                 //     + bf16(dA) K^                (into the NZ / dQ columns)
                 for (int kk = 0; kk < 4; ++kk)
-                    tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ob + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(sba + kk * 32, 16, 1024), idKK64, kk > 0);
+                    tc::mma_f16(tmem + cNZ, (tc::sdesc_sw128(sbase + BL::ob, 16, 1024) + kk * 2),
+                                (tc::sdesc_sw128(sba, 16, 1024) + kk * 2), idKK64, kk > 0);
                 if (kNorm)
                     tc::mma_f16(tmem + cNZ, tc::sdesc_sw128(sbase + BL::ca, 16, 1024),
                                 tc::sdesc_sw128(sba + kD * kD * 2, 16, 1024), idKK64, 1u);
@@ -684,7 +684,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 if (!ok) break;
                 tc::tc_fence_after();
                 for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts(tmem + cNZ, tmem + cDA + kk * 8, tc::sdesc_sw128(ka + kk * 2048, kTile, 1024),
+                    tc::mma_f16_ts(tmem + cNZ, tmem + cDA + kk * 8, (tc::sdesc_sw128(ka, kTile, 1024) + kk * 128),
                                    idKM64, 1u);
                 tc::mma_commit(&bars[B_DQFULL]);
                 // P of the next chunk, if not issued above
@@ -897,10 +897,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 tc::tc_fence_after();
                 // P^T = K^ q^^T ; dA^T = [V | 1] [o^ | c]^T   (key-major rows)
                 for (int kk = 0; kk < 4; ++kk) {
-                    tc::mma_f16(tmem + cPT, tc::sdesc_sw128(ka + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(qa + kk * 32, 16, 1024), idPP, kk > 0);
-                    tc::mma_f16(tmem + cDAT, tc::sdesc_sw128(va + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(sbase + BL::ob + kk * 32, 16, 1024), idPP, kk > 0);
+                    tc::mma_f16(tmem + cPT, (tc::sdesc_sw128(ka, 16, 1024) + kk * 2),
+                                (tc::sdesc_sw128(qa, 16, 1024) + kk * 2), idPP, kk > 0);
+                    tc::mma_f16(tmem + cDAT, (tc::sdesc_sw128(va, 16, 1024) + kk * 2),
+                                (tc::sdesc_sw128(sbase + BL::ob, 16, 1024) + kk * 2), idPP, kk > 0);
                 }
                 if (kNorm)
                     tc::mma_f16(tmem + cDAT, tc::sdesc_sw128(sbase + BL::ones, 16, 1024),
@@ -918,10 +918,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 if (!ok) break;
                 tc::tc_fence_after();
                 for (int kk = 0; kk < 4; ++kk) {
-                    tc::mma_f16(tmem + cDK, tc::sdesc_sw128(va + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(dsa + kk * 32, 16, 1024), idKK64, kk > 0);
-                    tc::mma_f16(tmem + cDV, tc::sdesc_sw128(ka + kk * 32, 16, 1024),
-                                tc::sdesc_sw128(dsa + kk * 2048, kTile, 1024), idKM64, kk > 0);
+                    tc::mma_f16(tmem + cDK, (tc::sdesc_sw128(va, 16, 1024) + kk * 2),
+                                (tc::sdesc_sw128(dsa, 16, 1024) + kk * 2), idKK64, kk > 0);
+                    tc::mma_f16(tmem + cDV, (tc::sdesc_sw128(ka, 16, 1024) + kk * 2),
+                                (tc::sdesc_sw128(dsa, kTile, 1024) + kk * 128), idKM64, kk > 0);
                 }
                 if (kNorm)
                     tc::mma_f16(tmem + cDK, tc::sdesc_sw128(sbase + BL::ones, 16, 1024),
@@ -930,10 +930,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
                 if (!ok) break;
                 tc::tc_fence_after();
                 for (int kk = 0; kk < 8; ++kk) {
-                    tc::mma_f16_ts(tmem + cDK, tmem + cDAT + kk * 8, tc::sdesc_sw128(qa + kk * 2048, kTile, 1024),
+                    tc::mma_f16_ts(tmem + cDK, tmem + cDAT + kk * 8, (tc::sdesc_sw128(qa, kTile, 1024) + kk * 128),
                                    idKM64, 1u);
                     tc::mma_f16_ts(tmem + cDV, tmem + cPT + kk * 8,
-                                   tc::sdesc_sw128(sbase + BL::ob + kk * 2048, kTile, 1024), idKM64, 1u);
+                                   (tc::sdesc_sw128(sbase + BL::ob, kTile, 1024) + kk * 128), idKM64, 1u);
                 }
                 tc::mma_commit(&bars[B_KVFULL]);
             }

@@ -226,7 +226,10 @@ __device__ __forceinline__ void tmem_st32_raw(uint32_t taddr, const uint32_t* v)
 // 128-byte-swizzled operand tile. K-major: rows of 128 B (64 16-bit values),
 // SBO = 1024 B between 8-row groups. MN-major: rows are K, 128 B of MN values
 // each, SBO = 1024 B between 8-K-row groups, LBO = stride between 64-wide MN
-// atoms (unused when MN = 64).
+// atoms (unused when MN = 64). The start-address field holds saddr / 16 and
+// shared addresses stay below 2^18, so the descriptor of saddr + off (off a
+// multiple of 16) is this descriptor plus off / 16: the K-step loops add 2 per
+// 32-byte step (16 K-major features) and 128 per 2048-byte step (16 MN-major rows).
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
