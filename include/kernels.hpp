@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define SUBQ_ABI_VERSION 3
+#define SUBQ_ABI_VERSION 4
 
 typedef enum subq_status {
     SUBQ_OK = 0,
@@ -58,7 +58,9 @@ typedef enum subq_status {
     SUBQ_ERR_UNSUPPORTED = 3,      /* a shape/dtype combination no kernel covers  */
     SUBQ_ERR_CUDA = 4,             /* a CUDA runtime error (message has the text) */
     SUBQ_ERR_TIMEOUT = 5,          /* a bounded device-side wait gave up          */
-    SUBQ_ERR_WORKSPACE = 6         /* workspace missing, too small or misaligned  */
+    SUBQ_ERR_WORKSPACE = 6,        /* workspace missing, too small or misaligned  */
+    SUBQ_ERR_STATE = 7             /* device status: a backward's segment_states was not
+                                      filled by the forward of the same call          */
 } subq_status;
 
 /* Same order as the reference's PrecisionMode (include/tensor.hpp:14-18);
@@ -146,8 +148,16 @@ typedef struct subq_bwd_args {
     size_t workspace_bytes;
     void* stream;
     /* Optional: the segment_states buffer the forward of the same inputs
-     * filled; used when it matches this call's segment split, else ignored. */
+     * filled. Alone, it is used when it matches this call's segment split and
+     * ignored otherwise. */
     const float* segment_states;
+    /* Optional (ABI 4): the forward's output o of the same call. Given with
+     * segment_states on the tensor-core path without decay, the backward runs
+     * in one pass from what that forward handed over (its per-chunk states and
+     * normalisers) instead of recomputing them; the buffer must then come from
+     * that very forward, else no gradient is written and subq_device_status
+     * reports SUBQ_ERR_STATE. */
+    subq_tensor4 out;
 } subq_bwd_args;
 
 /* Forward scan. Replaces run_attention_forward / the torch chunked forward. */

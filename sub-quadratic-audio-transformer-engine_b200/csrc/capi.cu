@@ -148,6 +148,10 @@ int fill_bwd(const subq_bwd_args* a, subq::ScanParams& p) {
     p.S_in = a->state_in; p.z_in = a->norm_in;
     p.dlg = a->dlog_gamma;
     p.seg_in = a->segment_states;
+    if (a->out.data) {
+        if ((rc = check_tensor(a->out, "out", dt, false))) return rc;
+        p.fo = a->out.data; p.fo_sb = a->out.stride_b; p.fo_sh = a->out.stride_h; p.fo_sn = a->out.stride_n;
+    }
     return SUBQ_OK;
 }
 
@@ -167,7 +171,8 @@ size_t gqa_bytes(const subq::ScanParams& p, int dtype) {
 }
 
 size_t scan_bwd_ws(const subq::ScanParams& p, int dtype, bool tc) {
-    return tc ? subq::tc_bwd_workspace_bytes(p) : exact_bwd_ws(p, dtype);
+    if (!tc) return exact_bwd_ws(p, dtype);
+    return subq::bwd1_usable(p) ? subq::bwd1_workspace_bytes(p) : subq::tc_bwd_workspace_bytes(p);
 }
 
 int check_workspace(void* ws, size_t have, size_t need) {
@@ -284,7 +289,9 @@ int subq_bwd(const subq_bwd_args* a) {
         p.dv = base + gqa_dk_bytes(p, a->desc.dtype);
         p.dv_sn = p.e, p.dv_sh = (int64_t)p.N * p.e, p.dv_sb = p.dv_sh * p.H;
     }
-    if (tc) {
+    if (tc && subq::bwd1_usable(p)) {  // one pass from the forward's handover
+        err = subq::launch_bwd1(p, a->desc.dtype, st, &launches);
+    } else if (tc) {
         err = subq::launch_bwd_tc(p, a->desc.dtype, st, &launches);
     } else {
         err = subq::launch_bwd_exact(p, a->desc.dtype, st);

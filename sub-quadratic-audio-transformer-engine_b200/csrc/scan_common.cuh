@@ -52,6 +52,9 @@ struct ScanParams {
     // their G is its own, in place of recomputing them.
     float* seg_out;
     const float* seg_in;
+    // The forward's output o (backward only, with seg_in): the one-pass
+    // backward forms the normaliser's adjoint from dO . o.
+    const void* fo; int64_t fo_sb, fo_sh, fo_sn;
 };
 
 // phi(x) = ELU(x) + 1 and its derivative (reference python/subq_audio/autograd.py:15-28).

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include "kernels.hpp"
+
 namespace subq {
 
 struct ScanParams;
@@ -26,6 +28,11 @@ size_t tc_segment_states_bytes(const ScanParams& p);
 // Returns the number of kernel launches issued through *launches.
 cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches);
 cudaError_t launch_bwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches);
+// One-pass backward from the forward's handover (scan_tc_bwd1.cu): no decay,
+// segment_states and the forward's output given.
+bool bwd1_usable(const ScanParams& p);
+size_t bwd1_workspace_bytes(const ScanParams& p);
+cudaError_t launch_bwd1(const ScanParams& p, int dtype, cudaStream_t st, int* launches);
 // Device-side status word of the tensor-core kernels (bounded waits).
 cudaError_t tc_read_status(cudaStream_t st, int* status);
 

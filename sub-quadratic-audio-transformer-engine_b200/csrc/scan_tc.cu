@@ -184,10 +184,12 @@ size_t tc_bwd_workspace_bytes(const ScanParams& p) {
     return tc_bwd_token_bytes(p) + flags;
 }
 
-// Header (256 bytes) + per sequence and segment the fp32 [S | z] state, 64 x 65.
+// The forward -> backward handover (tc_common.cuh HandLayout): segment-start
+// states, live-chunk plan and, without decay, the per-chunk state operands
+// and per-token normalisers of the one-pass backward.
 size_t tc_segment_states_bytes(const ScanParams& p) {
-    const size_t G = (size_t)tcs::fwd_segment_count(p);
-    return 256 + (size_t)p.B * p.H * G * tcs::kD * (tcs::kD + 1) * sizeof(float);
+    const int G = tcs::fwd_segment_count(p);
+    return tcs::HandLayout(p.B * p.H, p.N, G, p.decay_mode == SUBQ_DECAY_NONE).total;
 }
 
 cudaError_t launch_fwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* launches) {

@@ -171,7 +171,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     // The forward of the same call may hand over the segment-start states
     // (written with the same segment count): phase A and the prefix exchange
     // are then skipped.
-    const bool use_seg = p.seg_in != nullptr && *reinterpret_cast<const int*>(p.seg_in) == P.G;
+    // (the header stamps this call's shape and flags: a buffer from another call is ignored)
+    const int* hdr = reinterpret_cast<const int*>(p.seg_in);
+    const bool use_seg = hdr != nullptr && hdr[0] == P.G && hdr[1] == kHandMagic && hdr[2] == p.B * p.H &&
+                         hdr[3] == p.N && (hdr[4] & ~kHandChunks) == hand_flags(kRev, kNorm, kDecay ? 1 : 0, false);
     const int nA = use_seg ? 0 : share.b - share.a;  // phase-A chunks: this CTA's share of the segment sums
     // pipeline slots: [0, nA) phase A, [nA, nA + n) phase B, [nA + n, nA + 2n) phase C
     const int nslots = nA + 2 * n;

@@ -100,6 +100,13 @@ struct FwdParams {
     int G;
     int cps;
     int* status;
+    // handover to the backward (null when not written): header, live-chunk
+    // counts and prefix, per-chunk state operands and per-token normalisers
+    int* hdr;
+    int* nl;
+    int* off;
+    uint8_t* chunks;
+    float* zc;
 };
 
 template <bool kFp16, bool kNorm, bool kDecay, bool kRev>
@@ -147,11 +154,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     // The segments split the live chunks (up to the sequence's last live token);
     // the chunks after them are zero-filled at the end.
     const int nL = live_chunks(p, b, nC, reinterpret_cast<int*>(tslot + 1));
+    if (P.nl && g == 0) {
+        // live-chunk counts of the handover; the last CTA to record its count
+        // writes their prefix (the backward's work plan)
+        if (tid == 0) {
+            P.nl[bh] = nL;
+            __threadfence();
+            tslot[2] = atomicAdd(P.hdr + 5, 1) == p.B * p.H - 1 ? 1u : 0u;
+        }
+        __syncthreads();
+        if (tslot[2]) {
+            __threadfence();
+            block_prefix(P.nl, P.off, p.B * p.H, reinterpret_cast<int*>(sm + L::xz));
+            if (tid == 0) P.hdr[6] = kHandMagic;  // the plan is complete
+        }
+        __syncthreads();
+    }
+    if (P.hdr && bh == 0 && g == 0 && tid == 0) {
+        P.hdr[1] = kHandMagic;
+        P.hdr[2] = p.B * p.H;
+        P.hdr[3] = p.N;
+        P.hdr[4] = hand_flags(kRev, kNorm, kDecay ? 1 : 0, P.chunks != nullptr);
+    }
     const int cps = (nL + P.G - 1) / P.G;
     const int c_begin = min(nL, g * cps);
     const int n = min(nL, c_begin + cps) - c_begin;
     const PrefixShare share = prefix_share(g, P.G, nL, cps);
     const int n1 = share.b - share.a;  // phase-1 chunks: this CTA's share of the segment sums
+    // handover slot of chunk c (processing order) of this sequence: the bf16
+    // state operand, then z_c
+    auto chunk_slot = [&](int c) { return P.chunks + ((size_t)bh * nC + c) * kChunkSlot; };
 
     constexpr uint32_t idP = tc::idesc_f16<kFp16>(128, 128, false, false);
     constexpr uint32_t idOX = tc::idesc_f16<kFp16>(128, kNX, false, true);  // phi~(Q) [S | z]
@@ -455,12 +487,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 w[0] = (lane < 16) ? z : 0.f;
                 tc::tmem_st32(tmem + cS + loff + 64, w);
             }
+            if (P.chunks && n > 0 && lane < 16)
+                reinterpret_cast<float*>(chunk_slot(c_begin) + kSAtom)[srow] = kNorm ? z : 0.f;
         }
         tc::fence_proxy_async();
     }
     tc::tc_fence_before();
     __syncthreads();  // prefix state in place
     tc::tc_fence_after();
+    if (P.chunks && n > 0 && tid == 0) {  // the first chunk's state operand to the handover
+        tc::bulk_store(chunk_slot(c_begin), sm + L::sb, kSAtom);
+        tc::bulk_commit();
+    }
 
     // ============================================================ phase 2
     if (warp == kWarpProducer) {
@@ -646,13 +684,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                     if (lane < 16) {
                         float zc8[8] = {zv, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                         store_chunk<kFp16>(sbn + kD * kD * 2, srow, 0, zc8);
+                        if (P.chunks && i + 1 < n) reinterpret_cast<float*>(chunk_slot(c + 1) + kSAtom)[srow] = zv;
                     }
                 }
             }
             tc::fence_proxy_async();
             tc::tc_fence_before();
             tc::bar_sync(kBarCompute, kComputeThreads);
-            if (tid == 0) tc::mbar_arrive(&bars[B_SBDONE]);
+            if (tid == 0) {
+                tc::mbar_arrive(&bars[B_SBDONE]);
+                if (P.chunks && i + 1 < n) {  // the next chunk's state operand to the handover
+                    tc::bulk_store(chunk_slot(c + 1), sm + L::sb + ((i + 1) & 1) * L::sbuf, kSAtom);
+                    tc::bulk_commit();
+                }
+            }
             }
             if (i + 1 < n) {
                 ok = mask_p(i + 1);
@@ -673,7 +718,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             {
                 // O' and its normaliser column carry phi(q) unscaled: o = s O' / max(s Z', clamp)
                 float inv = m_row * p.scale;
-                if (kNorm) inv = inv / max_nan(p.scale * zi, p.clamp_min);
+                if (kNorm) {
+                    const float zc = max_nan(p.scale * zi, p.clamp_min);
+                    inv = inv / zc;
+                    if (P.zc && hf == 0 && act(c) * kC + row < p.N) P.zc[(int64_t)bh * p.N + act(c) * kC + row] = zc;
+                }
 #pragma unroll
                 for (int x = 0; x < 32; ++x) o[x] *= inv;
 #pragma unroll
@@ -741,6 +790,17 @@ cudaError_t launch(const ScanParams& p, cudaStream_t st) {
     const void* kern = reinterpret_cast<const void*>(&fwd_kernel<kFp16, kNorm, kDecay, kRev>);
     P.G = pick_segments(p, kern, kFwdThreads, L::total + 1024);
     P.cps = (nC + P.G - 1) / P.G;
+    if (p.seg_out) {
+        const HandLayout hl(p.B * p.H, p.N, P.G, !kDecay);
+        char* base = reinterpret_cast<char*>(p.seg_out);
+        P.hdr = reinterpret_cast<int*>(base);
+        P.nl = reinterpret_cast<int*>(base + hl.nl);
+        P.off = reinterpret_cast<int*>(base + hl.off);
+        if (!kDecay) {
+            P.chunks = reinterpret_cast<uint8_t*>(base + hl.chunks);
+            if (kNorm) P.zc = reinterpret_cast<float*>(base + hl.zc);
+        }
+    }
     void* args[] = {&P};
     return launch_cluster(kern, P.G, p.B * p.H, kFwdThreads, L::total + 1024, st, args);
 }

@@ -436,11 +436,135 @@ __device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
     return __uint_as_float(r);
 }
 
+// ------------------------------------------------ forward -> backward handover
+// The tensor-core forward fills the caller's segment_states buffer with what
+// the backward of the same inputs would otherwise recompute:
+//   header, 64 ints:  [0] segment count G of the forward's cluster split
+//                     [1] kHandMagic  [2] B*H  [3] N  [4] flags (kHand*)
+//                     [5] arrival count of the forward's CTAs (prefix pass)
+//                     [6] kHandMagic once the live-chunk prefix is written
+//   segment states:   per (sequence, segment) the fp32 [S | z] at the
+//                     segment's start, 64 rows of 65
+//   live chunks:      nL[B*H] and their exclusive prefix off[B*H + 1]
+//   chunk states:     per (sequence, chunk in processing order) the bf16
+//                     state operand S_c the forward's MMA read (a 64 x 64
+//                     128-byte-swizzled tile, 8 KB) and z_c (64 fp32)
+//   normalisers:      per token the clamped denominator Zc (fp32, [B*H, N])
+// The chunk states and normalisers are written by the undecayed kernels only
+// (kHandChunks); the one-pass backward needs them and the forward's output.
+constexpr int kHandMagic = 0x53514834;  // "SQH4"
+constexpr int kHandReverse = 1, kHandNormalize = 2, kHandDecay = 4, kHandChunks = 8;
+constexpr uint32_t kSAtom = kD * kD * 2;            // bf16 64 x 64 state operand
+constexpr size_t kChunkSlot = kSAtom + kD * 4 + 0;  // + z_c (64 fp32) = 8448 bytes
+
+struct HandLayout {
+    size_t seg, nl, off, chunks, zc, total;
+    __host__ __device__ static size_t a256(size_t x) { return (x + 255) / 256 * 256; }
+    __host__ __device__ HandLayout(int BH, int N, int G, bool chunk_data) {
+        const size_t nC = (size_t)(N + kC - 1) / kC;
+        seg = 256;
+        nl = seg + a256((size_t)BH * G * kD * (kD + 1) * sizeof(float));
+        off = nl + a256((size_t)BH * sizeof(int));
+        chunks = off + a256((size_t)(BH + 1) * sizeof(int));
+        zc = chunks + (chunk_data ? (size_t)BH * nC * kChunkSlot : 0);
+        total = zc + (chunk_data ? a256((size_t)BH * N * sizeof(float)) : 0);
+    }
+};
+
+__host__ __device__ inline int hand_flags(int reverse, int normalize, int decay_mode, bool chunks) {
+    return (reverse ? kHandReverse : 0) | (normalize ? kHandNormalize : 0) | (decay_mode ? kHandDecay : 0) |
+           (chunks ? kHandChunks : 0);
+}
+
+// Exclusive prefix of n ints (src) into dst[0..n], dst[n] = the total, by one
+// block; `scratch` is 33 ints of shared memory. Loads bypass L1 (the values
+// were written by other CTAs of the same launch).
+__device__ __forceinline__ void block_prefix(const int* src, int* dst, int n, int* scratch) {
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, w = tid >> 5, nw = (nt + 31) >> 5;
+    int carry = 0;
+    for (int base = 0; base < n; base += nt) {
+        const int i = base + tid;
+        const int x = i < n ? __ldcg(src + i) : 0;
+        int y = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, y, o);
+            if (lane >= o) y += t;
+        }
+        if (lane == 31) scratch[w] = y;
+        __syncthreads();
+        if (tid == 0) {
+            int acc = 0;
+            for (int k = 0; k < nw; ++k) {
+                const int t = scratch[k];
+                scratch[k] = acc;
+                acc += t;
+            }
+            scratch[32] = acc;
+        }
+        __syncthreads();
+        if (i < n) dst[i] = carry + scratch[w] + y - x;
+        carry += scratch[32];
+        __syncthreads();
+    }
+    if (tid == 0) dst[n] = carry;
+}
+
+// Grid-wide work plan of the one-pass backward: the live chunks of all
+// sequences, in sequence order, cut into R equal ranges; CTA r takes the
+// positions [w0(r), w0(r + 1)). A range runs over pieces: the part of one
+// sequence that falls in it.
+struct Plan {
+    const int* off;  // [BH + 1] live chunks before each sequence
+    int BH, R;
+    int64_t T;
+    __device__ int64_t w0(int r) const { return (int64_t)r * T / R; }
+    // the sequence holding position w < T (never an empty one)
+    __device__ int seq_at(int64_t w) const {
+        int lo = 0, hi = BH - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (__ldg(off + mid) <= w) lo = mid;
+            else hi = mid - 1;
+        }
+        return lo;
+    }
+};
+
+// Walks the chunks of one CTA's range: pieces in sequence order, the chunks
+// of a piece from its last one down (processing order within the sequence).
+struct Cursor {
+    int s, a, e, j;  // piece: sequence s, chunks [a, e); j chunks of it done
+    int64_t w, w1;   // piece start and range end (positions)
+    __device__ void begin(const Plan& pl, int r) {
+        w = pl.w0(r);
+        w1 = pl.w0(r + 1);
+        if (w < w1) piece(pl);
+    }
+    __device__ void piece(const Plan& pl) {
+        s = pl.seq_at(w);
+        const int o0 = __ldg(pl.off + s), o1 = __ldg(pl.off + s + 1);
+        a = (int)(w - o0);
+        e = (int)(min(w1, (int64_t)o1) - o0);
+        j = 0;
+    }
+    __device__ int chunk() const { return e - 1 - j; }
+    __device__ bool first() const { return j == 0; }
+    __device__ void next(const Plan& pl) {
+        if (a + ++j >= e) {
+            w = __ldg(pl.off + s) + e;
+            if (w < w1) piece(pl);
+        }
+    }
+};
+
 // Launch plumbing (scan_tc.cu).
 struct Maps;
 bool make_map(CUtensorMap* m, const void* base, int dtype, int N, int H, int B, int64_t sn, int64_t sh, int64_t sb);
 int pick_segments(const ScanParams& p, const void* kern, int threads, size_t smem);
 int* status_ptr();  // device address of the status word (current device)
+int fwd_segment_count(const ScanParams& p);
+int bwd1_grid(const ScanParams& p);  // CTAs of the one-pass backward
 cudaError_t launch_cluster(const void* kern, int G, int BH, int threads, size_t smem, cudaStream_t st, void** args);
 
 }  // namespace tcs

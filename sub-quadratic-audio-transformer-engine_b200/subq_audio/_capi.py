@@ -20,6 +20,7 @@ SUBQ_ERR_UNSUPPORTED = 3
 SUBQ_ERR_CUDA = 4
 SUBQ_ERR_TIMEOUT = 5
 SUBQ_ERR_WORKSPACE = 6
+SUBQ_ERR_STATE = 7
 
 SUBQ_FP32, SUBQ_FP16, SUBQ_BF16, SUBQ_FP64 = 0, 1, 2, 3
 SUBQ_DECAY_NONE, SUBQ_DECAY_SCALAR, SUBQ_DECAY_PER_HEAD, SUBQ_DECAY_PER_TOKEN = 0, 1, 2, 3
@@ -70,6 +71,7 @@ class BwdArgs(ctypes.Structure):
         ("dlog_gamma", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("stream", ctypes.c_void_p), ("segment_states", ctypes.c_void_p),
+        ("out", Tensor4),
     ]
 
 

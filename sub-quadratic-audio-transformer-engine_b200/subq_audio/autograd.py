@@ -145,9 +145,10 @@ class _CausalScan(torch.autograd.Function):
         seg = ops.SegmentStates()  # handed to the backward, which then skips recomputing them
         o, st = ops.scan_forward(q, k, v, log_gamma=lg, mask=mask_u8, normalize=True, state=state,
                                  return_state=want_state, reverse=reverse, segments=seg)
+        seg.out = None  # the output is saved below (autograd checks it is not modified in place)
         ctx.reverse = reverse
         ctx.seg = seg
-        ctx.save_for_backward(q, k, v, lg if isinstance(lg, torch.Tensor) else None, mask_u8)
+        ctx.save_for_backward(q, k, v, lg if isinstance(lg, torch.Tensor) else None, mask_u8, o)
         ctx.lg_is_tensor = isinstance(lg, torch.Tensor)
         ctx.state = state
         if want_state:
@@ -157,12 +158,12 @@ class _CausalScan(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do, _dS=None, _dz=None):
-        q, k, v, lg, mask_u8 = ctx.saved_tensors
+        q, k, v, lg, mask_u8, o = ctx.saved_tensors
         need_lg = ctx.lg_is_tensor and ctx.needs_input_grad[3]
         # dO in any layout with a contiguous last dimension (the kernels take strides)
         dq, dk, dv, dlg = ops.scan_backward(q, k, v, do, log_gamma=lg, mask=mask_u8,
                                             normalize=True, state=ctx.state, need_dlog_gamma=need_lg,
-                                            reverse=ctx.reverse, segments=ctx.seg)
+                                            reverse=ctx.reverse, segments=ctx.seg, forward_out=o)
         glg = None
         if need_lg:
             glg = dlg.to(lg.dtype)

@@ -127,14 +127,19 @@ def _workspace(nbytes: int, device: torch.device, keep: list) -> Tuple[int, int]
 
 
 class SegmentStates:
-    """Carrier of the segment-start states from a forward to the backward of
-    the same inputs: pass one instance as ``segments=`` to ``scan_forward``
-    (which fills it on the tensor-core path) and then to ``scan_backward``
-    (which then skips recomputing those states). An empty or mismatched
-    carrier is ignored by the backward."""
+    """Carrier of what a forward hands to the backward of the same inputs:
+    pass one instance as ``segments=`` to ``scan_forward`` (which fills it on
+    the tensor-core path: the states at the start of each segment and, without
+    decay, the state before every chunk and the per-token normalisers) and
+    then to ``scan_backward``. With the forward's output as well (``out``, set
+    by ``scan_forward``, or ``forward_out=`` of ``scan_backward``) an
+    undecayed backward runs in one pass from them; a decayed one skips
+    recomputing the segment states. The forward must be the same call's:
+    a carrier from other inputs gives wrong gradients."""
 
     def __init__(self) -> None:
         self.buf: Optional[torch.Tensor] = None
+        self.out: Optional[torch.Tensor] = None
 
 
 def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma: LogGamma = None,
@@ -184,6 +189,7 @@ def scan_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, log_gamma
             segments.buf = torch.empty(nbytes, dtype=torch.uint8, device=q.device) if nbytes else None
             if segments.buf is not None:
                 a.segment_states = segments.buf.data_ptr()
+            segments.out = o
         _capi.fwd(a)
     return o, ((S_out, z_out) if return_state else None)
 
@@ -193,9 +199,12 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
                   scale: Optional[float] = None, clamp_min: float = 1e-5,
                   state: Optional[Tuple[torch.Tensor, Optional[torch.Tensor]]] = None,
                   need_dlog_gamma: bool = False, flush_subnormal: bool = False, path: str = "auto",
-                  reverse: bool = False, segments: Optional[SegmentStates] = None):
+                  reverse: bool = False, segments: Optional[SegmentStates] = None,
+                  forward_out: Optional[torch.Tensor] = None):
     """Gradients of ``scan_forward``. Returns ``(dq, dk, dv, dlog_gamma | None)``;
-    dlog_gamma is float32 [B,H,N] (d loss / d log gamma_t per token)."""
+    dlog_gamma is float32 [B,H,N] (d loss / d log gamma_t per token).
+    ``segments`` (and ``forward_out``, else ``segments.out``) come from the
+    forward of the same call; see ``SegmentStates``."""
     _require_cuda(q, k, v, dout)
     q, k, v, dout = _inner_contig(q), _inner_contig(k), _inner_contig(v), _inner_contig(dout)
     _check_kv(q, k, v)
@@ -225,9 +234,17 @@ def scan_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch
             dlg = torch.empty((B, H, N), dtype=torch.float32, device=q.device)
             a.dlog_gamma = dlg.data_ptr()
         a.stream = torch.cuda.current_stream(q.device).cuda_stream
-        a.workspace, a.workspace_bytes = _workspace(_capi.bwd_workspace_bytes(a), q.device, keep)
         if segments is not None and segments.buf is not None and segments.buf.device == q.device:
             a.segment_states = segments.buf.data_ptr()
+            fo = forward_out if forward_out is not None else segments.out
+            if fo is not None:
+                if tuple(fo.shape) != (B, H, N, e) or fo.dtype != q.dtype or fo.device != q.device:
+                    raise ValueError("forward_out must be the forward's [B, H, N, e] output")
+                fo = _inner_contig(fo)
+                keep.append(fo)
+                a.out = _t4(fo)
+        # (after the handover fields: they decide the kernel path and its workspace)
+        a.workspace, a.workspace_bytes = _workspace(_capi.bwd_workspace_bytes(a), q.device, keep)
         _capi.bwd(a)
     return dq, dk, dv, dlg
 

@@ -37,15 +37,16 @@ def test_struct_layout_matches_header(tmp_path):
     src = tmp_path / "layout.c"
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "kernels.hpp"\n'
-        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(subq_tensor4), sizeof(subq_scan_desc),"
+        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(subq_tensor4), sizeof(subq_scan_desc),"
         " sizeof(subq_fwd_args), sizeof(subq_bwd_args), offsetof(subq_scan_desc, log_gamma),"
-        " offsetof(subq_fwd_args, state_in), offsetof(subq_bwd_args, dlog_gamma));return 0;}\n")
+        " offsetof(subq_fwd_args, state_in), offsetof(subq_bwd_args, dlog_gamma),"
+        " offsetof(subq_bwd_args, out));return 0;}\n")
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-x", "c", "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe)], check=True)
     got = list(map(int, subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()))
     want = [ctypes.sizeof(_capi.Tensor4), ctypes.sizeof(_capi.ScanDesc), ctypes.sizeof(_capi.FwdArgs),
             ctypes.sizeof(_capi.BwdArgs), _capi.ScanDesc.log_gamma.offset, _capi.FwdArgs.state_in.offset,
-            _capi.BwdArgs.dlog_gamma.offset]
+            _capi.BwdArgs.dlog_gamma.offset, _capi.BwdArgs.out.offset]
     assert got == want
 
 
@@ -64,7 +65,7 @@ def _fwd_args(B=1, H=1, N=8, d=4, e=4, dtype=_capi.SUBQ_FP32):
 
 def test_abi_version_and_error_text():
     lib = _capi.load()
-    assert lib.subq_abi_version() == 3
+    assert lib.subq_abi_version() == 4
     a = _fwd_args()
     a.desc.head_dim = 0
     assert lib.subq_fwd(ctypes.byref(a)) == _capi.SUBQ_ERR_INVALID_ARGUMENT

@@ -320,8 +320,11 @@ def test_feature_map_known_answers():
 
 @pytest.mark.parametrize("decay,H,N", [(None, 8, 4000), ("token", 1, 3000), (None, 2, 700)])
 def test_backward_with_forward_segment_states_is_unchanged(decay, H, N):
-    """The backward given the forward's segment-start states (skipping its own
-    recomputation of them) returns the same gradients as without them."""
+    """The backward given the forward's handover (the segment-start states; and,
+    without decay, the per-chunk states and normalisers for the one-pass
+    backward) returns the same gradients as without it: equal up to rounding
+    with decay (the same kernel, states not recomputed), within bf16 rounding
+    without (a different kernel)."""
     B = 2
     q, k, v, do, lg, m, st = make_case(B, H, N, 64, 64, torch.bfloat16, seed=61 + N, decay=decay, mask=True,
                                        state=True)
@@ -337,4 +340,4 @@ def test_backward_with_forward_segment_states_is_unchanged(decay, H, N):
     assert ops.last_path() == "tensorcore"
     for x, y in zip(got, ref):
         if y is not None:
-            assert rel_err(x, y.double().cpu().numpy()) < 1e-3
+            assert rel_err(x, y.double().cpu().numpy()) < (1e-3 if decay else 1e-2)
