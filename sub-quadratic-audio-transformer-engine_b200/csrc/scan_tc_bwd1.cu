@@ -709,6 +709,7 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
                 const uint32_t qa = sbase + s * LA::stage + LA::q, oa = sbase + s * LA::stage + LA::g;
                 const uint32_t ca = sbase + s * LA::stage + LA::ct;
                 const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024), dbo = tc::sdesc_sw128(oa, kTile, 1024);
+                #pragma unroll 1
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
                     tc::mma_f16(tmem, dqt + kk * 128, dbo + kk * 128, idS64, acc);
