@@ -181,18 +181,19 @@ int subq_feature_map(void* x, int64_t n, int32_t dtype, void* stream);
  * the reference, whose backward allocates its scratch on every call). For
  * callers that may not supply or grow device memory per call, such as a
  * real-time audio callback or a host with a fixed device budget: the scratch
- * is a static 8 MiB device buffer of the library, sized by
- * subq_bwd_workspace_bytes: 8 bytes per token-head (B x H x N) on the
- * tensor-core path (1,048,576 token-heads), 12 with per-token decay (plus 4
- * bytes per sequence) and on the float32 exact path (699,050 token-heads),
- * and grouped K/V adds dK and dV per query head. Larger calls return
- * SUBQ_ERR_WORKSPACE. `workspace` and `workspace_bytes` of args are ignored.
- * Nothing in the buffer needs to start at zero (what must, the call clears
- * itself). There is
- * one buffer per device, so calls that overlap in time on one device race:
- * serialise them. The first call on a device looks the buffer up with that
- * device current; make it before capturing any of the device's streams.
- * Results equal subq_bwd's. */
+ * is a static 8 MiB device buffer of the library. A call fits when
+ * subq_bwd_workspace_bytes(args) <= 8 MiB: the recomputing tensor-core path
+ * takes 8 bytes per token-head (B x H x N; 1,048,576 token-heads), 12 with
+ * per-token decay (plus 4 bytes per sequence) and on the float32 exact path
+ * (699,050), 24 on the float64 exact path (349,525); the one-pass backward
+ * (segment_states and out given) takes a fixed 16.6 KB per SM (about 2.5 MB on
+ * a B200) whatever the length; grouped K/V adds dK and dV per query head.
+ * Larger calls return SUBQ_ERR_WORKSPACE. `workspace` and `workspace_bytes` of
+ * args are ignored. Nothing in the buffer needs to start at zero (what must,
+ * the call clears itself). There is one buffer per device, so calls that
+ * overlap in time on one device race: serialise them. The first call on a
+ * device looks the buffer up with that device current; make it before
+ * capturing any of the device's streams. Results equal subq_bwd's. */
 int subq_bwd_noalloc(const subq_bwd_args* args);
 
 /* Synchronises `stream`, then reads and clears the device status word of the

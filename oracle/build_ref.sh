@@ -10,9 +10,14 @@
 # The reference's own build system (CMake + FetchContent) is not used; with no
 # USE_CUDA/USE_HIP define its HAL header selects the host fallback.
 set -euo pipefail
-REF=${SUBQ_REFERENCE_ROOT:-/root/reference}
+# The reference tree is named by SUBQ_REFERENCE_ROOT (required).
+REF=${SUBQ_REFERENCE_ROOT:-}
 HERE=$(cd "$(dirname "$0")" && pwd)
 OUT="$HERE/_ref"
+if [ -z "$REF" ]; then
+  echo "SUBQ_REFERENCE_ROOT is not set: point it at the reference tree to build oracle/_ref" >&2
+  exit 0
+fi
 if [ ! -d "$REF/src/kernels" ]; then
   echo "reference tree not found at $REF; oracle/_ref not rebuilt" >&2
   exit 0

@@ -346,16 +346,19 @@ int subq_device_info(int device, char* arch, size_t arch_len, size_t* memory_byt
 // when the module loads, so the call itself allocates nothing.
 //
 //  * Capacity: kNoAllocScratchBytes = 8 MiB against subq_bwd_workspace_bytes:
-//    1,048,576 token-heads (B x H x N) on the tensor-core path (8 bytes each),
-//    about 699,000 with per-token decay (12 bytes each plus a flag per
-//    sequence) and on the float32 exact path (12 bytes each); grouped K/V adds
-//    dK and dV per query head. A larger call is rejected with
-//    SUBQ_ERR_WORKSPACE before anything is launched.
+//    1,048,576 token-heads (B x H x N) on the recomputing tensor-core path (8
+//    bytes each), about 699,000 with per-token decay (12 bytes each plus a
+//    flag per sequence) and on the float32 exact path (12 bytes each), about
+//    349,000 on the float64 exact path (24 bytes each); the one-pass backward
+//    (given the forward's handover) takes a fixed 16.6 KB per SM whatever the
+//    length; grouped K/V adds dK and dV per query head. A larger call is
+//    rejected with SUBQ_ERR_WORKSPACE before anything is launched.
 //  * Nothing in the scratch has to start at zero when the call begins: every
 //    call writes each per-token entry it later reads (the clamped normaliser
-//    and the quotient coefficient, or the exact path's per-token values)
-//    before reading it, and the decayed path clears its per-sequence fallback
-//    flags itself (a memset on the call's stream, not an allocation).
+//    and the quotient coefficient, the exact path's per-token values, or the
+//    one-pass backward's adjoint sums) before reading it, and the decayed
+//    path clears its per-sequence fallback flags itself (a memset on the
+//    call's stream, not an allocation).
 //  * One buffer per device: calls that overlap in time on one device (two
 //    streams, or host threads without ordering between them) race on it, so
 //    such callers must serialise their calls.

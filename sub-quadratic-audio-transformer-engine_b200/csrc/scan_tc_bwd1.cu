@@ -71,13 +71,14 @@ enum {
     F_TDONE = 2,         // [2] feature map -> MMA: q^, k^, z tile
     F_OUT = 4,           // [2] compute -> producer: dq, dk, dv staged over the stage's dO, k, v tiles
     F_OC = 6,            // [2] compute -> MMA: o^ (over dO) and the c tile of the stage
-    F_MFULL = 8,         // MMA -> compute, feature map: P^T, dA^T
+    F_MFULL = 8,         // MMA -> feature map: P^T
     F_MDONEP = 9,        // feature map -> MMA: P^T masked (bf16 in place)
     F_MDONEA = 10,       // compute -> MMA: dA^T masked (bf16 in place and in shared memory)
     F_DSFULL = 11,       // MMA -> compute: the chunk's MMAs done ([dS | dz] after it)
     F_EPI = 12,          // compute -> MMA: dV, dK, dQ~ read
     F_DSB = 13,          // compute -> MMA: bf16 dS and the dz tile of the later tokens in place
-    F_COUNT = 14
+    F_MFULLA = 14,       // MMA -> compute: dA^T
+    F_COUNT = 15
 };
 
 // TMEM: P^T [0,128) (bf16 in [0,64), then dV in [64,128)), dA^T [128,256)
@@ -87,7 +88,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t cPT = 0, cDAT = 128, cDQ = 256, cDS = 320;
 
 struct Bwd1Params {
-    CUtensorMap tm_q, tm_k, tm_v, tm_g, tm_dq, tm_dk, tm_dv;
+    CUtensorMap tm_q, tm_k, tm_v, tm_g, tm_dq, tm_dk, tm_dv, tm_fo;
     ScanParams p;
     Plan pl;
     const int* hdr;          // handover header (checked against this call)
@@ -308,11 +309,12 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                     const uint64_t dv = tc::sdesc_sw128(va, 16, 1024), dob = tc::sdesc_sw128(oa, 16, 1024);
                     #pragma unroll 1
                     for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + cPT, dk + kk * 2, dq + kk * 2, idPP, kk > 0);
+                    tc::mma_commit(&bars[F_MFULL]);
                     #pragma unroll 1
                     for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + cDAT, dv + kk * 2, dob + kk * 2, idPP, kk > 0);
                     if (kNorm) tc::mma_f16(tmem + cDAT, sdesc_sw32(oneA), sdesc_sw32(ca), idPP, 1u);
                 }
-                tc::mma_commit(&bars[F_MFULL]);
+                tc::mma_commit(&bars[F_MFULLA]);
                 ok = wait_bar(&bars[F_MDONEP], i & 1, P.status);
                 if (ok) ok = wait_bar(&bars[F_DSB], i & 1, P.status);
                 if (!ok) break;
@@ -533,7 +535,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             Cursor cn = cu;
             cn.next(pl);  // the next chunk
             // (1) mask dA^T (also into shared memory for dQ~); the feature-map warps mask P^T
-            if (!cwait(&bars[F_MFULL], i & 1)) break;
+            if (!cwait(&bars[F_MFULLA], i & 1)) break;
             mask_tile(cDAT, true);
             tc::tmem_wait_st();
             publish(&bars[F_MDONEA]);
@@ -596,11 +598,11 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
 //    CTAs of the sequence start from);
 //  * every CTA zeroes dq, dk, dv of its share of the dead chunks (those after
 //    each sequence's last live token), with TMA stores of a zero tile.
-constexpr int kAdjStages = 4;
+constexpr int kAdjStages = 3;
 struct LA {
-    // stage: q^ and o^ (over dO), the c tile
-    static constexpr uint32_t q = 0, g = kTile, ct = 2 * kTile;
-    static constexpr uint32_t stage = 2 * kTile + kMTile;
+    // stage: q^, o^ (over dO), the forward's output o, the c tile
+    static constexpr uint32_t q = 0, g = kTile, o = 2 * kTile, ct = 3 * kTile;
+    static constexpr uint32_t stage = 3 * kTile + kMTile;
     static constexpr uint32_t zt = kAdjStages * stage;  // zero tile
     static constexpr uint32_t dx = zt + kTile;          // [2][256] partial dot products
     static constexpr uint32_t bars = dx + 2048;
@@ -681,8 +683,9 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
                 if (u >= 1) ok = wait_bar(&bars[A_EMPTY + s], (u - 1) & 1, P.status);
                 if (!ok) break;
                 uint8_t* base = sm + s * LA::stage;
-                tc::mbar_arrive_expect_tx(&bars[A_FULL + s], 2 * kTile);
+                tc::mbar_arrive_expect_tx(&bars[A_FULL + s], (kNorm ? 3u : 2u) * kTile);
                 tc::tma_load_4d(base + LA::g, &P.tm_g, 0, mem_chunk(i) * kC, h, b, &bars[A_FULL + s]);
+                if (kNorm) tc::tma_load_4d(base + LA::o, &P.tm_fo, 0, mem_chunk(i) * kC, h, b, &bars[A_FULL + s]);
                 tc::tma_load_4d(base + LA::q, &P.tm_q, 0, mem_chunk(i) * kC, h, b, &bars[A_FULL + s]);
             }
         }
@@ -728,24 +731,19 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
         const int row = quad * 32 + lane, srow = quad * 16 + lane;
         const uint32_t loff = (uint32_t)(quad * 32) << 16;
         float* dxs = reinterpret_cast<float*>(sm + LA::dx);
-        for (int i = 0; i < n && ok; ++i) {
-            const int s = i % kAdjStages, u = i / kAdjStages;
+        // mask and normaliser of a row of chunk i (the normaliser one chunk ahead)
+        auto row_info = [&](int i, float& m, float& zc) {
             const int t = mem_chunk(i) * kC + row;
             const bool in = t < p.N;
-            const float m = in ? (p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f) : 0.f;
-            uint4 ov[4];
-            float zc = 1.f;
-            if (kNorm && m != 0.f) {  // in flight during the wait
-                const uint4* src = reinterpret_cast<const uint4*>(
-                    reinterpret_cast<const typename E::T*>(p.fo) + (int64_t)b * p.fo_sb + (int64_t)h * p.fo_sh +
-                    (int64_t)t * p.fo_sn + hf * 32);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) ov[j] = __ldg(src + j);
-                zc = __ldg(P.zc + (int64_t)sq * p.N + t);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) ov[j] = make_uint4(0, 0, 0, 0);
-            }
+            m = in ? (p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f) : 0.f;
+            zc = (kNorm && m != 0.f) ? __ldg(P.zc + (int64_t)sq * p.N + t) : 1.f;
+        };
+        float m_next = 0.f, zc_next = 1.f;
+        if (n > 0) row_info(0, m_next, zc_next);
+        for (int i = 0; i < n && ok; ++i) {
+            const int s = i % kAdjStages, u = i / kAdjStages;
+            const float m = m_next, zc = zc_next;
+            if (i + 1 < n) row_info(i + 1, m_next, zc_next);
             ok = tc::bar_and(kBarCompute, kComputeThreads, wait_bar(&bars[A_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
             uint8_t* gt = sm + s * LA::stage + LA::g;
@@ -753,16 +751,11 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
             load_chunks<kFp16>(gt, row, hf * 4, 4, go);
             float inv = m;
             if (kNorm) {
+                float ov[32];
+                load_chunks<kFp16>(sm + s * LA::stage + LA::o, row, hf * 4, 4, ov);
                 float dot = 0.f;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const typename E::T2* o2 = reinterpret_cast<const typename E::T2*>(&ov[j]);
-#pragma unroll
-                    for (int y = 0; y < 4; ++y) {
-                        const float2 bb = E::to2(o2[y]);
-                        dot = fmaf(go[8 * j + 2 * y], bb.x, fmaf(go[8 * j + 2 * y + 1], bb.y, dot));
-                    }
-                }
+                for (int x = 0; x < 32; ++x) dot = fmaf(go[x], ov[x], dot);
                 dxs[(i & 1) * 256 + hf * 128 + row] = dot;
                 tc::bar_sync(kBarCompute, kComputeThreads);
                 const float full = dxs[(i & 1) * 256 + row] + dxs[(i & 1) * 256 + 128 + row];
@@ -815,7 +808,8 @@ cudaError_t launch1(const ScanParams& p, cudaStream_t st, int* launches) {
         !make_map(&P.tm_g, p.g, dt, p.N, p.H, p.B, p.g_sn, p.g_sh, p.g_sb) ||
         !make_map(&P.tm_dq, p.o, dt, p.N, p.H, p.B, p.o_sn, p.o_sh, p.o_sb) ||
         !make_map(&P.tm_dk, p.dk, dt, p.N, p.H, p.B, p.dk_sn, p.dk_sh, p.dk_sb) ||
-        !make_map(&P.tm_dv, p.dv, dt, p.N, p.H, p.B, p.dv_sn, p.dv_sh, p.dv_sb))
+        !make_map(&P.tm_dv, p.dv, dt, p.N, p.H, p.B, p.dv_sn, p.dv_sh, p.dv_sb) ||
+        !make_map(&P.tm_fo, p.fo, dt, p.N, p.H, p.B, p.fo_sn, p.fo_sh, p.fo_sb))
         return cudaErrorInvalidValue;
     P.status = status_ptr();
     if (!P.status) return cudaErrorInvalidDevice;

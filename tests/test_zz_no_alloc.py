@@ -22,12 +22,10 @@ def _case(B, H, N, d, dtype, seed):
     return q, k, v, do, mask
 
 
-def _noalloc_backward(q, k, v, do, mask, log_gamma=None):
-    """One subq_bwd_noalloc call: the caller provides inputs and outputs only
-    (with a per-token decay also the d log(gamma) output, returned last)."""
+def _noalloc_args(q, k, v, do, mask, log_gamma=None, seg=None, keep=None):
     B, H, N, d = q.shape
-    keep = []
-    dq, dk, dv = (torch.empty_like(q) for _ in range(3))
+    keep = [] if keep is None else keep
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     a = _capi.BwdArgs()
     a.desc = ops._desc(q, v, log_gamma, mask, True, None, 1e-5, False, "auto", keep)
     dlg = None
@@ -36,10 +34,20 @@ def _noalloc_backward(q, k, v, do, mask, log_gamma=None):
         a.dlog_gamma = dlg.data_ptr()
     a.q, a.k, a.v, a.dout = ops._t4(q), ops._t4(k), ops._t4(v), ops._t4(do)
     a.dq, a.dk, a.dv = ops._t4(dq), ops._t4(dk), ops._t4(dv)
+    if seg is not None:  # the forward's handover and output: the one-pass backward
+        a.segment_states = seg.buf.data_ptr()
+        a.out = ops._t4(seg.out)
     a.stream = torch.cuda.current_stream().cuda_stream
     a.workspace, a.workspace_bytes = None, 0
+    return a, (dq, dk, dv) if log_gamma is None else (dq, dk, dv, dlg)
+
+
+def _noalloc_backward(q, k, v, do, mask, log_gamma=None, seg=None):
+    """One subq_bwd_noalloc call: the caller provides inputs and outputs only
+    (with a per-token decay also the d log(gamma) output, returned last)."""
+    a, outs = _noalloc_args(q, k, v, do, mask, log_gamma, seg)
     _capi.bwd_noalloc(a)
-    return (dq, dk, dv) if log_gamma is None else (dq, dk, dv, dlg)
+    return outs
 
 
 @pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 64), (torch.float32, 16)])
@@ -90,3 +98,49 @@ def test_noalloc_backward_rejects_calls_above_its_scratch():
     for x, y in zip(got, ref):
         assert torch.equal(x, y)
     assert math.isfinite(got[0].float().abs().max().item())
+
+
+def test_noalloc_backward_grouped_kv_equals_subq_bwd_twice():
+    """Grouped K/V: the static scratch also holds dK, dV per query head until
+    the group sums read them back (a second kernel reading the scratch)."""
+    g = torch.Generator().manual_seed(41)
+    B, H, Hkv, N = 2, 4, 2, 900
+    q, do = (torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).cuda() for _ in range(2))
+    k, v = (torch.randn(B, Hkv, N, 64, generator=g).to(torch.bfloat16).cuda() for _ in range(2))
+    mask = (torch.arange(N)[None, :] < torch.tensor([N, 600])[:, None]).cuda()
+    ref = ops.scan_backward(q, k, v, do, mask=mask)[:3]
+    assert ops.last_path() == "tensorcore"
+    for _ in range(2):
+        got = _noalloc_backward(q, k, v, do, mask)
+        torch.cuda.synchronize()
+        for x, y in zip(got, ref):
+            assert torch.equal(x, y)
+    # one token above what fits: the grouped buffers make each token-head 264 bytes
+    n_big = 64
+    while True:
+        qb = torch.zeros(1, H, n_big, 64, dtype=torch.bfloat16, device="cuda")
+        kb = torch.zeros(1, Hkv, n_big, 64, dtype=torch.bfloat16, device="cuda")
+        a, _ = _noalloc_args(qb, kb, kb, qb, None)
+        if _capi.bwd_workspace_bytes(a) > (8 << 20):
+            break
+        n_big *= 2
+    with pytest.raises(_capi.SubqError) as err:
+        _capi.bwd_noalloc(a)
+    assert err.value.code == _capi.SUBQ_ERR_WORKSPACE
+
+
+def test_noalloc_one_pass_backward_equals_subq_bwd_twice():
+    """With the forward's handover and output the backward runs in one pass;
+    its scratch (the adjoint sums of the CTAs' first pieces) is then a fixed
+    size, whatever the sequence length."""
+    q, k, v, do, mask = _case(3, 4, 5000, 64, torch.bfloat16, seed=53)
+    seg = ops.SegmentStates()
+    ops.scan_forward(q, k, v, mask=mask, segments=seg)
+    ref = ops.scan_backward(q, k, v, do, mask=mask, segments=seg)[:3]
+    assert ops.last_launches() == 2  # the one-pass backward
+    for _ in range(2):
+        got = _noalloc_backward(q, k, v, do, mask, seg=seg)
+        torch.cuda.synchronize()
+        assert ops.last_launches() == 2
+        for x, y in zip(got, ref):
+            assert torch.equal(x, y)
