@@ -30,6 +30,13 @@ public:
                           void* dK, void* dV, size_t batch, size_t seq_len, size_t d_model,
                           float decay_factor, const float* S0, void* stream);
 
+    // Synchronises `stream` and raises std::runtime_error when the device
+    // status word records that a bounded device-side wait gave up
+    // (SUBQ_ERR_TIMEOUT) or that a backward was handed another call's forward
+    // state (SUBQ_ERR_STATE) since the last check: the outputs of the calls in
+    // between are not valid. The status word is read and cleared.
+    void check_device(void* stream = nullptr);
+
     MemoryArena& arena() { return arena_; }
 
 private:

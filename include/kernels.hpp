@@ -196,11 +196,21 @@ int subq_feature_map(void* x, int64_t n, int32_t dtype, void* stream);
  * capturing any of the device's streams. Results equal subq_bwd's. */
 int subq_bwd_noalloc(const subq_bwd_args* args);
 
-/* Synchronises `stream`, then reads and clears the device status word of the
- * current device: SUBQ_OK, or SUBQ_ERR_TIMEOUT when a bounded device-side wait
- * of a tensor-core kernel gave up since the last query (its outputs are then
- * not valid). Returns SUBQ_ERR_CUDA if the synchronisation itself fails. */
+/* Reads and clears (in one atomic step, ordered on `stream`) the device status
+ * word of the current device, then synchronises `stream`: SUBQ_OK, or
+ * SUBQ_ERR_TIMEOUT when a bounded device-side wait of a tensor-core kernel gave
+ * up since the last query, or SUBQ_ERR_STATE when a backward was given the
+ * segment_states of another call's forward (the outputs are then not valid).
+ * Returns SUBQ_ERR_CUDA if the launch or the synchronisation fails. */
 int subq_device_status(void* stream, int* status);
+
+/* Diagnostic (no counterpart in the reference): launches one block whose
+ * bounded device-side wait - the one every tensor-core kernel uses on its
+ * pipeline barriers - waits on a barrier that nothing arrives at, with its
+ * limit shortened to `polls` (1..2^20) polls. It gives up and records
+ * SUBQ_ERR_TIMEOUT in the device status word, as a stalled kernel would, so
+ * that a caller can test its handling of subq_device_status without a fault. */
+int subq_selftest_wait_timeout(int polls, void* stream);
 
 /* Kernel path the last successful subq_fwd / subq_bwd of this thread ran. */
 int subq_last_path(void);

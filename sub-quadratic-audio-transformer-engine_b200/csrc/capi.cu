@@ -207,6 +207,14 @@ int subq_device_status(void* stream, int* status) {
 
 int subq_last_launches(void) { return g_last_launches; }
 
+int subq_selftest_wait_timeout(int polls, void* stream) {
+    if (polls < 1 || polls > (1 << 20)) return fail(SUBQ_ERR_INVALID_ARGUMENT, "polls must be in [1, 2^20]");
+    cudaError_t err = subq::tc_selftest_wait_timeout(polls, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail_cuda(err, "subq_selftest_wait_timeout launch");
+    g_last_launches = 1;
+    return SUBQ_OK;
+}
+
 size_t subq_fwd_workspace_bytes(const subq_fwd_args* a) {
     subq::ScanParams p;
     if (fill_fwd(a, p) != SUBQ_OK) return 0;

@@ -130,6 +130,7 @@ public:
                 }
                 arena_.set_offset(saved);
                 check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+                engine_.check_device();
             }
             return out;
         } catch (const std::exception& e) {

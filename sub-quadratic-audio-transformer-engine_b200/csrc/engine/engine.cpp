@@ -49,6 +49,19 @@ struct ArenaMark {
 
 Engine::Engine(MemoryArena& arena) : arena_(arena) {}
 
+void Engine::check_device(void* stream) {
+    int st = SUBQ_OK;
+    const int rc = subq_device_status(stream, &st);
+    if (rc != SUBQ_OK) throw_status(rc);
+    if (st == SUBQ_ERR_TIMEOUT)
+        throw std::runtime_error("a bounded device-side wait of a tensor-core kernel gave up (SUBQ_ERR_TIMEOUT); "
+                                 "the outputs since the last check are not valid");
+    if (st != SUBQ_OK)
+        throw std::runtime_error("device status " + std::to_string(st) +
+                                 ": a backward was given the forward state of another call; its gradients are "
+                                 "not valid");
+}
+
 void Engine::forward(AttentionContext& ctx, void* stream) {
     if (ctx.Q.dimensions.size() != 3) throw std::invalid_argument("Q must be [batch, seq_len, d_model]");
     const size_t B = ctx.Q.dimensions[0], N = ctx.Q.dimensions[1], D = ctx.Q.dimensions[2];
@@ -139,7 +152,7 @@ float Engine::backward_engine(const void* dO, const void* Q, const void* K, cons
         check_cuda(cudaMemcpyAsync(host.data(), dlg, sizeof(float) * host.size(), cudaMemcpyDeviceToHost, st),
                    "cudaMemcpyAsync (d_gamma)");
     }
-    check_cuda(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    check_device(stream);  // synchronises the stream
     double acc = 0.0;
     for (float x : host) acc += x;
     return (float)(acc / gamma);

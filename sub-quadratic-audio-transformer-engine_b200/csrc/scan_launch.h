@@ -35,5 +35,7 @@ size_t bwd1_workspace_bytes(const ScanParams& p);
 cudaError_t launch_bwd1(const ScanParams& p, int dtype, cudaStream_t st, int* launches);
 // Device-side status word of the tensor-core kernels (bounded waits).
 cudaError_t tc_read_status(cudaStream_t st, int* status);
+// Diagnostic bounded wait that runs out (see subq_selftest_wait_timeout).
+cudaError_t tc_selftest_wait_timeout(int polls, cudaStream_t st);
 
 }  // namespace subq

@@ -11,15 +11,22 @@
 namespace subq {
 
 // First error code raised by a bounded device-side wait of the tensor-core
-// kernels (SUBQ_ERR_TIMEOUT), read and cleared by subq_device_status.
+// kernels (SUBQ_ERR_TIMEOUT) or by a backward given another call's forward
+// handover (SUBQ_ERR_STATE); read and cleared by subq_device_status.
 __device__ int g_tc_status;
+// Where the read-and-clear kernel leaves the value it took.
+__device__ int g_tc_status_taken;
 
 namespace tcs {
 
+// Device address of the status word, looked up once per device (on the
+// device's first tensor-core launch or status query) under a lock.
 int* status_ptr() {
+    static std::mutex mu;
     static int* ptrs[64] = {nullptr};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
     if (!ptrs[dev]) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_tc_status) != cudaSuccess) return nullptr;
@@ -27,6 +34,28 @@ int* status_ptr() {
     }
     return ptrs[dev];
 }
+
+namespace {
+// Takes the status word and clears it in one atomic step (a timeout recorded
+// by a kernel on another stream is not lost between a read and a clear).
+__global__ void status_take_kernel() { g_tc_status_taken = atomicExch(&g_tc_status, 0); }
+
+// Diagnostic: one bounded wait on a barrier that nothing arrives at, with the
+// limit shortened to `polls`; it gives up and records SUBQ_ERR_TIMEOUT.
+__global__ void wait_timeout_kernel(int polls) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&bar, 1);
+        tc::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        bool done = false;
+        for (int i = 0; i < polls && !done; ++i) done = tc::mbar_test_wait(&bar, 0);
+        if (!done) atomicCAS(&g_tc_status, 0, (int)SUBQ_ERR_TIMEOUT);
+    }
+}
+}  // namespace
 
 cudaError_t launch_fwd_v2(const ScanParams& p, int dtype, cudaStream_t st);
 int fwd_segment_count(const ScanParams& p);
@@ -220,15 +249,18 @@ cudaError_t launch_bwd_tc(const ScanParams& p, int dtype, cudaStream_t st, int* 
 
 cudaError_t tc_read_status(cudaStream_t st, int* status) {
     int v = 0;
-    cudaError_t err = cudaMemcpyFromSymbolAsync(&v, g_tc_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+    tcs::status_take_kernel<<<1, 1, 0, st>>>();
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess)
+        err = cudaMemcpyFromSymbolAsync(&v, g_tc_status_taken, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
     if (err == cudaSuccess) err = cudaStreamSynchronize(st);
-    if (err == cudaSuccess && v != 0) {
-        const int zero = 0;
-        err = cudaMemcpyToSymbolAsync(g_tc_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
-        if (err == cudaSuccess) err = cudaStreamSynchronize(st);
-    }
     *status = v;
     return err;
+}
+
+cudaError_t tc_selftest_wait_timeout(int polls, cudaStream_t st) {
+    tcs::wait_timeout_kernel<<<1, 32, 0, st>>>(polls);
+    return cudaGetLastError();
 }
 
 }  // namespace subq

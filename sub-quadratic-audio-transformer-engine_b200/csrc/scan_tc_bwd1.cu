@@ -290,7 +290,8 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
         }
     } else if (warp == kWarpMma) {
         // ------------------------------------------------------------- MMA
-        if (lane == 0) {
+        // (the whole warp runs this, converged; one elected lane issues each MMA)
+        {
             const uint32_t dsa = sbase + L1::dsb, oneA = sbase + L1::ones, dza = sbase + L1::dzt;
             const uint32_t daa = sbase + L1::da;
             for (int i = 0; i < n && ok; ++i) {
@@ -301,6 +302,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 ok = wait_bar(&bars[F_TDONE + s], u & 1, P.status);
                 if (ok) ok = wait_bar(&bars[F_OC + s], u & 1, P.status);
                 if (ok && i >= 1) ok = wait_bar(&bars[F_EPI], (i - 1) & 1, P.status);
+                ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc::tc_fence_after();
                 // P^T = K^ q^^T ; dA^T = V o^^T + 1 c^T
@@ -308,15 +310,16 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                     const uint64_t dk = tc::sdesc_sw128(ka, 16, 1024), dq = tc::sdesc_sw128(qa, 16, 1024);
                     const uint64_t dv = tc::sdesc_sw128(va, 16, 1024), dob = tc::sdesc_sw128(oa, 16, 1024);
                     #pragma unroll 1
-                    for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + cPT, dk + kk * 2, dq + kk * 2, idPP, kk > 0);
-                    tc::mma_commit(&bars[F_MFULL]);
+                    for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cPT, dk + kk * 2, dq + kk * 2, idPP, kk > 0);
+                    tc::mma_commit_w(&bars[F_MFULL]);
                     #pragma unroll 1
-                    for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + cDAT, dv + kk * 2, dob + kk * 2, idPP, kk > 0);
-                    if (kNorm) tc::mma_f16(tmem + cDAT, sdesc_sw32(oneA), sdesc_sw32(ca), idPP, 1u);
+                    for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cDAT, dv + kk * 2, dob + kk * 2, idPP, kk > 0);
+                    if (kNorm) tc::mma_f16_w(tmem + cDAT, sdesc_sw32(oneA), sdesc_sw32(ca), idPP, 1u);
                 }
-                tc::mma_commit(&bars[F_MFULLA]);
+                tc::mma_commit_w(&bars[F_MFULLA]);
                 ok = wait_bar(&bars[F_MDONEP], i & 1, P.status);
                 if (ok) ok = wait_bar(&bars[F_DSB], i & 1, P.status);
+                ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc::tc_fence_after();
                 const uint64_t dkm = tc::sdesc_sw128(ka, kTile, 1024), dqm = tc::sdesc_sw128(qa, kTile, 1024);
@@ -327,39 +330,40 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 // dV = P^T o^ + K^ dS   (A = bf16 P^T from TMEM, 8 columns per 16 tokens)
                 #pragma unroll 1
                 for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts(tmem + cPT + 64, tmem + cPT + kk * 8, dom + kk * 128, idKM64, kk > 0);
+                    tc::mma_f16_ts_w(tmem + cPT + 64, tmem + cPT + kk * 8, dom + kk * 128, idKM64, kk > 0);
                 #pragma unroll 1
-                for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + cPT + 64, dk + kk * 2, dsm + kk * 128, idKM64, 1u);
+                for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cPT + 64, dk + kk * 2, dsm + kk * 128, idKM64, 1u);
                 // dQ~ = o^ S_c^T + c z_c^T (before dA^T is masked)
                 #pragma unroll 1
-                for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + cDQ, dob + kk * 2, dsat + kk * 2, idKK64, kk > 0);
-                if (kNorm) tc::mma_f16(tmem + cDQ, sdesc_sw32(ca), sdesc_sw32(za), idKK64, 1u);
+                for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cDQ, dob + kk * 2, dsat + kk * 2, idKK64, kk > 0);
+                if (kNorm) tc::mma_f16_w(tmem + cDQ, sdesc_sw32(ca), sdesc_sw32(za), idKK64, 1u);
                 ok = wait_bar(&bars[F_MDONEA], i & 1, P.status);
+                ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc::tc_fence_after();
                 // dK~ = dA^T q^ + V dS^T + 1 dz^T
                 #pragma unroll 1
                 for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts(tmem + cDAT + 64, tmem + cDAT + kk * 8, dqm + kk * 128, idKM64, kk > 0);
+                    tc::mma_f16_ts_w(tmem + cDAT + 64, tmem + cDAT + kk * 8, dqm + kk * 128, idKM64, kk > 0);
                 #pragma unroll 1
-                for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + cDAT + 64, dv + kk * 2, dsk + kk * 2, idKK64, 1u);
-                if (kNorm) tc::mma_f16(tmem + cDAT + 64, sdesc_sw32(oneA), sdesc_sw32(dza), idKK64, 1u);
+                for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cDAT + 64, dv + kk * 2, dsk + kk * 2, idKK64, 1u);
+                if (kNorm) tc::mma_f16_w(tmem + cDAT + 64, sdesc_sw32(oneA), sdesc_sw32(dza), idKK64, 1u);
                 // dQ~ += dA K^  (A = masked dA^T in shared memory, read as dA: MN-major over queries)
                 {
                     const uint64_t dda = tc::sdesc_sw128(daa, kTile, 1024);
                     #pragma unroll 1
-                    for (int kk = 0; kk < 8; ++kk) tc::mma_f16(tmem + cDQ, dda + kk * 128, dkm + kk * 128, idMM64, 1u);
+                    for (int kk = 0; kk < 8; ++kk) tc::mma_f16_w(tmem + cDQ, dda + kk * 128, dkm + kk * 128, idMM64, 1u);
                 }
                 // [dS | dz] += q^^T [o^ | c]  (M = 64: dS from the o^ tile, dz from the c tile)
                 {
                     const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024);
                     #pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk) {
-                        tc::mma_f16(tmem + cDS, dqt + kk * 128, dom + kk * 128, idS64, 1u);
-                        if (kNorm) tc::mma_f16(tmem + cDS + 64, dqt + kk * 128, sdesc_sw32(ca + kk * 512), idZ16, 1u);
+                        tc::mma_f16_w(tmem + cDS, dqt + kk * 128, dom + kk * 128, idS64, 1u);
+                        if (kNorm) tc::mma_f16_w(tmem + cDS + 64, dqt + kk * 128, sdesc_sw32(ca + kk * 512), idZ16, 1u);
                     }
                 }
-                tc::mma_commit(&bars[F_DSFULL]);
+                tc::mma_commit_w(&bars[F_DSFULL]);
             }
         }
         __syncwarp();
@@ -703,10 +707,10 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
             if (r == 0) tc::mbar_arrive(&bars[A_TDONE + s]);
         }
     } else if (warp == kWarpMma) {
-        if (lane == 0) {
+        {  // warp-converged; one elected lane issues
             for (int i = 0; i < n && ok; ++i) {
                 const int s = i % kAdjStages, u = i / kAdjStages;
-                ok = wait_bar(&bars[A_TDONE + s], u & 1, P.status);
+                ok = __all_sync(0xffffffffu, wait_bar(&bars[A_TDONE + s], u & 1, P.status));
                 if (!ok) break;
                 tc::tc_fence_after();
                 const uint32_t qa = sbase + s * LA::stage + LA::q, oa = sbase + s * LA::stage + LA::g;
@@ -715,12 +719,12 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
                 #pragma unroll 1
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                    tc::mma_f16(tmem, dqt + kk * 128, dbo + kk * 128, idS64, acc);
-                    if (kNorm) tc::mma_f16(tmem + 64, dqt + kk * 128, sdesc_sw32(ca + kk * 512), idZ16, acc);
+                    tc::mma_f16_w(tmem, dqt + kk * 128, dbo + kk * 128, idS64, acc);
+                    if (kNorm) tc::mma_f16_w(tmem + 64, dqt + kk * 128, sdesc_sw32(ca + kk * 512), idZ16, acc);
                 }
-                tc::mma_commit(&bars[A_EMPTY + s]);
+                tc::mma_commit_w(&bars[A_EMPTY + s]);
             }
-            if (n > 0 && ok) tc::mma_commit(&bars[A_DONE]);
+            if (n > 0 && ok) tc::mma_commit_w(&bars[A_DONE]);
         }
         __syncwarp();
     } else if (warp < 8) {

@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         const uint32_t n80 = kNorm ? idSX : tc::idesc_f16<kFp16>(64, 64, true, true);
         const uint64_t da = tc::sdesc_sw128(ka, kTile, 1024), db = tc::sdesc_sw128(va, lbo, 1024);
         for (int kk = 0; kk < 8; ++kk)  // a K-step of 16 tokens is 2048 bytes on (a descriptor step of 128)
-            tc::mma_f16(tmem + col, da + kk * 128, db + kk * 128, n80, (first && kk == 0) ? 0u : 1u);
+            tc::mma_f16_w(tmem + col, da + kk * 128, db + kk * 128, n80, (first && kk == 0) ? 0u : 1u);
     };
 
     // Chunk of pipeline slot j: phase-1 slots (j < n1) visit the share in an
@@ -287,26 +287,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     } else if (warp >= 8 && warp < 12) {
         transform(0, n1);
     } else if (warp == kWarpMma) {
-        if (kDecay && lane == 0) {
+        // (the whole warp runs the MMA role, converged; one elected lane issues)
+        if (kDecay) {
             // decayed sums: each chunk's phi~(K')^T [V | 1] into one of two
             // buffers in the O' columns; the compute warps chain them
             for (int j = 0; j < n1 && ok; ++j) {
                 const int s = j % kStages, u = j / kStages;
                 ok = wait_bar(&bars[B_TDONE + s], u & 1, P.status);
                 if (ok && j >= 2) ok = wait_bar(&bars[B_UDONE + (j & 1)], ((j >> 1) - 1) & 1, P.status);
+                ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc::tc_fence_after();
                 mma_state(s, true, cO + (j & 1) * kNX);
-                tc::mma_commit(&bars[B_EMPTY + s]);
-                tc::mma_commit(&bars[B_UFULL + (j & 1)]);
+                tc::mma_commit_w(&bars[B_EMPTY + s]);
+                tc::mma_commit_w(&bars[B_UFULL + (j & 1)]);
             }
-        } else if (lane == 0) {
+        } else {
             // the share's two partial sums accumulate in S' (before the segment
             // boundary) and in the still unused P columns (after it)
             bool first1 = true, first2 = true;
             for (int j = 0; j < n1 && ok; ++j) {
                 const int s = j % kStages, u = j / kStages;
-                ok = wait_bar(&bars[B_TDONE + s], u & 1, P.status);
+                ok = __all_sync(0xffffffffu, wait_bar(&bars[B_TDONE + s], u & 1, P.status));
                 if (!ok) break;
                 tc::tc_fence_after();
                 if (chunk_of(j) < share.x) {
@@ -316,9 +318,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                     mma_state(s, first2, cP);
                     first2 = false;
                 }
-                tc::mma_commit(&bars[B_EMPTY + s]);
+                tc::mma_commit_w(&bars[B_EMPTY + s]);
             }
-            if (n1 > 0 && ok) tc::mma_commit(&bars[B_SFULL]);
+            if (n1 > 0 && ok) tc::mma_commit_w(&bars[B_SFULL]);
         }
         __syncwarp();
     }
@@ -507,17 +509,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     } else if (warp >= 8 && warp < 12) {
         transform(n1, n1 + n);
     } else if (warp == kWarpMma) {
-        if (lane == 0) {
+        {  // warp-converged; one elected lane issues each MMA
             auto issue_p = [&](int i) -> bool {  // P[i % 2] = phi~(Q) phi~(K)^T
                 const int j = n1 + i, s = j % kStages, u = j / kStages, bf = i & 1;
-                if (!wait_bar(&bars[B_TDONE + s], u & 1, P.status)) return false;
-                if (i >= 2 && !wait_bar(&bars[B_PSDONE + bf], ((i >> 1) - 1) & 1, P.status)) return false;
+                if (!__all_sync(0xffffffffu, wait_bar(&bars[B_TDONE + s], u & 1, P.status))) return false;
+                if (i >= 2 && !__all_sync(0xffffffffu, wait_bar(&bars[B_PSDONE + bf], ((i >> 1) - 1) & 1, P.status)))
+                    return false;
                 tc::tc_fence_after();
                 const uint64_t dq = tc::sdesc_sw128(sbase + s * L::stage + L::q, 16, 1024);
                 const uint64_t dk = tc::sdesc_sw128(sbase + s * L::stage + L::k, 16, 1024);
                 for (int kk = 0; kk < 4; ++kk)  // 16 features are 32 bytes on (a descriptor step of 2)
-                    tc::mma_f16(tmem + cP + bf * 128, dq + kk * 2, dk + kk * 2, idP, kk > 0);
-                tc::mma_commit(&bars[B_PFULL + bf]);
+                    tc::mma_f16_w(tmem + cP + bf * 128, dq + kk * 2, dk + kk * 2, idP, kk > 0);
+                tc::mma_commit_w(&bars[B_PFULL + bf]);
                 return true;
             };
             if (n > 0) ok = issue_p(0);
@@ -526,29 +529,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 // [S|z]_c+1 first: the compute warps turn it into the next chunk's
                 // bf16 operand while this chunk's other MMAs run. It may start once
                 // the previous refresh has read S' (and written sb[i % 2]).
-                if (i >= 1) ok = wait_bar(&bars[B_SBDONE], (i - 1) & 1, P.status);
+                if (i >= 1) ok = __all_sync(0xffffffffu, wait_bar(&bars[B_SBDONE], (i - 1) & 1, P.status));
                 if (!ok) break;
                 tc::tc_fence_after();
                 mma_state(s, kDecay);  // with decay: this chunk's sum alone, chained in registers
-                tc::mma_commit(&bars[B_SFULL]);
+                tc::mma_commit_w(&bars[B_SFULL]);
                 if (i + 1 < n) ok = issue_p(i + 1);
                 if (ok) ok = wait_bar(&bars[B_PSDONE + bf], pu & 1, P.status);
                 if (ok && i >= 2) ok = wait_bar(&bars[B_ODONE + bf], (pu - 1) & 1, P.status);
+                ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc::tc_fence_after();
                 const uint32_t tOb = tmem + cO + bf * kNX;
                 const uint64_t dq = tc::sdesc_sw128(sbase + s * L::stage + L::q, 16, 1024);
                 const uint64_t dsb = tc::sdesc_sw128(sbase + L::sb + (i & 1) * L::sbuf, kD * kD * 2, 1024);
                 for (int kk = 0; kk < 4; ++kk)  // [O | Zi] = phi~(Q) [S_c | z_c]
-                    tc::mma_f16(tOb, dq + kk * 2, dsb + kk * 128, kNorm ? idOX : idO, kk > 0);
+                    tc::mma_f16_w(tOb, dq + kk * 2, dsb + kk * 128, kNorm ? idOX : idO, kk > 0);
                 // [O | Zi] += P [V | 1]: bf16 P read from TMEM (8 columns per 16 tokens);
                 // the ones column adds the causal row sums to the normaliser
                 const uint32_t lbo = kNorm ? L::ones - (s * L::stage + L::v) : kTile;
                 const uint64_t dv = tc::sdesc_sw128(sbase + s * L::stage + L::v, lbo, 1024);
                 for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts(tOb, tmem + cP + bf * 128 + kk * 8, dv + kk * 128, kNorm ? idOX : idO, 1u);
-                tc::mma_commit(&bars[B_OFULL + bf]);
-                tc::mma_commit(&bars[B_EMPTY + s]);
+                    tc::mma_f16_ts_w(tOb, tmem + cP + bf * 128 + kk * 8, dv + kk * 128, kNorm ? idOX : idO, 1u);
+                tc::mma_commit_w(&bars[B_OFULL + bf]);
+                tc::mma_commit_w(&bars[B_EMPTY + s]);
             }
         }
         __syncwarp();

@@ -31,7 +31,7 @@ EXPORTED = (
     "subq_fwd", "subq_bwd", "subq_fwd_workspace_bytes", "subq_bwd_workspace_bytes",
     "subq_feature_map", "subq_last_path", "subq_last_launches", "subq_last_error",
     "subq_abi_version", "subq_device_info", "subq_device_status", "subq_bwd_noalloc",
-    "subq_segment_states_bytes",
+    "subq_segment_states_bytes", "subq_selftest_wait_timeout",
 )
 
 
@@ -122,6 +122,8 @@ def load() -> ctypes.CDLL:
             lib.subq_device_info.restype = ctypes.c_int
             lib.subq_device_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
             lib.subq_device_status.restype = ctypes.c_int
+            lib.subq_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_void_p]
+            lib.subq_selftest_wait_timeout.restype = ctypes.c_int
             _lib = lib
     return _lib
 
@@ -164,6 +166,11 @@ def device_status(stream: int = 0) -> int:
     st = ctypes.c_int(0)
     check(load().subq_device_status(ctypes.c_void_p(stream), ctypes.byref(st)))
     return int(st.value)
+
+
+def selftest_wait_timeout(polls: int = 1000, stream: int = 0) -> None:
+    """subq_selftest_wait_timeout: a bounded device-side wait that runs out."""
+    check(load().subq_selftest_wait_timeout(int(polls), ctypes.c_void_p(stream)))
 
 
 def last_path() -> int:

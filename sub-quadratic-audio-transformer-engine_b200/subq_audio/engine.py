@@ -64,7 +64,9 @@ class AudioTransformerEngine:
                 Qc, Kc, Vc = Q.contiguous().float(), K.contiguous().float(), V.contiguous().float()
                 O = torch.empty_like(Qc)
                 B, N, D = Qc.shape
-                torch.cuda.current_stream(Qc.device).synchronize()
+                from . import ops
+
+                ops.check_device_status(Qc.device)  # synchronises the inputs' stream
                 self._engine.forward_raw(Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), O.data_ptr(),
                                          int(B), int(N), int(D), float(decay_factor))
                 return O.to(Q.dtype)
@@ -90,13 +92,19 @@ class AudioTransformerEngine:
                 out = SubQAttentionFunction.apply(q, k, v, w)
                 (out * dO).sum().backward()
                 dw = float(w.grad.item()) if w.grad is not None else 0.0
+                if q.is_cuda:  # (.item() has synchronised) a device-side wait that gave up raises here
+                    from . import ops
+
+                    ops.check_device_status(q.device)
                 return (q.grad.contiguous().to(Q.dtype), k.grad.contiguous().to(Q.dtype),
                         v.grad.contiguous().to(Q.dtype), dw / (gamma * (1.0 - gamma)))
             if Q.is_cuda and getattr(dO, "is_cuda", False):
                 dOc, Qc, Kc, Vc = (x.contiguous().float() for x in (dO, Q, K, V))
                 dQ, dK, dV = torch.empty_like(Qc), torch.empty_like(Kc), torch.empty_like(Vc)
                 B, N, D = Qc.shape
-                torch.cuda.current_stream(Qc.device).synchronize()
+                from . import ops
+
+                ops.check_device_status(Qc.device)  # synchronises the inputs' stream
                 d_decay = self._engine.backward_raw(dOc.data_ptr(), Qc.data_ptr(), Kc.data_ptr(), Vc.data_ptr(),
                                                     dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(),
                                                     int(B), int(N), int(D), float(decay_factor))

@@ -319,6 +319,25 @@ def feature_map_(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
+def check_device_status(device: Optional[torch.device] = None) -> None:
+    """Synchronises the current stream of ``device`` (default: the current
+    device) and raises ``SubqError`` when, since the last check, a bounded
+    device-side wait of a tensor-core kernel gave up (SUBQ_ERR_TIMEOUT) or a
+    backward was given the handover of another call's forward
+    (SUBQ_ERR_STATE): the outputs of the calls in between are then not valid.
+    The scan launches themselves never synchronise; callers check at their own
+    synchronisation points (``AudioTransformerEngine`` does)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        st = _capi.device_status(torch.cuda.current_stream(dev).cuda_stream)
+    if st == _capi.SUBQ_ERR_TIMEOUT:
+        raise _capi.SubqError(st, "a bounded device-side wait of a tensor-core kernel gave up "
+                                  "(SUBQ_ERR_TIMEOUT); the outputs since the last check are not valid")
+    if st != _capi.SUBQ_OK:
+        raise _capi.SubqError(st, f"device status {st}: a backward was given the forward state of another "
+                                  "call; its gradients are not valid")
+
+
 def last_path() -> str:
     return {0: "auto", 1: "exact", 2: "tensorcore"}.get(_capi.last_path(), "?")
 
