@@ -17,6 +17,13 @@ path): weak scaling; time = max over ranks of the device-timed region.
 takes its slice; with 8 ranks one sequence of H=8 heads each, which the
 kernels spread over clusters of up to 8 CTAs per head).
 
+  python bench.py --impl reference [--steps K] [--warmup W]
+
+times the reference's own C++ engine (its float32 CPU build, oracle/_ref) on
+the host's cores: each step is one rank's batch, B x H head-sequences each
+run at the live length the GPU step masks it to, forward + backward; step i
+takes rank (i mod N)'s lengths; the time is the wall clock of each step.
+
   python bench.py --workload encoder [--seq-len 16384] [--batch 4]
 
 prints a second kind of line (not the default): one training step of the
@@ -320,52 +327,91 @@ def encoder_main(args, rank, world, local_rank):
 
 # --------------------------------------------------------------------------
 # Reference CPU arm: the reference's own C++ engine (built from its sources
-# into oracle/_ref), forward + backward on one (b,h) head-sequence per task.
+# into oracle/_ref, float32). A step is one rank's batch as the GPU step sees
+# it: B x H head-sequences, each run at its live length (the key-padding
+# length the GPU step masks with), forward + backward through
+# SubQEngine.forward / .backward, one process per host core, longest first.
 # --------------------------------------------------------------------------
-def _ref_task(args):
-    seed, n, d = args
+_REF = {}
+
+
+def live_lengths(rank, strong=False):
+    """Key-padding lengths U[N/2, N] of one rank's B sequences (weak scaling:
+    seed 4321 + rank; strong scaling: the shared batch, seed 4321)."""
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(4321 if strong else 4321 + rank)
+    return torch.randint(N // 2, N + 1, (B,), generator=g)
+
+
+def _ref_init():
     import numpy as np
 
     sys.path.insert(0, os.path.join(REPO, "oracle", "_ref"))
     import _C  # the reference's pybind module (CPU build)
 
-    rng = np.random.default_rng(seed)
-    q, k, v, do = (rng.standard_normal((1, n, d)).astype(np.float32) for _ in range(4))
-    eng = _C.SubQEngine(64 * 1024 * 1024)
-    t0 = time.perf_counter()
-    eng.forward(q, k, v, 1.0)
-    eng.backward(do, q, k, v, 1.0)
-    return time.perf_counter() - t0
+    rng = np.random.default_rng(os.getpid())
+    _REF["eng"] = _C.SubQEngine(64 * 1024 * 1024)  # forward/backward reset its arena per call
+    _REF["x"] = [rng.standard_normal((1, N, D)).astype(np.float32) for _ in range(4)]
 
 
-# One head-sequence (N=8192) takes about 0.3 s through the reference engine on
-# one core; 32 per core keeps a sample near 10 s of wall time.
-CPU_TASKS_PER_CORE = 32
+def _ref_task(n):
+    q, k, v, do = (x[:, :n] for x in _REF["x"])
+    _REF["eng"].forward(q, k, v, 1.0)
+    _REF["eng"].backward(do, q, k, v, 1.0)
+    return n
 
 
-def cpu_reference(tasks_per_core=CPU_TASKS_PER_CORE, cores=None):
-    """Times the reference CPU path on a bounded sample; returns (tokens/s, info)."""
-    import multiprocessing as mp
+class RefPool:
+    """The reference engine on every host core (spawned workers, started
+    before this process makes its first CUDA call)."""
 
-    ref_so = [f for f in os.listdir(os.path.join(REPO, "oracle", "_ref")) if f.startswith("_C")] \
-        if os.path.isdir(os.path.join(REPO, "oracle", "_ref")) else []
-    if not ref_so:
-        return None, {"unavailable": "oracle/_ref was not built"}
-    cores = cores or os.cpu_count() or 1
-    ntask = cores * tasks_per_core
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(cores) as pool:
-        pool.map(_ref_task, [(1, 256, D)] * cores)  # warm the workers
+    def __init__(self):
+        import multiprocessing as mp
+
+        self.cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+        self.pool = mp.get_context("spawn").Pool(self.cores, initializer=_ref_init)
+        self.pool.map(_ref_task, [256] * self.cores, chunksize=1)
+
+    def step(self, lens):
+        """Seconds of wall time for one batch at these live lengths."""
+        tasks = sorted((int(n) for n in lens for _ in range(H)), reverse=True)
         t0 = time.perf_counter()
-        pool.map(_ref_task, [(100 + i, N, D) for i in range(ntask)])
-        wall = time.perf_counter() - t0
-    # one (b,h) sequence of N tokens is 1/H of a token's work (a token has H heads)
-    tokens = ntask * N / H
-    return tokens / wall, {"kind": "reference", "cores": cores,
-                           "sample": f"{ntask} head-sequences (N={N}, d={D}) through the reference C++ "
-                                     f"SubQEngine.forward+backward (float32, one process per core), "
-                                     f"scaled to tokens of {H} heads",
-                           "wall_s": round(wall, 3)}
+        self.pool.map(_ref_task, tasks, chunksize=1)
+        return time.perf_counter() - t0
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def ref_unavailable():
+    d = os.path.join(REPO, "oracle", "_ref")
+    if not os.path.isdir(d) or not any(f.startswith("_C") for f in os.listdir(d)):
+        return "oracle/_ref was not built"
+    return None
+
+
+def ref_sample_text(cores, steps, lens_note):
+    return (f"{steps} steps, each one rank's batch: {B}x{H} head-sequences (d={D}) at their live lengths "
+            f"({lens_note}), through the reference C++ SubQEngine.forward+backward (float32), "
+            f"{cores} processes, one per core")
+
+
+def cpu_reference(steps=2):
+    """The reference CPU path on rank 0's batch (a bounded sample: two steps);
+    returns (tokens/s, info)."""
+    why = ref_unavailable()
+    if why:
+        return None, {"unavailable": why}
+    pool = RefPool()
+    lens = live_lengths(0).tolist()
+    walls = [pool.step(lens) for _ in range(steps)]
+    pool.close()
+    wall = sum(walls)
+    return B * N * steps / wall, {"kind": "reference", "cores": pool.cores,
+                                  "sample": ref_sample_text(pool.cores, steps, "rank 0's lengths"),
+                                  "wall_s": round(wall, 3)}
 
 
 # --------------------------------------------------------------------------
@@ -450,25 +496,33 @@ def main():
         return encoder_main(args, rank, world, local_rank)
 
     if args.impl == "reference":
-        if rank != 0:
+        if rank != 0:  # rank 0 alone times the reference; the others exit without work
             return 0
-        # each "step" is one bounded sample of the workload on all host cores
-        vals = []
-        info = {}
-        for _ in range(max(1, args.warmup // 3)):
-            cpu_reference(tasks_per_core=CPU_TASKS_PER_CORE)
-        for _ in range(args.steps if args.steps <= 3 else 3):
-            v, info = cpu_reference(tasks_per_core=CPU_TASKS_PER_CORE)
-            if v is None:
-                print(json.dumps({"impl": "reference", "unavailable": info["unavailable"]}))
-                return 0
-            vals.append(v)
-        val = statistics.median(vals)
+        why = ref_unavailable()
+        if why:
+            print(json.dumps({"impl": "reference", "unavailable": why}))
+            return 0
+        strong = args.scaling == "strong"
+        # step i runs rank (i mod world)'s batch at that rank's live lengths (strong
+        # scaling: the one shared batch); a step is the work one GPU does in one step
+        batches = [live_lengths(0, strong=True).tolist()] if strong else \
+            [live_lengths(r).tolist() for r in range(world)]
+        pool = RefPool()
+        for i in range(args.warmup):
+            pool.step(batches[i % len(batches)])
+        walls = [pool.step(batches[i % len(batches)]) for i in range(args.steps)]
+        pool.close()
+        ms = 1e3 * sum(walls) / len(walls)
+        val = B * N / (ms / 1e3)  # tokens of one step's batch (B sequences of N positions)
+        note = "the shared batch's lengths" if strong else \
+            ("rank 0's lengths" if world == 1 else f"ranks 0..{world - 1}'s lengths in turn")
         line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
-                "steps": len(vals), "warmup": args.warmup, "ms_per_step": B * N / val * 1e3 * world,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "ms_per_step_min": 1e3 * min(walls), "ms_per_step_max": 1e3 * max(walls),
+                "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "config": CONFIG,
-                "cpu_baseline": {"value": val, "unit": UNIT, **info},
+                "cpu_baseline": {"value": val, "unit": UNIT, "kind": "reference", "cores": pool.cores,
+                                 "sample": ref_sample_text(pool.cores, args.steps, note)},
                 "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return 0
@@ -479,7 +533,7 @@ def main():
     # The CPU-baseline pool starts (spawn) before the first GPU call.
     cpu_val, cpu_info = (None, None)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_val, cpu_info = cpu_reference(tasks_per_core=CPU_TASKS_PER_CORE)
+        cpu_val, cpu_info = cpu_reference()
 
     if world > 1:
         torch.cuda.set_device(local_rank)
@@ -496,7 +550,7 @@ def main():
     Bl = B // world if strong else B  # this rank's sequences
     g = torch.Generator(device="cpu").manual_seed(1234 if strong else 1234 + rank)
     q, k, v, do = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16) for _ in range(4))
-    lens = torch.randint(N // 2, N + 1, (B,), generator=g)
+    lens = live_lengths(rank, strong)
     if strong:  # one slice of the shared batch per rank
         sl = slice(rank * Bl, (rank + 1) * Bl)
         q, k, v, do, lens = (x[sl].contiguous() for x in (q, k, v, do, lens))

@@ -23,6 +23,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import library as _library  # noqa: F401  (registers torch.ops.subq_audio)
 from . import ops
 
 StateLike = Optional[Union[torch.Tensor, Tuple[torch.Tensor, ...]]]
@@ -138,32 +139,31 @@ def _split_state(past_state: StateLike):
 class _CausalScan(torch.autograd.Function):
     """One scan direction on the kernels (causal, or reverse time for the
     second direction of the bidirectional scan); differentiable in q, k, v,
-    log_gamma."""
+    log_gamma. Runs the ``subq_audio::scan_fwd`` / ``scan_bwd`` operators
+    (traceable: they carry fake kernels); the forward's handover buffer and
+    output go to the backward, which then runs in one pass."""
 
     @staticmethod
-    def forward(ctx, q, k, v, lg, mask_u8, state, want_state, reverse=False):
-        seg = ops.SegmentStates()  # handed to the backward, which then skips recomputing them
-        o, st = ops.scan_forward(q, k, v, log_gamma=lg, mask=mask_u8, normalize=True, state=state,
-                                 return_state=want_state, reverse=reverse, segments=seg)
-        seg.out = None  # the output is saved below (autograd checks it is not modified in place)
+    def forward(ctx, q, k, v, lg, mask_u8, S0, z0, want_state, reverse=False):
+        lg_t = lg if isinstance(lg, torch.Tensor) else None
+        if lg is not None and lg_t is None:
+            lg_t = torch.tensor(float(lg), dtype=torch.float32, device=q.device)
+        o, S, z, handover = torch.ops.subq_audio.scan_fwd(q, k, v, lg_t, mask_u8, S0, z0, reverse, want_state)
         ctx.reverse = reverse
-        ctx.seg = seg
-        ctx.save_for_backward(q, k, v, lg if isinstance(lg, torch.Tensor) else None, mask_u8, o)
         ctx.lg_is_tensor = isinstance(lg, torch.Tensor)
-        ctx.state = state
+        ctx.save_for_backward(q, k, v, lg_t, mask_u8, S0, z0, o, handover)
         if want_state:
-            ctx.mark_non_differentiable(st[0], st[1])
-            return o, st[0], st[1]
+            ctx.mark_non_differentiable(S, z)
+            return o, S, z
         return o, None, None
 
     @staticmethod
     def backward(ctx, do, _dS=None, _dz=None):
-        q, k, v, lg, mask_u8, o = ctx.saved_tensors
+        q, k, v, lg, mask_u8, S0, z0, o, handover = ctx.saved_tensors
         need_lg = ctx.lg_is_tensor and ctx.needs_input_grad[3]
         # dO in any layout with a contiguous last dimension (the kernels take strides)
-        dq, dk, dv, dlg = ops.scan_backward(q, k, v, do, log_gamma=lg, mask=mask_u8,
-                                            normalize=True, state=ctx.state, need_dlog_gamma=need_lg,
-                                            reverse=ctx.reverse, segments=ctx.seg, forward_out=o)
+        dq, dk, dv, dlg = torch.ops.subq_audio.scan_bwd(q, k, v, do, lg, mask_u8, S0, z0, o, handover,
+                                                        ctx.reverse, need_lg)
         glg = None
         if need_lg:
             glg = dlg.to(lg.dtype)
@@ -171,7 +171,7 @@ class _CausalScan(torch.autograd.Function):
                 glg = glg.sum()
             elif lg.dim() == 1:
                 glg = glg.sum(dim=(0, 2))
-        return dq, dk, dv, glg, None, None, None, None
+        return dq, dk, dv, glg, None, None, None, None, None
 
 
 def _to_device_inputs(q, k, v):
@@ -188,12 +188,12 @@ def _single_direction(q, k, v, decay_w, past_state, valid_mask, want_state, reve
     lg = _log_gamma(decay_w, B, H, T, q.device)
     mask_u8 = _token_mask(valid_mask, B, T, q.device)
     st = _split_state(past_state)
+    S0 = Z0 = None
     if st is not None:
-        S, Z = st
-        S = S.to(device=q.device, dtype=torch.float32)
-        Z = None if Z is None else Z.to(device=q.device, dtype=torch.float32).reshape(B, H, D)
-        st = (S, Z)
-    o, S_next, z_next = _CausalScan.apply(q, k, v, lg, mask_u8, st, want_state, reverse)
+        S0, Z0 = st
+        S0 = S0.detach().to(device=q.device, dtype=torch.float32).reshape(B, H, D, v.shape[-1]).contiguous()
+        Z0 = None if Z0 is None else Z0.detach().to(device=q.device, dtype=torch.float32).reshape(B, H, D).contiguous()
+    o, S_next, z_next = _CausalScan.apply(q, k, v, lg, mask_u8, S0, Z0, want_state, reverse)
     return o, S_next, z_next
 
 
@@ -211,10 +211,11 @@ def chunkwise_flash_linear_attention(q: torch.Tensor, k: torch.Tensor, v: torch.
     return out.contiguous(), S_next
 
 
-def _chunkwise(q, k, v, decay_w, past_state, attention_mask, is_causal):
+def _chunkwise(q, k, v, decay_w, past_state, attention_mask, is_causal, want_state=True):
     """chunkwise_flash_linear_attention with ``out`` in q's memory order (a
     [B, H, T, D] view of a [B, T, H, D] buffer when q is a view of a
-    projection's output), for callers that transpose it back."""
+    projection's output), for callers that transpose it back. Without
+    ``want_state`` the final state is not formed (None is returned for it)."""
     is_3d = q.ndim == 3
     if is_3d:
         q, k, v = q.unsqueeze(1), k.unsqueeze(1), v.unsqueeze(1)
@@ -222,7 +223,7 @@ def _chunkwise(q, k, v, decay_w, past_state, attention_mask, is_causal):
     B, H, T, D = q.shape
     valid_mask = _normalize_attention_mask(
         attention_mask.to(q.device) if attention_mask is not None else None, q.dtype, T)
-    out, S_next, z_next = _single_direction(q, k, v, decay_w, past_state, valid_mask, True)
+    out, S_next, z_next = _single_direction(q, k, v, decay_w, past_state, valid_mask, want_state)
     if not is_causal:
         # Bidirectional: add the reverse-time scan and remove the double-counted
         # diagonal (in normalised linear attention the self term is v). The
@@ -234,8 +235,9 @@ def _chunkwise(q, k, v, decay_w, past_state, attention_mask, is_causal):
         out = out + out_b - diag
         if valid_mask is not None:
             out = out * valid_mask.expand_as(out)
-    S_next = S_next.to(q.device)
-    S_next.Z = z_next.unsqueeze(-1)
+    if want_state:
+        S_next = S_next.to(q.device)
+        S_next.Z = z_next.unsqueeze(-1)
     if is_3d:
         out = out.squeeze(1)
     if home is not None:
@@ -385,7 +387,8 @@ class SubQLinearAttention(nn.Module):
             decay_w = self.raw_decay
         # the scan writes out in Q's memory order ([B, L, H, D] under the [B, H, L, D]
         # view), so the transpose back below needs no copy
-        out, next_state = _chunkwise(Q, K, V, decay_w, past_state, attention_mask, self.is_causal)
+        out, next_state = _chunkwise(Q, K, V, decay_w, past_state, attention_mask, self.is_causal,
+                                     want_state=use_cache)
         if self.head_norm is not None:
             # with the weight in the activations' dtype torch runs its fused RMSNorm
             # kernel (an fp32 weight on bf16 activations takes an unfused path)

@@ -138,13 +138,13 @@ def test_handover_from_another_call_is_reported():
 
 def test_full_size_headline_workload_matches_oracle():
     """The headline workload at its own size, with the benchmark's own inputs:
-    B=8, H=8, N=8192, d=64 bf16, key-padding lengths U[N/2, N] (seed 1234, as
-    bench.py rank 0 draws them), forward + one-pass backward as the
+    B=8, H=8, N=8192, d=64 bf16, key-padding lengths U[N/2, N] (inputs seed 1234,
+    lengths seed 4321, as bench.py rank 0 draws them), forward + one-pass backward as the
     benchmark's step runs them, against the float64 oracle."""
     B, H, N, D = 8, 8, 8192, 64
     g = torch.Generator(device="cpu").manual_seed(1234)
     q, k, v, do = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16) for _ in range(4))
-    lens = torch.randint(N // 2, N + 1, (B,), generator=g)
+    lens = torch.randint(N // 2, N + 1, (B,), generator=torch.Generator(device="cpu").manual_seed(4321))
     m = torch.arange(N)[None, :] < lens[:, None]
     o, dq, dk, dv, launches = _run(q, k, v, do, m, None, True, False)
     assert launches == 2
