@@ -151,6 +151,7 @@ class _CausalScan(torch.autograd.Function):
         o, S, z, handover = torch.ops.subq_audio.scan_fwd(q, k, v, lg_t, mask_u8, S0, z0, reverse, want_state)
         ctx.reverse = reverse
         ctx.lg_is_tensor = isinstance(lg, torch.Tensor)
+        ctx.lg_strided = lg_t is not None and lg_t.dim() == 3 and not lg_t.is_contiguous()
         ctx.save_for_backward(q, k, v, lg_t, mask_u8, S0, z0, o, handover)
         if want_state:
             ctx.mark_non_differentiable(S, z)
@@ -167,6 +168,12 @@ class _CausalScan(torch.autograd.Function):
         glg = None
         if need_lg:
             glg = dlg.to(lg.dtype)
+            if ctx.lg_strided:
+                # the gradient in log(gamma)'s own memory order (a [B, H, N] view of a
+                # gate projection's [B, N, H] output): the elementwise backward ops that
+                # follow then see one layout, for which torch's fake (tracing) and real
+                # kernels agree on the output strides
+                glg = torch.empty_like(lg).copy_(glg)
             if lg.dim() == 0:
                 glg = glg.sum()
             elif lg.dim() == 1:

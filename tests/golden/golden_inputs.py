@@ -93,3 +93,87 @@ def autograd_inputs(spec):
 def stream_inputs():
     g = _rng("stream")
     return [g.standard_normal((1, 2, 4 * STREAM_SPLIT, 16)) for _ in range(3)]
+
+
+# ---------------------------------------------------------------------------
+# Block cases: one pre-LayerNorm transformer block of the reference's audio
+# model (python/subq_audio/model.py:97-135: LayerNorm -> SubQLinearAttention
+# -> residual -> LayerNorm -> Linear/GELU/Linear -> residual) at d_model 768,
+# 12 heads of 64, data-dependent decay gating, MSE loss to seeded targets.
+# ---------------------------------------------------------------------------
+BLOCK_CASES = {
+    "block_causal": dict(B=2, T=512, d=768, H=12, Hkv=12, ffn=3072, causal=True, mask=False),
+    "block_bidir_gqa_mask": dict(B=2, T=384, d=768, H=12, Hkv=4, ffn=3072, causal=False, mask=True),
+}
+BLOCK_ROW_STEP = 64  # output / input-gradient rows kept in the fixture (float32): every 64th position
+BLOCK_HEAD = 256     # leading elements of each flattened parameter gradient kept
+
+
+def make_block(attn_cls, spec):
+    """The block with ``attn_cls`` (the reference's SubQLinearAttention or this
+    package's) as its attention; parameter names are the same for both."""
+    import torch.nn as nn
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            d = spec["d"]
+            self.input_layernorm = nn.LayerNorm(d, eps=1e-5)
+            self.self_attn = attn_cls(d, num_heads=spec["H"], num_key_value_heads=spec["Hkv"],
+                                      is_causal=spec["causal"])
+            self.post_attention_layernorm = nn.LayerNorm(d, eps=1e-5)
+            self.fc1 = nn.Linear(d, spec["ffn"])
+            self.fc2 = nn.Linear(spec["ffn"], d)
+            self.act = nn.GELU()
+
+        def forward(self, x, attention_mask=None):
+            h = x + self.self_attn(self.input_layernorm(x), attention_mask=attention_mask)[0]
+            return h + self.fc2(self.act(self.fc1(self.post_attention_layernorm(h))))
+
+    return Block()
+
+
+def block_params(name, block):
+    """Seeded values for every parameter of ``block`` (float64 numpy, by name):
+    Linear weights N(0, 1/fan_in), biases N(0, 0.02^2), norm weights 1 + N(0,
+    0.1^2), norm biases N(0, 0.1^2), raw decay logit(0.99) + N(0, 0.5^2)."""
+    g = _rng("params/" + name)
+    out = {}
+    for pname, p in sorted(block.named_parameters()):
+        shape = tuple(p.shape)
+        if pname.endswith("raw_decay"):
+            val = np.log(0.99 / 0.01) + 0.5 * g.standard_normal(shape)
+        elif "norm" in pname and pname.endswith("weight"):
+            val = 1.0 + 0.1 * g.standard_normal(shape)
+        elif "norm" in pname:
+            val = 0.1 * g.standard_normal(shape)
+        elif pname.endswith("weight"):
+            val = g.standard_normal(shape) / np.sqrt(shape[-1])
+        else:
+            val = 0.02 * g.standard_normal(shape)
+        out[pname] = val
+    return out
+
+
+def load_block_params(block, values):
+    import torch
+
+    with torch.no_grad():
+        for pname, p in block.named_parameters():
+            p.copy_(torch.from_numpy(values[pname]).to(p.dtype))
+
+
+def block_inputs(name, spec):
+    """x ~ N(0,1) [B, T, d], targets ~ N(0,1), a key-padding mask (or None),
+    and one unit direction per parameter gradient (for projections)."""
+    g = _rng("inputs/" + name)
+    B, T, d = spec["B"], spec["T"], spec["d"]
+    x = g.standard_normal((B, T, d))
+    y = g.standard_normal((B, T, d))
+    mask = lengths_mask(B, T, g) if spec["mask"] else None
+    return x, y, mask
+
+
+def block_direction(name, pname, shape):
+    r = _rng(f"dir/{name}/{pname}").standard_normal(shape)
+    return r / np.linalg.norm(r)
