@@ -317,26 +317,38 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                     if (kNorm) tc::mma_f16_w(tmem + cDAT, sdesc_sw32(oneA), sdesc_sw32(ca), idPP, 1u);
                 }
                 tc::mma_commit_w(&bars[F_MFULLA]);
-                ok = wait_bar(&bars[F_MDONEP], i & 1, P.status);
-                if (ok) ok = wait_bar(&bars[F_DSB], i & 1, P.status);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-                tc::tc_fence_after();
                 const uint64_t dkm = tc::sdesc_sw128(ka, kTile, 1024), dqm = tc::sdesc_sw128(qa, kTile, 1024);
                 const uint64_t dom = tc::sdesc_sw128(oa, kTile, 1024);
                 const uint64_t dob = tc::sdesc_sw128(oa, 16, 1024), dsat = tc::sdesc_sw128(sa, 16, 1024);
                 const uint64_t dv = tc::sdesc_sw128(va, 16, 1024), dsk = tc::sdesc_sw128(dsa, 16, 1024);
                 const uint64_t dk = tc::sdesc_sw128(ka, 16, 1024), dsm = tc::sdesc_sw128(dsa, kTile, 1024);
+                // The products that need no mask run while P^T and dA^T are masked.
+                // dQ~ = o^ S_c^T + c z_c^T
+                #pragma unroll 1
+                for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cDQ, dob + kk * 2, dsat + kk * 2, idKK64, kk > 0);
+                if (kNorm) tc::mma_f16_w(tmem + cDQ, sdesc_sw32(ca), sdesc_sw32(za), idKK64, 1u);
+                // [dS | dz] += q^^T [o^ | c]  (M = 64: dS from the o^ tile, dz from the c tile), once
+                // the compute warps have copied [dS | dz] of the later tokens (the bf16 operand)
+                ok = __all_sync(0xffffffffu, wait_bar(&bars[F_DSB], i & 1, P.status));
+                if (!ok) break;
+                tc::tc_fence_after();
+                {
+                    const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024);
+                    #pragma unroll 1
+                    for (int kk = 0; kk < 8; ++kk) {
+                        tc::mma_f16_w(tmem + cDS, dqt + kk * 128, dom + kk * 128, idS64, 1u);
+                        if (kNorm) tc::mma_f16_w(tmem + cDS + 64, dqt + kk * 128, sdesc_sw32(ca + kk * 512), idZ16, 1u);
+                    }
+                }
+                ok = __all_sync(0xffffffffu, wait_bar(&bars[F_MDONEP], i & 1, P.status));
+                if (!ok) break;
+                tc::tc_fence_after();
                 // dV = P^T o^ + K^ dS   (A = bf16 P^T from TMEM, 8 columns per 16 tokens)
                 #pragma unroll 1
                 for (int kk = 0; kk < 8; ++kk)
                     tc::mma_f16_ts_w(tmem + cPT + 64, tmem + cPT + kk * 8, dom + kk * 128, idKM64, kk > 0);
                 #pragma unroll 1
                 for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cPT + 64, dk + kk * 2, dsm + kk * 128, idKM64, 1u);
-                // dQ~ = o^ S_c^T + c z_c^T (before dA^T is masked)
-                #pragma unroll 1
-                for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cDQ, dob + kk * 2, dsat + kk * 2, idKK64, kk > 0);
-                if (kNorm) tc::mma_f16_w(tmem + cDQ, sdesc_sw32(ca), sdesc_sw32(za), idKK64, 1u);
                 ok = wait_bar(&bars[F_MDONEA], i & 1, P.status);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
@@ -353,15 +365,6 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                     const uint64_t dda = tc::sdesc_sw128(daa, kTile, 1024);
                     #pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk) tc::mma_f16_w(tmem + cDQ, dda + kk * 128, dkm + kk * 128, idMM64, 1u);
-                }
-                // [dS | dz] += q^^T [o^ | c]  (M = 64: dS from the o^ tile, dz from the c tile)
-                {
-                    const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024);
-                    #pragma unroll 1
-                    for (int kk = 0; kk < 8; ++kk) {
-                        tc::mma_f16_w(tmem + cDS, dqt + kk * 128, dom + kk * 128, idS64, 1u);
-                        if (kNorm) tc::mma_f16_w(tmem + cDS + 64, dqt + kk * 128, sdesc_sw32(ca + kk * 512), idZ16, 1u);
-                    }
                 }
                 tc::mma_commit_w(&bars[F_DSFULL]);
             }
@@ -429,11 +432,11 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             put_ds(v, z);
         };
         // the forward's output (this thread's half row) and normaliser of chunk i
+        // (issued together with the mask's load: the mask is applied afterwards)
         auto fetch_o = [&](const Where& w, uint4* ov, float& zc) {
             const int t = w.mc * kC + row;
-            const float m = row_mask_of(p, w, row);
             zc = 1.f;
-            if (kNorm && m != 0.f) {
+            if (kNorm && t < p.N) {
                 const uint4* src = reinterpret_cast<const uint4*>(
                     reinterpret_cast<const typename E::T*>(p.fo) + (int64_t)w.b * p.fo_sb + (int64_t)w.h * p.fo_sh +
                     (int64_t)t * p.fo_sn + hf * 32);
@@ -451,8 +454,8 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             uint4 ov[4];
             float zc;
             fetch_o(w, ov, zc);  // (in flight during the wait)
-            if (!cwait(&bars[F_FULL + s], (i / kStages) & 1)) return false;
             const float m = row_mask_of(p, w, row);
+            if (!cwait(&bars[F_FULL + s], (i / kStages) & 1)) return false;
             uint8_t* gt = slot_ptr(i, L1::g);
             float go[32];
             load_chunks<kFp16>(gt, row, hf * 4, 4, go);
@@ -472,7 +475,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 tc::bar_sync(kBarCompute, kComputeThreads);
                 const float full = dxs[(i & 1) * 256 + row] + dxs[(i & 1) * 256 + 128 + row];
                 if (hf == 0) mtile_row<kFp16>(slot_ptr(i, L1::ct), row, m != 0.f ? -full / zc : 0.f);
-                inv = m / zc;
+                inv = m != 0.f ? m / zc : 0.f;
             } else {
                 tc::bar_sync(kBarCompute, kComputeThreads);  // every half row of dO is read
             }
@@ -536,6 +539,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
         for (int i = 0; i < n && ok; ++i) {
             const Where w = where_of(p, pl, cu, kRev);
             const int s = i % kStages;
+            const float m_row = row_mask_of(p, w, row);  // (for the epilogue; loaded early)
             Cursor cn = cu;
             cn.next(pl);  // the next chunk
             // (1) mask dA^T (also into shared memory for dQ~); the feature-map warps mask P^T
@@ -545,11 +549,19 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             publish(&bars[F_MDONEA]);
             // (2) o^, c of the next chunk (the tensor core runs this chunk's products)
             if (i + 1 < n && !make_oc(i + 1, where_of(p, pl, cn, kRev))) break;
-            // (3) epilogue, once the chunk's MMAs are done
+            // (3) once the chunk's MMAs are done: [dS | dz] after this chunk, the next
+            // chunk's operand (or the next piece's suffix), first, so that the next
+            // chunk's [dS | dz] products can run while its masks are made
             if (!cwait(&bars[F_DSFULL], i & 1)) break;
+            if (i + 1 < n) {
+                if (cn.first()) install(cn);
+                else refresh();
+            }
+            publish(&bars[F_DSB]);
+            tc::tc_fence_after();
+            // (4) epilogue; the producer stores the gradients
             {
-                const float m = row_mask_of(p, w, row);
-                const float sm_ = p.scale * m;
+                const float sm_ = p.scale * m_row;
                 uint32_t rv[32], rk[32], rq[32];
                 tc::tmem_ld32_issue(tmem + cPT + 64 + loff + hf * 32, rv);
                 tc::tmem_ld32_issue(tmem + cDAT + 64 + loff + hf * 32, rk);
@@ -580,13 +592,6 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 }
                 publish(&bars[F_OUT + s]);  // the producer stores them and reloads the stage
             }
-            // (4) [dS | dz] after this chunk: the next chunk's operand (or the next
-            // piece's suffix); then the stores
-            if (i + 1 < n) {
-                if (cn.first()) install(cn);
-                else refresh();
-            }
-            publish(&bars[F_DSB]);
             cu = cn;
         }
     }
@@ -604,9 +609,10 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
 //    each sequence's last live token), with TMA stores of a zero tile.
 constexpr int kAdjStages = 3;
 struct LA {
-    // stage: q^, o^ (over dO), the forward's output o, the c tile
-    static constexpr uint32_t q = 0, g = kTile, o = 2 * kTile, ct = 3 * kTile;
-    static constexpr uint32_t stage = 3 * kTile + kMTile;
+    // stage: q^, o^ (over dO), the forward's output o, and the c atom (column 0
+    // = c_t), the last 16 columns of the N = 80 operand [o^ | c]
+    static constexpr uint32_t q = 0, g = kTile, o = 2 * kTile, cat = 3 * kTile;
+    static constexpr uint32_t stage = 4 * kTile;
     static constexpr uint32_t zt = kAdjStages * stage;  // zero tile
     static constexpr uint32_t dx = zt + kTile;          // [2][256] partial dot products
     static constexpr uint32_t bars = dx + 2048;
@@ -653,7 +659,7 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
 
     // dead chunks: D = B H nC - T in all, this CTA's even share; dead chunks
     // before sequence s number s nC - off[s]; those of s are its memory chunks [nL_s, nC)
-    if (tid == 0) {
+    auto zero_dead = [&]() {
         const int BH = p.B * p.H, nC = P.nC;
         const int64_t D = (int64_t)BH * nC - pl.T;
         const int64_t d0 = D * r_cta / gridDim.x, d1 = D * (r_cta + 1) / gridDim.x;
@@ -675,10 +681,10 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
             }
             tc::bulk_commit();
         }
-    }
+    };
 
-    constexpr uint32_t idS64 = tc::idesc_f16<kFp16>(64, 64, true, true);
-    constexpr uint32_t idZ16 = tc::idesc_f16<kFp16>(64, 16, true, true);
+    // [dS | dz] += q^^T [o^ | c]: M = 64, N = 80 (o^ atom, then the c atom LBO bytes on)
+    constexpr uint32_t idSX = tc::idesc_f16<kFp16>(64, kNorm ? kNX : 64, true, true);
     bool ok = true;
     if (warp == kWarpProducer) {
         if (lane == 0) {
@@ -692,6 +698,8 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
                 if (kNorm) tc::tma_load_4d(base + LA::o, &P.tm_fo, 0, mem_chunk(i) * kC, h, b, &bars[A_FULL + s]);
                 tc::tma_load_4d(base + LA::q, &P.tm_q, 0, mem_chunk(i) * kC, h, b, &bars[A_FULL + s]);
             }
+            zero_dead();
+            tc::bulk_wait0();  // the zero stores are done with the tile
         }
         __syncwarp();
     } else if (warp >= 8 && warp < 12) {
@@ -714,21 +722,18 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
                 if (!ok) break;
                 tc::tc_fence_after();
                 const uint32_t qa = sbase + s * LA::stage + LA::q, oa = sbase + s * LA::stage + LA::g;
-                const uint32_t ca = sbase + s * LA::stage + LA::ct;
-                const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024), dbo = tc::sdesc_sw128(oa, kTile, 1024);
+                const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024);
+                const uint64_t dbo = tc::sdesc_sw128(oa, LA::cat - LA::g, 1024);
                 #pragma unroll 1
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                    tc::mma_f16_w(tmem, dqt + kk * 128, dbo + kk * 128, idS64, acc);
-                    if (kNorm) tc::mma_f16_w(tmem + 64, dqt + kk * 128, sdesc_sw32(ca + kk * 512), idZ16, acc);
-                }
+                for (int kk = 0; kk < 8; ++kk)
+                    tc::mma_f16_w(tmem, dqt + kk * 128, dbo + kk * 128, idSX, (i > 0 || kk > 0) ? 1u : 0u);
                 tc::mma_commit_w(&bars[A_EMPTY + s]);
             }
             if (n > 0 && ok) tc::mma_commit_w(&bars[A_DONE]);
         }
         __syncwarp();
     } else if (warp < 8) {
-        // o^ = m dO / Zc (over the dO tile) and c = -(dO . o) / Zc (the c tile):
+        // o^ = m dO / Zc (over the dO tile) and c = -(dO . o) / Zc (column 0 of the c atom):
         // two threads per row (row = 32 (warp % 4) + lane, column half = warp / 4)
         using E = Elem<kFp16>;
         const int quad = warp & 3, hf = warp >> 2;
@@ -736,11 +741,12 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
         const uint32_t loff = (uint32_t)(quad * 32) << 16;
         float* dxs = reinterpret_cast<float*>(sm + LA::dx);
         // mask and normaliser of a row of chunk i (the normaliser one chunk ahead)
+        // (both loads issue at once: the normaliser's does not wait for the mask's)
         auto row_info = [&](int i, float& m, float& zc) {
             const int t = mem_chunk(i) * kC + row;
             const bool in = t < p.N;
             m = in ? (p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f) : 0.f;
-            zc = (kNorm && m != 0.f) ? __ldg(P.zc + (int64_t)sq * p.N + t) : 1.f;
+            zc = (kNorm && in) ? __ldg(P.zc + (int64_t)sq * p.N + t) : 1.f;
         };
         float m_next = 0.f, zc_next = 1.f;
         if (n > 0) row_info(0, m_next, zc_next);
@@ -763,8 +769,8 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
                 dxs[(i & 1) * 256 + hf * 128 + row] = dot;
                 tc::bar_sync(kBarCompute, kComputeThreads);
                 const float full = dxs[(i & 1) * 256 + row] + dxs[(i & 1) * 256 + 128 + row];
-                if (hf == 0) mtile_row<kFp16>(sm + s * LA::stage + LA::ct, row, m != 0.f ? -full / zc : 0.f);
-                inv = m / zc;
+                if (hf == 0) atom_col0<kFp16>(sm + s * LA::stage + LA::cat, row, m != 0.f ? -full / zc : 0.f);
+                inv = m != 0.f ? m / zc : 0.f;
             } else {
                 tc::bar_sync(kBarCompute, kComputeThreads);  // every half row of dO is read
             }
@@ -794,7 +800,6 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
             }
         }
     }
-    if (tid == 0) tc::bulk_wait0();  // the zero stores are done with the tile
     tc::tc_fence_before();
     __syncthreads();
     if (warp == kWarpMma && need) tc::tmem_dealloc(tmem, 128);

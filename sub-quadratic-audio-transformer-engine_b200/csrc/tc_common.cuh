@@ -418,6 +418,19 @@ __device__ __forceinline__ void mtile_row2(uint8_t* tile, int r, float x0, float
     *reinterpret_cast<uint4*>(tile + r * 32 + ((sw ^ 1) << 4)) = make_uint4(0, 0, 0, 0);
 }
 
+// Row r of a 128 x 64 tile (128-byte swizzle) with x in column 0 and zeros in
+// columns 1-15: the extra 16 columns of an N = 80 MN-major operand whose first
+// 64 columns are another atom (columns 16-63 are never read).
+template <bool kFp16>
+__device__ __forceinline__ void atom_col0(uint8_t* tile, int r, float x) {
+    using E = Elem<kFp16>;
+    uint4 c0 = make_uint4(0, 0, 0, 0);
+    typename E::T2* h = reinterpret_cast<typename E::T2*>(&c0);
+    h[0] = E::from2(x, 0.f);
+    *reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, 0)) = c0;
+    *reinterpret_cast<uint4*>(tile + tc::sw128_chunk(r, 1)) = make_uint4(0, 0, 0, 0);
+}
+
 // 32-byte-swizzled MN-major operand (N = 16): SBO = 256 B between 8-row groups.
 __device__ __forceinline__ uint64_t sdesc_sw32(uint32_t saddr) {
     uint64_t d = 0;
