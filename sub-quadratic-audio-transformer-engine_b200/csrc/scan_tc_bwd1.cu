@@ -309,11 +309,9 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 {
                     const uint64_t dk = tc::sdesc_sw128(ka, 16, 1024), dq = tc::sdesc_sw128(qa, 16, 1024);
                     const uint64_t dv = tc::sdesc_sw128(va, 16, 1024), dob = tc::sdesc_sw128(oa, 16, 1024);
-                    #pragma unroll 1
-                    for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cPT, dk + kk * 2, dq + kk * 2, idPP, kk > 0);
+                    tc::mma_f16_x4(tmem + cPT, dk, 2, dq, 2, idPP, 0u);
                     tc::mma_commit_w(&bars[F_MFULL]);
-                    #pragma unroll 1
-                    for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cDAT, dv + kk * 2, dob + kk * 2, idPP, kk > 0);
+                    tc::mma_f16_x4(tmem + cDAT, dv, 2, dob, 2, idPP, 0u);
                     if (kNorm) tc::mma_f16_w(tmem + cDAT, sdesc_sw32(oneA), sdesc_sw32(ca), idPP, 1u);
                 }
                 tc::mma_commit_w(&bars[F_MFULLA]);
@@ -324,8 +322,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 const uint64_t dk = tc::sdesc_sw128(ka, 16, 1024), dsm = tc::sdesc_sw128(dsa, kTile, 1024);
                 // The products that need no mask run while P^T and dA^T are masked.
                 // dQ~ = o^ S_c^T + c z_c^T
-                #pragma unroll 1
-                for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cDQ, dob + kk * 2, dsat + kk * 2, idKK64, kk > 0);
+                tc::mma_f16_x4(tmem + cDQ, dob, 2, dsat, 2, idKK64, 0u);
                 if (kNorm) tc::mma_f16_w(tmem + cDQ, sdesc_sw32(ca), sdesc_sw32(za), idKK64, 1u);
                 // [dS | dz] += q^^T [o^ | c]  (M = 64: dS from the o^ tile, dz from the c tile), once
                 // the compute warps have copied [dS | dz] of the later tokens (the bf16 operand)
@@ -334,37 +331,28 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 tc::tc_fence_after();
                 {
                     const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024);
-                    #pragma unroll 1
-                    for (int kk = 0; kk < 8; ++kk) {
-                        tc::mma_f16_w(tmem + cDS, dqt + kk * 128, dom + kk * 128, idS64, 1u);
-                        if (kNorm) tc::mma_f16_w(tmem + cDS + 64, dqt + kk * 128, sdesc_sw32(ca + kk * 512), idZ16, 1u);
-                    }
+                    tc::mma_f16_x8(tmem + cDS, dqt, 128, dom, 128, idS64, 1u);
+                    // (the c tile's 16-token steps are 512 bytes: 32 in the descriptor)
+                    if (kNorm) tc::mma_f16_x8(tmem + cDS + 64, dqt, 128, sdesc_sw32(ca), 32, idZ16, 1u);
                 }
                 ok = __all_sync(0xffffffffu, wait_bar(&bars[F_MDONEP], i & 1, P.status));
                 if (!ok) break;
                 tc::tc_fence_after();
                 // dV = P^T o^ + K^ dS   (A = bf16 P^T from TMEM, 8 columns per 16 tokens)
-                #pragma unroll 1
-                for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts_w(tmem + cPT + 64, tmem + cPT + kk * 8, dom + kk * 128, idKM64, kk > 0);
-                #pragma unroll 1
-                for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cPT + 64, dk + kk * 2, dsm + kk * 128, idKM64, 1u);
+                tc::mma_f16_ts_x8(tmem + cPT + 64, tmem + cPT, 8, dom, 128, idKM64, 0u);
+                tc::mma_f16_x4(tmem + cPT + 64, dk, 2, dsm, 128, idKM64, 1u);
                 ok = wait_bar(&bars[F_MDONEA], i & 1, P.status);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc::tc_fence_after();
                 // dK~ = dA^T q^ + V dS^T + 1 dz^T
-                #pragma unroll 1
-                for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts_w(tmem + cDAT + 64, tmem + cDAT + kk * 8, dqm + kk * 128, idKM64, kk > 0);
-                #pragma unroll 1
-                for (int kk = 0; kk < 4; ++kk) tc::mma_f16_w(tmem + cDAT + 64, dv + kk * 2, dsk + kk * 2, idKK64, 1u);
+                tc::mma_f16_ts_x8(tmem + cDAT + 64, tmem + cDAT, 8, dqm, 128, idKM64, 0u);
+                tc::mma_f16_x4(tmem + cDAT + 64, dv, 2, dsk, 2, idKK64, 1u);
                 if (kNorm) tc::mma_f16_w(tmem + cDAT + 64, sdesc_sw32(oneA), sdesc_sw32(dza), idKK64, 1u);
                 // dQ~ += dA K^  (A = masked dA^T in shared memory, read as dA: MN-major over queries)
                 {
                     const uint64_t dda = tc::sdesc_sw128(daa, kTile, 1024);
-                    #pragma unroll 1
-                    for (int kk = 0; kk < 8; ++kk) tc::mma_f16_w(tmem + cDQ, dda + kk * 128, dkm + kk * 128, idMM64, 1u);
+                    tc::mma_f16_x8(tmem + cDQ, dda, 128, dkm, 128, idMM64, 1u);
                 }
                 tc::mma_commit_w(&bars[F_DSFULL]);
             }
@@ -405,14 +393,32 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             const int sq = cu.s;
             const int o1 = __ldg(pl.off + sq + 1);
             if (cu.w1 < (int64_t)o1 && lane < 16) {
-                for (int r2 = r_cta + 1; r2 < pl.R; ++r2) {
-                    const int64_t a2 = pl.w0(r2);
-                    if (a2 >= o1) break;
-                    if (pl.w0(r2 + 1) == a2) continue;  // an empty range
-                    const float* src = P.agg + ((size_t)r2 * kD + srow) * (kD + 1);
+                // the later CTAs whose ranges start inside sequence sq, two at a time:
+                // both rows' loads are issued before their sums (one load latency for two)
+                int r2 = r_cta + 1;
+                int64_t a2 = pl.w0(r2);
+                while (r2 < pl.R && a2 < o1) {
+                    int rr[2] = {-1, -1};
+                    for (int k = 0; k < 2 && r2 < pl.R && a2 < o1;) {
+                        const int64_t a3 = pl.w0(r2 + 1);
+                        if (a3 > a2) rr[k++] = r2;  // (an empty range has no first piece)
+                        ++r2;
+                        a2 = a3;
+                    }
+                    const float* s0 = P.agg + ((size_t)max(rr[0], 0) * kD + srow) * (kD + 1);
+                    const float* s1 = P.agg + ((size_t)max(rr[1], 0) * kD + srow) * (kD + 1);
+                    const bool h0 = rr[0] >= 0, h1 = rr[1] >= 0;
+                    float x0[33], x1[33];
 #pragma unroll
-                    for (int x = 0; x < 32; ++x) v[x] += src[hf * 32 + x];
-                    if (kNorm) z += src[kD];
+                    for (int x = 0; x < 32; ++x) {
+                        x0[x] = h0 ? __ldg(s0 + hf * 32 + x) : 0.f;
+                        x1[x] = h1 ? __ldg(s1 + hf * 32 + x) : 0.f;
+                    }
+                    x0[32] = (kNorm && h0) ? __ldg(s0 + kD) : 0.f;
+                    x1[32] = (kNorm && h1) ? __ldg(s1 + kD) : 0.f;
+#pragma unroll
+                    for (int x = 0; x < 32; ++x) v[x] += x0[x] + x1[x];
+                    z += x0[32] + x1[32];
                 }
             }
             tc::tmem_st32(tmem + cDS + loff + hf * 32, v);
@@ -724,9 +730,7 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
                 const uint32_t qa = sbase + s * LA::stage + LA::q, oa = sbase + s * LA::stage + LA::g;
                 const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024);
                 const uint64_t dbo = tc::sdesc_sw128(oa, LA::cat - LA::g, 1024);
-                #pragma unroll 1
-                for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_w(tmem, dqt + kk * 128, dbo + kk * 128, idSX, (i > 0 || kk > 0) ? 1u : 0u);
+                tc::mma_f16_x8(tmem, dqt, 128, dbo, 128, idSX, i > 0 ? 1u : 0u);
                 tc::mma_commit_w(&bars[A_EMPTY + s]);
             }
             if (n > 0 && ok) tc::mma_commit_w(&bars[A_DONE]);

@@ -206,8 +206,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         const uint32_t lbo = L::ones - (s * L::stage + L::v);  // V atom -> ones atom
         const uint32_t n80 = kNorm ? idSX : tc::idesc_f16<kFp16>(64, 64, true, true);
         const uint64_t da = tc::sdesc_sw128(ka, kTile, 1024), db = tc::sdesc_sw128(va, lbo, 1024);
-        for (int kk = 0; kk < 8; ++kk)  // a K-step of 16 tokens is 2048 bytes on (a descriptor step of 128)
-            tc::mma_f16_w(tmem + col, da + kk * 128, db + kk * 128, n80, (first && kk == 0) ? 0u : 1u);
+        // 8 K-steps of 16 tokens, each 2048 bytes on (a descriptor step of 128)
+        tc::mma_f16_x8(tmem + col, da, 128, db, 128, n80, first ? 0u : 1u);
     };
 
     // Chunk of pipeline slot j: phase-1 slots (j < n1) visit the share in an
@@ -518,8 +518,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 tc::tc_fence_after();
                 const uint64_t dq = tc::sdesc_sw128(sbase + s * L::stage + L::q, 16, 1024);
                 const uint64_t dk = tc::sdesc_sw128(sbase + s * L::stage + L::k, 16, 1024);
-                for (int kk = 0; kk < 4; ++kk)  // 16 features are 32 bytes on (a descriptor step of 2)
-                    tc::mma_f16_w(tmem + cP + bf * 128, dq + kk * 2, dk + kk * 2, idP, kk > 0);
+                // 4 K-steps of 16 features, each 32 bytes on (a descriptor step of 2)
+                tc::mma_f16_x4(tmem + cP + bf * 128, dq, 2, dk, 2, idP, 0u);
                 tc::mma_commit_w(&bars[B_PFULL + bf]);
                 return true;
             };
@@ -543,14 +543,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 const uint32_t tOb = tmem + cO + bf * kNX;
                 const uint64_t dq = tc::sdesc_sw128(sbase + s * L::stage + L::q, 16, 1024);
                 const uint64_t dsb = tc::sdesc_sw128(sbase + L::sb + (i & 1) * L::sbuf, kD * kD * 2, 1024);
-                for (int kk = 0; kk < 4; ++kk)  // [O | Zi] = phi~(Q) [S_c | z_c]
-                    tc::mma_f16_w(tOb, dq + kk * 2, dsb + kk * 128, kNorm ? idOX : idO, kk > 0);
+                tc::mma_f16_x4(tOb, dq, 2, dsb, 128, kNorm ? idOX : idO, 0u);  // [O | Zi] = phi~(Q) [S_c | z_c]
                 // [O | Zi] += P [V | 1]: bf16 P read from TMEM (8 columns per 16 tokens);
                 // the ones column adds the causal row sums to the normaliser
                 const uint32_t lbo = kNorm ? L::ones - (s * L::stage + L::v) : kTile;
                 const uint64_t dv = tc::sdesc_sw128(sbase + s * L::stage + L::v, lbo, 1024);
-                for (int kk = 0; kk < 8; ++kk)
-                    tc::mma_f16_ts_w(tOb, tmem + cP + bf * 128 + kk * 8, dv + kk * 128, kNorm ? idOX : idO, 1u);
+                tc::mma_f16_ts_x8(tOb, tmem + cP + bf * 128, 8, dv, 128, kNorm ? idOX : idO, 1u);
                 tc::mma_commit_w(&bars[B_OFULL + bf]);
                 tc::mma_commit_w(&bars[B_EMPTY + s]);
             }

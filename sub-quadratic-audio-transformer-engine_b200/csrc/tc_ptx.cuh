@@ -176,6 +176,28 @@ __device__ __forceinline__ void mma_commit_w(uint64_t* bar) {
         : "memory");
 }
 
+// Groups of K-steps, one warp-converged MMA each: step j uses the descriptors
+// a + j * as and b + j * bs (TMEM column ta + j * ts for an A in TMEM); the
+// first step accumulates when `acc` is nonzero, the others always. (Issuing a
+// group from one asm block with a single elect is faster in isolation, about
+// 35-50 instead of 100 cycles per MMA, but made both scans slower: the forward
+// 0.109 vs 0.107 ms, the one-pass backward 0.198 vs 0.187 ms at B=8 H=8
+// N=8192; the rolled loops are kept.)
+__device__ __forceinline__ void mma_f16_x4(uint32_t d, uint64_t a, uint64_t as, uint64_t b, uint64_t bs, uint32_t id,
+                                           uint32_t acc) {
+    for (int k = 0; k < 4; ++k) mma_f16_w(d, a + k * as, b + k * bs, id, k > 0 ? 1u : acc);
+}
+__device__ __forceinline__ void mma_f16_x8(uint32_t d, uint64_t a, uint64_t as, uint64_t b, uint64_t bs, uint32_t id,
+                                           uint32_t acc) {
+#pragma unroll 1
+    for (int k = 0; k < 8; ++k) mma_f16_w(d, a + k * as, b + k * bs, id, k > 0 ? 1u : acc);
+}
+__device__ __forceinline__ void mma_f16_ts_x8(uint32_t d, uint32_t ta, uint32_t ts, uint64_t b, uint64_t bs,
+                                              uint32_t id, uint32_t acc) {
+#pragma unroll 1
+    for (int k = 0; k < 8; ++k) mma_f16_ts_w(d, ta + k * ts, b + k * bs, id, k > 0 ? 1u : acc);
+}
+
 // Arrives on `bar` once every MMA issued so far by this thread has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
