@@ -56,8 +56,9 @@ struct L1 {
     static constexpr uint32_t dsb = da + 2 * kTile;   // bf16 dS of the later tokens (64 x 64)
     static constexpr uint32_t dzt = dsb + kSAtom;     // dz tile: row f, column 0 = dz[f]
     static constexpr uint32_t ones = dzt + 2048;      // ones tile: column 0 = 1 (128 x 16)
-    static constexpr uint32_t dx = ones + kMTile;     // [2][128] partial dot products
-    static constexpr uint32_t bars = dx + 1024;
+    static constexpr uint32_t dx = ones + kMTile;     // [2][2][128] fp32 partial dot products (chunk parity, half)
+    static constexpr uint32_t inst = dx + 2048;       // [64][65] fp32: the later CTAs' sums for the last piece
+    static constexpr uint32_t bars = inst + kD * (kD + 1) * 4;
     static constexpr uint32_t tslot = bars + 8 * 16;
     static constexpr uint32_t total = tslot + 16;
 };
@@ -78,7 +79,8 @@ enum {
     F_EPI = 12,          // compute -> MMA: dV, dK, dQ~ read
     F_DSB = 13,          // compute -> MMA: bf16 dS and the dz tile of the later tokens in place
     F_MFULLA = 14,       // MMA -> compute: dA^T
-    F_COUNT = 15
+    F_INST = 15,         // feature map -> compute: the last piece's suffix sums in shared memory
+    F_COUNT = 16
 };
 
 // TMEM: P^T [0,128) (bf16 in [0,64), then dV in [64,128)), dA^T [128,256)
@@ -275,6 +277,39 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             }
             tc::tmem_wait_st();
         };
+        // While the first chunk loads: when this CTA's last piece continues in later
+        // CTAs, the sum of their first pieces' q^^T [o^ | c] (adj_kernel) is that
+        // piece's suffix; it goes to shared memory, in the [64][65] layout of agg.
+        {
+            float* inst = reinterpret_cast<float*>(sm + L1::inst);
+            const int sqL = n > 0 ? pl.seq_at(cur0.w1 - 1) : 0;
+            const int o1 = n > 0 ? __ldg(pl.off + sqL + 1) : 0;
+            if (n > 0 && cur0.w1 < (int64_t)o1) {
+                float acc[33];
+#pragma unroll
+                for (int x = 0; x < 33; ++x) acc[x] = 0.f;
+                int64_t a2 = pl.w0(r_cta + 1);
+                for (int r2 = r_cta + 1; r2 < pl.R && a2 < o1; ++r2) {
+                    const int64_t a3 = pl.w0(r2 + 1);
+                    if (a3 > a2) {  // (an empty range has no first piece)
+                        const float* src = P.agg + (size_t)r2 * kD * (kD + 1);
+#pragma unroll
+                        for (int x = 0; x < 33; ++x) {
+                            const int idx = r + x * kTransformThreads;
+                            if (idx < kD * (kD + 1)) acc[x] += __ldg(src + idx);
+                        }
+                    }
+                    a2 = a3;
+                }
+#pragma unroll
+                for (int x = 0; x < 33; ++x) {
+                    const int idx = r + x * kTransformThreads;
+                    if (idx < kD * (kD + 1)) inst[idx] = acc[x];
+                }
+            }
+            tc::bar_sync(kBarTransform, kTransformThreads);
+            if (r == 0) tc::mbar_arrive(&bars[F_INST]);
+        }
         Cursor cu = cur0;
         if (n > 0) transform(0, cu);
         for (int i = 0; i < n && ok; ++i) {
@@ -390,35 +425,14 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             float v[32], z = 0.f;
 #pragma unroll
             for (int x = 0; x < 32; ++x) v[x] = 0.f;
-            const int sq = cu.s;
-            const int o1 = __ldg(pl.off + sq + 1);
-            if (cu.w1 < (int64_t)o1 && lane < 16) {
-                // the later CTAs whose ranges start inside sequence sq, two at a time:
-                // both rows' loads are issued before their sums (one load latency for two)
-                int r2 = r_cta + 1;
-                int64_t a2 = pl.w0(r2);
-                while (r2 < pl.R && a2 < o1) {
-                    int rr[2] = {-1, -1};
-                    for (int k = 0; k < 2 && r2 < pl.R && a2 < o1;) {
-                        const int64_t a3 = pl.w0(r2 + 1);
-                        if (a3 > a2) rr[k++] = r2;  // (an empty range has no first piece)
-                        ++r2;
-                        a2 = a3;
-                    }
-                    const float* s0 = P.agg + ((size_t)max(rr[0], 0) * kD + srow) * (kD + 1);
-                    const float* s1 = P.agg + ((size_t)max(rr[1], 0) * kD + srow) * (kD + 1);
-                    const bool h0 = rr[0] >= 0, h1 = rr[1] >= 0;
-                    float x0[33], x1[33];
+            const int o1 = __ldg(pl.off + cu.s + 1);
+            if (cu.w1 < (int64_t)o1) {  // the last piece, continued by later CTAs
+                if (!cwait(&bars[F_INST], 0)) return;
+                if (lane < 16) {
+                    const float* src = reinterpret_cast<const float*>(sm + L1::inst) + srow * (kD + 1);
 #pragma unroll
-                    for (int x = 0; x < 32; ++x) {
-                        x0[x] = h0 ? __ldg(s0 + hf * 32 + x) : 0.f;
-                        x1[x] = h1 ? __ldg(s1 + hf * 32 + x) : 0.f;
-                    }
-                    x0[32] = (kNorm && h0) ? __ldg(s0 + kD) : 0.f;
-                    x1[32] = (kNorm && h1) ? __ldg(s1 + kD) : 0.f;
-#pragma unroll
-                    for (int x = 0; x < 32; ++x) v[x] += x0[x] + x1[x];
-                    z += x0[32] + x1[32];
+                    for (int x = 0; x < 32; ++x) v[x] = src[hf * 32 + x];
+                    if (kNorm) z = src[kD];
                 }
             }
             tc::tmem_st32(tmem + cDS + loff + hf * 32, v);
