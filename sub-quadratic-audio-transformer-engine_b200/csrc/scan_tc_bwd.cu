@@ -238,17 +238,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
     };
     auto transform = [&](int jlo, int jhi) {
         const int r = tid - 256;
-        float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
-        float a_next = (kDecay && jlo < jhi) ? decay_log2_at(p, b, h, act(chunk_of(jlo)) * kC + r, m_next) : 0.f;
+        // (mask byte and log(gamma) loaded a chunk ahead, raw: they are tested and
+        // scaled after the wait, so the loads overlap it)
+        int mr_next = jlo < jhi ? mask_raw_at(p, b, act(chunk_of(jlo)) * kC + r) : 0;
+        float lg_next = (kDecay && jlo < jhi) ? decay_log_raw(p, b, h, act(chunk_of(jlo)) * kC + r) : 0.f;
         for (int j = jlo; j < jhi && ok; ++j) {
             const int s = j % kStages, u = j / kStages;
-            const float m = m_next, a = a_next;
-            if (j + 1 < jhi) {
-                m_next = row_mask_at(chunk_of(j + 1), r);
-                if (kDecay) a_next = decay_log2_at(p, b, h, act(chunk_of(j + 1)) * kC + r, m_next);
+            const int mr = mr_next;
+            const float lg = lg_next;
+            if (j + 1 < jhi) {  // in flight during the wait
+                mr_next = mask_raw_at(p, b, act(chunk_of(j + 1)) * kC + r);
+                if (kDecay) lg_next = decay_log_raw(p, b, h, act(chunk_of(j + 1)) * kC + r);
             }
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
+            const float m = mr != 0 ? 1.f : 0.f;
+            const float a = (kDecay && m != 0.f) ? lg * kLog2e : 0.f;
             uint8_t* base = sm + s * BL::stage;
             if constexpr (kDecay) {
                 float b63, b127;

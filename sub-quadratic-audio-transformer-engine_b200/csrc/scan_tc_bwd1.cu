@@ -126,11 +126,17 @@ __device__ __forceinline__ Where where_of(const ScanParams& p, const Plan& pl, c
     w.mc = rev ? w.nLs - 1 - w.c : w.c;  // the chunk's place in memory
     return w;
 }
-__device__ __forceinline__ float row_mask_of(const ScanParams& p, const Where& w, int r) {
+// The mask byte of row r of a chunk (1 without a mask, 0 past the sequence's
+// end). The load is predicated on the position alone and its value is not
+// tested here, so a thread waits for it only where it is used (mask_f, after the
+// barrier waits), not at the load.
+__device__ __forceinline__ int row_mask_raw(const ScanParams& p, const Where& w, int r) {
     const int t = w.mc * kC + r;
-    if (t >= p.N) return 0.f;
-    return p.mask ? (p.mask[(int64_t)w.b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
+    int v = t < p.N ? 1 : 0;
+    if (p.mask && t < p.N) v = __ldg(p.mask + (int64_t)w.b * p.mask_sb + t);
+    return v;
 }
+__device__ __forceinline__ float mask_f(int raw) { return raw != 0 ? 1.f : 0.f; }
 
 template <bool kFp16, bool kNorm, bool kRev>
 __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constant__ Bwd1Params P) {
@@ -231,12 +237,12 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
         const uint32_t toff = (uint32_t)((warp & 3) * 32) << 16;  // TMEM lanes of this warp
         auto transform = [&](int i, const Cursor& cu) -> bool {
             const int s = i % kStages, u = i / kStages;
-            const float m = row_mask_of(p, where_of(p, pl, cu, kRev), r);
+            const int mr = row_mask_raw(p, where_of(p, pl, cu, kRev), r);
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[F_FULL + s], u & 1, P.status)) && ok;
             if (!ok) return false;
             uint8_t* base = sm + s * L1::stage;
             chunks_phi<kFp16>(base + L1::q, r, 0, 8, true);  // scale is applied in the epilogue
-            chunks_phi<kFp16>(base + L1::k, r, 0, 8, m != 0.f);
+            chunks_phi<kFp16>(base + L1::k, r, 0, 8, mr != 0);
             if (kNorm && r < kD) mtile_row<kFp16>(base + L1::zt, r, reinterpret_cast<const float*>(base + L1::zv)[r]);
             tc::fence_proxy_async();
             tc::bar_sync(kBarTransform, kTransformThreads);
@@ -474,8 +480,9 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             uint4 ov[4];
             float zc;
             fetch_o(w, ov, zc);  // (in flight during the wait)
-            const float m = row_mask_of(p, w, row);
+            const int mr = row_mask_raw(p, w, row);
             if (!cwait(&bars[F_FULL + s], (i / kStages) & 1)) return false;
+            const float m = mask_f(mr);
             uint8_t* gt = slot_ptr(i, L1::g);
             float go[32];
             load_chunks<kFp16>(gt, row, hf * 4, 4, go);
@@ -559,7 +566,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
         for (int i = 0; i < n && ok; ++i) {
             const Where w = where_of(p, pl, cu, kRev);
             const int s = i % kStages;
-            const float m_row = row_mask_of(p, w, row);  // (for the epilogue; loaded early)
+            const int mr_row = row_mask_raw(p, w, row);  // (for the epilogue; loaded early)
             Cursor cn = cu;
             cn.next(pl);  // the next chunk
             // (1) mask dA^T (also into shared memory for dQ~); the feature-map warps mask P^T
@@ -581,7 +588,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             tc::tc_fence_after();
             // (4) epilogue; the producer stores the gradients
             {
-                const float sm_ = p.scale * m_row;
+                const float sm_ = p.scale * mask_f(mr_row);
                 uint32_t rv[32], rk[32], rq[32];
                 tc::tmem_ld32_issue(tmem + cPT + 64 + loff + hf * 32, rv);
                 tc::tmem_ld32_issue(tmem + cDAT + 64 + loff + hf * 32, rk);
@@ -627,12 +634,13 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
 //    CTAs of the sequence start from);
 //  * every CTA zeroes dq, dk, dv of its share of the dead chunks (those after
 //    each sequence's last live token), with TMA stores of a zero tile.
-constexpr int kAdjStages = 3;
+// Four stages of q^, o^ (over dO) and the forward's output o; once a row's
+// o . dO is formed, c_t goes into column 0 of the same row of the o tile, which
+// is then the last 16 columns of the N = 80 operand [o^ | c].
+constexpr int kAdjStages = 4;
 struct LA {
-    // stage: q^, o^ (over dO), the forward's output o, and the c atom (column 0
-    // = c_t), the last 16 columns of the N = 80 operand [o^ | c]
-    static constexpr uint32_t q = 0, g = kTile, o = 2 * kTile, cat = 3 * kTile;
-    static constexpr uint32_t stage = 4 * kTile;
+    static constexpr uint32_t q = 0, g = kTile, o = 2 * kTile;
+    static constexpr uint32_t stage = 3 * kTile;
     static constexpr uint32_t zt = kAdjStages * stage;  // zero tile
     static constexpr uint32_t dx = zt + kTile;          // [2][256] partial dot products
     static constexpr uint32_t bars = dx + 2048;
@@ -641,7 +649,8 @@ struct LA {
 };
 static_assert(LA::stage % 1024 == 0 && LA::zt % 1024 == 0, "alignment");
 static_assert(LA::total + 1024 <= 232448, "shared memory");
-enum { A_FULL = 0, A_TDONE = 4, A_EMPTY = 8, A_DONE = 12, A_COUNT = 13 };
+enum { A_FULL = 0, A_TDONE = kAdjStages, A_EMPTY = 2 * kAdjStages, A_DONE = 3 * kAdjStages, A_COUNT = A_DONE + 1 };
+static_assert(A_COUNT <= 16, "barrier slots");
 
 template <bool kFp16, bool kNorm, bool kRev>
 __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant__ Bwd1Params P, float* agg) {
@@ -703,7 +712,7 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
         }
     };
 
-    // [dS | dz] += q^^T [o^ | c]: M = 64, N = 80 (o^ atom, then the c atom LBO bytes on)
+    // [dS | dz] += q^^T [o^ | c]: M = 64, N = 80 (the o^ tile, then the c columns LBO bytes on)
     constexpr uint32_t idSX = tc::idesc_f16<kFp16>(64, kNorm ? kNX : 64, true, true);
     bool ok = true;
     if (warp == kWarpProducer) {
@@ -743,7 +752,7 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
                 tc::tc_fence_after();
                 const uint32_t qa = sbase + s * LA::stage + LA::q, oa = sbase + s * LA::stage + LA::g;
                 const uint64_t dqt = tc::sdesc_sw128(qa, kTile, 1024);
-                const uint64_t dbo = tc::sdesc_sw128(oa, LA::cat - LA::g, 1024);
+                const uint64_t dbo = tc::sdesc_sw128(oa, LA::o - LA::g, 1024);
                 tc::mma_f16_x8(tmem, dqt, 128, dbo, 128, idSX, i > 0 ? 1u : 0u);
                 tc::mma_commit_w(&bars[A_EMPTY + s]);
             }
@@ -751,29 +760,34 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
         }
         __syncwarp();
     } else if (warp < 8) {
-        // o^ = m dO / Zc (over the dO tile) and c = -(dO . o) / Zc (column 0 of the c atom):
-        // two threads per row (row = 32 (warp % 4) + lane, column half = warp / 4)
+        // o^ = m dO / Zc (over the dO tile) and c = -(dO . o) / Zc (column 0 of the o
+        // tile): two threads per row (row = 32 (warp % 4) + lane, column half = warp / 4)
         using E = Elem<kFp16>;
         const int quad = warp & 3, hf = warp >> 2;
         const int row = quad * 32 + lane, srow = quad * 16 + lane;
         const uint32_t loff = (uint32_t)(quad * 32) << 16;
         float* dxs = reinterpret_cast<float*>(sm + LA::dx);
-        // mask and normaliser of a row of chunk i (the normaliser one chunk ahead)
-        // (both loads issue at once: the normaliser's does not wait for the mask's)
-        auto row_info = [&](int i, float& m, float& zc) {
+        // mask and normaliser of a row of chunk i (loaded a chunk ahead); both loads
+        // issue at once (the normaliser's does not wait for the mask's)
+        // (the mask byte is kept raw until it is used: see row_mask_raw)
+        auto row_info = [&](int i, int& mr, float& zc) {
             const int t = mem_chunk(i) * kC + row;
             const bool in = t < p.N;
-            m = in ? (p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f) : 0.f;
+            mr = in ? 1 : 0;
+            if (p.mask && in) mr = __ldg(p.mask + (int64_t)b * p.mask_sb + t);
             zc = (kNorm && in) ? __ldg(P.zc + (int64_t)sq * p.N + t) : 1.f;
         };
-        float m_next = 0.f, zc_next = 1.f;
-        if (n > 0) row_info(0, m_next, zc_next);
+        int mr_next = 0;
+        float zc_next = 1.f;
+        if (n > 0) row_info(0, mr_next, zc_next);
         for (int i = 0; i < n && ok; ++i) {
             const int s = i % kAdjStages, u = i / kAdjStages;
-            const float m = m_next, zc = zc_next;
-            if (i + 1 < n) row_info(i + 1, m_next, zc_next);
+            const int mr = mr_next;
+            const float zc = zc_next;
+            if (i + 1 < n) row_info(i + 1, mr_next, zc_next);
             ok = tc::bar_and(kBarCompute, kComputeThreads, wait_bar(&bars[A_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
+            const float m = mask_f(mr);
             uint8_t* gt = sm + s * LA::stage + LA::g;
             float go[32];
             load_chunks<kFp16>(gt, row, hf * 4, 4, go);
@@ -785,9 +799,9 @@ __global__ void __launch_bounds__(kThreads1, 1) adj_kernel(const __grid_constant
 #pragma unroll
                 for (int x = 0; x < 32; ++x) dot = fmaf(go[x], ov[x], dot);
                 dxs[(i & 1) * 256 + hf * 128 + row] = dot;
-                tc::bar_sync(kBarCompute, kComputeThreads);
+                tc::bar_sync(kBarCompute, kComputeThreads);  // (every half row of o is read)
                 const float full = dxs[(i & 1) * 256 + row] + dxs[(i & 1) * 256 + 128 + row];
-                if (hf == 0) atom_col0<kFp16>(sm + s * LA::stage + LA::cat, row, m != 0.f ? -full / zc : 0.f);
+                if (hf == 0) atom_col0<kFp16>(sm + s * LA::stage + LA::o, row, m != 0.f ? -full / zc : 0.f);
                 inv = m != 0.f ? m / zc : 0.f;
             } else {
                 tc::bar_sync(kBarCompute, kComputeThreads);  // every half row of dO is read

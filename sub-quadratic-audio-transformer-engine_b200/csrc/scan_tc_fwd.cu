@@ -194,11 +194,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     // chunks from the last one down (act maps to the chunk's place in memory),
     // and each chunk's rows from 127 down (the mask and decay scan follow).
     auto act = [&](int c) { return kRev ? nL - 1 - c : c; };
-    auto row_mask_at = [&](int chunk, int r) -> float {
-        const int t = act(chunk) * kC + r;
-        if (t >= p.N) return 0.f;
-        return p.mask ? (p.mask[(int64_t)b * p.mask_sb + t] ? 1.f : 0.f) : 1.f;
-    };
     // [S|z] (+)= phi~(K)^T [V | 1] over the chunk in stage s (8 K-steps of 16 tokens),
     // into the M = 64 accumulator at TMEM column `col`.
     auto mma_state = [&](int s, bool first, uint32_t col = cS) {
@@ -239,18 +234,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     };
     auto transform = [&](int jlo, int jhi) {
         const int r = tid - 256;
-        float m_next = jlo < jhi ? row_mask_at(chunk_of(jlo), r) : 0.f;
-        float a_next = (kDecay && jlo < jhi) ? decay_log2_at(p, b, h, act(chunk_of(jlo)) * kC + r, m_next) : 0.f;
+        // (mask byte and log(gamma) loaded a chunk ahead, raw: they are tested and
+        // scaled after the wait, so the loads overlap it)
+        int mr_next = jlo < jhi ? mask_raw_at(p, b, act(chunk_of(jlo)) * kC + r) : 0;
+        float lg_next = (kDecay && jlo < jhi) ? decay_log_raw(p, b, h, act(chunk_of(jlo)) * kC + r) : 0.f;
         for (int j = jlo; j < jhi && ok; ++j) {
             const bool ph2 = j >= n1;
             const int s = j % kStages, u = j / kStages;
-            const float m = m_next, a = a_next;
+            const int mr = mr_next;
+            const float lg = lg_next;
             if (j + 1 < jhi) {  // in flight during the wait
-                m_next = row_mask_at(chunk_of(j + 1), r);
-                if (kDecay) a_next = decay_log2_at(p, b, h, act(chunk_of(j + 1)) * kC + r, m_next);
+                mr_next = mask_raw_at(p, b, act(chunk_of(j + 1)) * kC + r);
+                if (kDecay) lg_next = decay_log_raw(p, b, h, act(chunk_of(j + 1)) * kC + r);
             }
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[B_FULL + s], u & 1, P.status)) && ok;
             if (!ok) break;
+            const float m = mr != 0 ? 1.f : 0.f;
+            const float a = (kDecay && m != 0.f) ? lg * kLog2e : 0.f;
             uint8_t* base = sm + s * L::stage;
             if constexpr (kDecay) {
                 float b63, b127;
@@ -635,11 +635,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
         }
         if (n > 0 && ok) ok = mask_p(0);
         // the output rows' mask values, loaded one chunk ahead (off the epilogue's path)
-        float m_next = n > 0 ? row_mask_at(c_begin, row) : 0.f;
+        int mr_next = n > 0 ? mask_raw_at(p, b, act(c_begin) * kC + row) : 0;  // (raw: tested where used)
         for (int i = 0; i < n && ok; ++i) {
             const int c = c_begin + i, bf = i & 1, pu = i >> 1;
-            const float m_row = m_next;
-            if (i + 1 < n) m_next = row_mask_at(c + 1, row);
+            const int mr_row = mr_next;
+            if (i + 1 < n) mr_next = mask_raw_at(p, b, act(c + 1) * kC + row);
             // state refresh: bf16 [S | z]_c+1 into sb[(i + 1) % 2], the next chunk's operand
             ok = tc::bar_and(kBarCompute, kComputeThreads,
                              wait_bar(&bars[B_SFULL], sfull_count & 1, P.status)) && ok;
@@ -719,7 +719,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             if (tid == 0) tc::mbar_arrive(&bars[B_ODONE + bf]);  // every thread has read O'[bf]
             {
                 // O' and its normaliser column carry phi(q) unscaled: o = s O' / max(s Z', clamp)
-                float inv = m_row * p.scale;
+                float inv = (mr_row != 0 ? 1.f : 0.f) * p.scale;
                 if (kNorm) {
                     const float zc = max_nan(p.scale * zi, p.clamp_min);
                     inv = inv / zc;

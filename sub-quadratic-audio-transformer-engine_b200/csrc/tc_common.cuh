@@ -281,6 +281,18 @@ __device__ __forceinline__ float decay_log2_at(const ScanParams& p, int b, int h
     if (t >= p.N || m == 0.f) return 0.f;
     return token_log_gamma(p, b, h, t) * kLog2e;
 }
+// log(gamma_t) as loaded (0 past the sequence's end), for a caller that applies
+// the mask and the log2 factor where it uses the value: nothing tests or scales
+// the loaded value at the load, so no instruction waits for it there.
+__device__ __forceinline__ float decay_log_raw(const ScanParams& p, int b, int h, int t) {
+    return t < p.N ? token_log_gamma(p, b, h, t) : 0.f;
+}
+// The mask byte of token t of sequence b as loaded (1 without a mask, 0 past the end).
+__device__ __forceinline__ int mask_raw_at(const ScanParams& p, int b, int t) {
+    int v = t < p.N ? 1 : 0;
+    if (p.mask && t < p.N) v = __ldg(p.mask + (int64_t)b * p.mask_sb + t);
+    return v;
+}
 
 // Inclusive scan of the chunk's log2 decay over the 128 threads of a 4-warp
 // group (thread r holds token r's value a). Returns B_r; b63 and b127 receive
