@@ -78,6 +78,9 @@ def parse():
                         "over the ranks (one slice each)")
     p.add_argument("--seq-len", type=int, default=16384)
     p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--scan-batch", type=int, default=8,
+                   help="scan workload: sequences per GPU (the headline case is 8; a smaller batch is "
+                        "the small case of the kernel profiles)")
     return p.parse_args()
 
 
@@ -473,7 +476,12 @@ def profile_traffic():
 
 
 def main():
+    global B, METRIC, CONFIG
     args = parse()
+    if args.scan_batch != B:
+        B = args.scan_batch
+        METRIC = METRIC.replace("B=8", f"B={B}")
+        CONFIG = {**CONFIG, "batch_per_gpu": B}
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
@@ -687,7 +695,8 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {**CONFIG, "kernel_path": path_used, "batch_this_gpu": Bl},
             "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "roofline": {"bound": "hbm", "kernel": dom + (" (pre-pass + one-pass launches)" if dom == "bwd" else ""),
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "peak_source": src,
                          "traffic": (tr * 1.0 if tr is not None else None),
                          "algorithmic_bytes": dom_bytes, "launch_ms": dom_ms},
