@@ -241,8 +241,9 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[F_FULL + s], u & 1, P.status)) && ok;
             if (!ok) return false;
             uint8_t* base = sm + s * L1::stage;
-            chunks_phi<kFp16>(base + L1::q, r, 0, 8, true);  // scale is applied in the epilogue
-            chunks_phi<kFp16>(base + L1::k, r, 0, 8, mr != 0);
+            // q^ then m phi(k) (scale is applied in the epilogue); one copy of the code
+#pragma unroll 1
+            for (int tt = 0; tt < 2; ++tt) chunks_phi<kFp16>(base + (tt ? L1::k : L1::q), r, 0, 8, tt ? mr != 0 : true);
             if (kNorm && r < kD) mtile_row<kFp16>(base + L1::zt, r, reinterpret_cast<const float*>(base + L1::zv)[r]);
             tc::fence_proxy_async();
             tc::bar_sync(kBarTransform, kTransformThreads);
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
         // bf16 into the row's first 64 columns. One thread holds the whole row, so
         // it overwrites only columns it has already read.
         auto mask_pt = [&]() {
-#pragma unroll
+#pragma unroll 1
             for (int half = 0; half < 2; ++half) {
                 const bool dead = kRev ? (half == 1 && r < 64) : (half == 0 && r >= 64);
                 const bool diag = half == (r >> 6);
@@ -317,16 +318,19 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             if (r == 0) tc::mbar_arrive(&bars[F_INST]);
         }
         Cursor cu = cur0;
-        if (n > 0) transform(0, cu);
-        for (int i = 0; i < n && ok; ++i) {
-            ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[F_MFULL], i & 1, P.status)) && ok;
-            if (!ok) break;
-            tc::tc_fence_after();
-            mask_pt();
-            tc::tc_fence_before();
-            tc::bar_sync(kBarTransform, kTransformThreads);
-            if (r == 0) tc::mbar_arrive(&bars[F_MDONEP]);
-            cu.next(pl);
+        // i = -1 only maps chunk 0 (one call site of each step keeps the code small);
+        // a CTA without chunks runs no iteration (its cursor holds no piece)
+        for (int i = n > 0 ? -1 : 0; i < n && ok; ++i) {
+            if (i >= 0) {
+                ok = tc::bar_and(kBarTransform, kTransformThreads, wait_bar(&bars[F_MFULL], i & 1, P.status)) && ok;
+                if (!ok) break;
+                tc::tc_fence_after();
+                mask_pt();
+                tc::tc_fence_before();
+                tc::bar_sync(kBarTransform, kTransformThreads);
+                if (r == 0) tc::mbar_arrive(&bars[F_MDONEP]);
+                if (i + 1 < n) cu.next(pl);
+            }
             if (i + 1 < n && !transform(i + 1, cu)) break;
         }
     } else if (warp == kWarpMma) {
@@ -557,29 +561,27 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             tc::tmem_st32_raw_nowait(tmem + tcol + loff + hf * 32, packed);
         };
 
-        Cursor cu = cur0;
-        if (n > 0) {
-            install(cu);
-            publish(&bars[F_DSB]);
-            make_oc(0, where_of(p, pl, cu, kRev));
-        }
-        for (int i = 0; i < n && ok; ++i) {
-            const Where w = where_of(p, pl, cu, kRev);
+        // i = -1 only prepares chunk 0 (o^, c and its [dS | dz] operand): one call
+        // site of each step keeps the loop's code small. A CTA without chunks runs
+        // no iteration (its cursor holds no piece), and cn never steps past the range.
+        Cursor cu = cur0, cn = cur0;  // chunk i and chunk i + 1
+        for (int i = n > 0 ? -1 : 0; i < n && ok; ++i) {
             const int s = i % kStages;
-            const int mr_row = row_mask_raw(p, w, row);  // (for the epilogue; loaded early)
-            Cursor cn = cu;
-            cn.next(pl);  // the next chunk
-            // (1) mask dA^T (also into shared memory for dQ~); the feature-map warps mask P^T
-            if (!cwait(&bars[F_MFULLA], i & 1)) break;
-            mask_tile(cDAT, true);
-            tc::tmem_wait_st();
-            publish(&bars[F_MDONEA]);
+            int mr_row = 0;
+            if (i >= 0) {
+                mr_row = row_mask_raw(p, where_of(p, pl, cu, kRev), row);  // (for the epilogue; loaded early)
+                // (1) mask dA^T (also into shared memory for dQ~); the feature-map warps mask P^T
+                if (!cwait(&bars[F_MFULLA], i & 1)) break;
+                mask_tile(cDAT, true);
+                tc::tmem_wait_st();
+                publish(&bars[F_MDONEA]);
+            }
             // (2) o^, c of the next chunk (the tensor core runs this chunk's products)
             if (i + 1 < n && !make_oc(i + 1, where_of(p, pl, cn, kRev))) break;
             // (3) once the chunk's MMAs are done: [dS | dz] after this chunk, the next
             // chunk's operand (or the next piece's suffix), first, so that the next
             // chunk's [dS | dz] products can run while its masks are made
-            if (!cwait(&bars[F_DSFULL], i & 1)) break;
+            if (i >= 0 && !cwait(&bars[F_DSFULL], i & 1)) break;
             if (i + 1 < n) {
                 if (cn.first()) install(cn);
                 else refresh();
@@ -587,7 +589,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
             publish(&bars[F_DSB]);
             tc::tc_fence_after();
             // (4) epilogue; the producer stores the gradients
-            {
+            if (i >= 0) {
                 const float sm_ = p.scale * mask_f(mr_row);
                 uint32_t rv[32], rk[32], rq[32];
                 tc::tmem_ld32_issue(tmem + cPT + 64 + loff + hf * 32, rv);
@@ -620,6 +622,7 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 publish(&bars[F_OUT + s]);  // the producer stores them and reloads the stage
             }
             cu = cn;
+            if (i + 2 < n) cn.next(pl);
         }
     }
 
