@@ -136,24 +136,50 @@ def test_handover_from_another_call_is_reported():
     assert _capi.device_status() == _capi.SUBQ_OK  # read and cleared
 
 
+_FULL = {}
+
+
+def _full_size_case():
+    """The headline workload with the benchmark's own inputs: B=8, H=8, N=8192,
+    d=64 bf16, key-padding lengths U[N/2, N] (inputs seed 1234, lengths seed
+    4321, as bench.py rank 0 draws them), and the float64 oracle's forward and
+    backward on them (computed once for the tests below)."""
+    if not _FULL:
+        B, H, N, D = 8, 8, 8192, 64
+        g = torch.Generator(device="cpu").manual_seed(1234)
+        q, k, v, do = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16) for _ in range(4))
+        lens = torch.randint(N // 2, N + 1, (B,), generator=torch.Generator(device="cpu").manual_seed(4321))
+        m = torch.arange(N)[None, :] < lens[:, None]
+        f = lambda t: t.double().numpy()  # noqa: E731
+        mn = np.broadcast_to(m.double().numpy()[:, None, :], (B, H, N))
+        ref_o = oracle.forward(f(q), f(k), f(v), mask=mn, normalize=True, scale=1 / math.sqrt(D))[0]
+        rq, rk, rv, _ = oracle.backward(f(q), f(k), f(v), f(do), mask=mn, normalize=True, scale=1 / math.sqrt(D))
+        _FULL.update(inputs=(q, k, v, do, m), ref=(ref_o, rq, rk, rv))
+    return _FULL["inputs"], _FULL["ref"]
+
+
 def test_full_size_headline_workload_matches_oracle():
-    """The headline workload at its own size, with the benchmark's own inputs:
-    B=8, H=8, N=8192, d=64 bf16, key-padding lengths U[N/2, N] (inputs seed 1234,
-    lengths seed 4321, as bench.py rank 0 draws them), forward + one-pass backward as the
-    benchmark's step runs them, against the float64 oracle."""
-    B, H, N, D = 8, 8, 8192, 64
-    g = torch.Generator(device="cpu").manual_seed(1234)
-    q, k, v, do = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16) for _ in range(4))
-    lens = torch.randint(N // 2, N + 1, (B,), generator=torch.Generator(device="cpu").manual_seed(4321))
-    m = torch.arange(N)[None, :] < lens[:, None]
+    """Forward + one-pass backward at the headline size, as the benchmark's
+    step runs them (the forward hands its chunk states to the backward)."""
+    (q, k, v, do, m), (ref_o, rq, rk, rv) = _full_size_case()
     o, dq, dk, dv, launches = _run(q, k, v, do, m, None, True, False)
     assert launches == 2
-    f = lambda t: t.double().numpy()  # noqa: E731
-    mn = np.broadcast_to(m.double().numpy()[:, None, :], (B, H, N))
-    ref_o = oracle.forward(f(q), f(k), f(v), mask=mn, normalize=True, scale=1 / math.sqrt(D))[0]
-    assert rel_err(o, ref_o) < 2e-2, "o"
-    del ref_o
-    rq, rk, rv, _ = oracle.backward(f(q), f(k), f(v), f(do), mask=mn, normalize=True, scale=1 / math.sqrt(D))
-    assert rel_err(dq, rq) < 2e-2, "dq"
-    assert rel_err(dk, rk) < 2e-2, "dk"
-    assert rel_err(dv, rv) < 2e-2, "dv"
+    for name, got, ref in (("o", o, ref_o), ("dq", dq, rq), ("dk", dk, rk), ("dv", dv, rv)):
+        assert rel_err(got, ref) < 2e-2, name
+
+
+def test_full_size_through_reference_function():
+    """The same inputs through SubQAttentionFunction (the reference's autograd
+    entry point, autograd.py:547-660): its forward on the tensor cores and its
+    backward, which saves only q, k, v, w and recomputes the forward states."""
+    from subq_audio.autograd import SubQAttentionFunction
+
+    (q, k, v, do, m), (ref_o, rq, rk, rv) = _full_size_case()
+    qd, kd, vd = (x.cuda().requires_grad_(True) for x in (q, k, v))
+    o = SubQAttentionFunction.apply(qd, kd, vd, None, 64, m.cuda(), True)
+    o.backward(do.cuda())
+    torch.cuda.synchronize()
+    assert _capi.device_status() == _capi.SUBQ_OK
+    assert ops.last_path() == "tensorcore"
+    for name, got, ref in (("o", o.detach(), ref_o), ("dq", qd.grad, rq), ("dk", kd.grad, rk), ("dv", vd.grad, rv)):
+        assert rel_err(got, ref) < 2e-2, name
