@@ -129,26 +129,20 @@ static int max_active_clusters(const void* kern, int G, int threads, size_t smem
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        // clusters of 9-16 CTAs are a non-portable size (B200 allows 16)
-        if (G > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-            n = 0;
-        else if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess)
-            n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();  // a failed query leaves no sticky error behind
     cache[key] = n;
     return n;
 }
 
-// Segments (CTAs of one cluster) per sequence: the largest G <= 16 (and <= the
+// Segments (CTAs of one cluster) per sequence: the largest G <= 8 (and <= the
 // chunk count) for which every sequence's cluster is resident at once, so the
 // grid runs in one wave; G = 1 when even single CTAs need more than one wave.
-// 16 is B200's non-portable cluster limit: a few long sequences, as in
-// streaming inference, get 16 CTAs each.
 int pick_segments(const ScanParams& p, const void* kern, int threads, size_t smem) {
     const int nC = (p.N + kC - 1) / kC;
     const int bh = p.B * p.H;
-    for (int G = std::min(16, nC); G > 1; --G)
+    for (int G = std::min(8, nC); G > 1; --G)
         if (bh <= max_active_clusters(kern, G, threads, smem)) return G;
     return 1;
 }
@@ -156,10 +150,6 @@ int pick_segments(const ScanParams& p, const void* kern, int threads, size_t sme
 cudaError_t launch_cluster(const void* kern, int G, int BH, int threads, size_t smem, cudaStream_t st, void** args) {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    if (G > 8) {
-        err = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (err != cudaSuccess) return err;
-    }
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(G, BH, 1);

@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
 #pragma unroll
         for (int x = 0; x < 32; ++x) v[x] = 0.f;
         z = 0.f;
-        int pr[32], pb[32], np = 0;  // (<= 2 pieces per earlier CTA of the cluster)
+        int pr[16], pb[16], np = 0;
         for (int r = 0; r < P.G; ++r) {
             const PrefixShare sr = prefix_share(r, P.G, nL, cps);
             if (min(sr.b, sr.x) > sr.a && sr.seg < g) pr[np] = r, pb[np++] = 0;
@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_kernel(const __grid_consta
 #pragma unroll
         for (int x = 0; x < 32; ++x) v[x] = 0.f;
         z = 0.f;
-        int pr[16], pb[16], np = 0;  // (one piece per later CTA of the cluster)
+        int pr[8], pb[8], np = 0;
         for (int r = g + 1; r < P.G; ++r) pr[np] = r, pb[np++] = 0;
         float wl = 1.f;
         if (kDecay) {

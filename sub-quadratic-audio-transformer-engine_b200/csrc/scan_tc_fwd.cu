@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     for (int x = 0; x < 32; ++x) v[x] = 0.f;
     if (warp < 8) {
         const int quad = warp & 3, hf = warp >> 2, row = quad * 16 + (lane & 15);
-        int pr[32], pb[32], np = 0;  // the pieces of the segments before this one, in order (<= 2 per CTA)
+        int pr[16], pb[16], np = 0;  // the pieces of the segments before this one, in order
         for (int r = 0; r < P.G; ++r) {
             const PrefixShare sr = prefix_share(r, P.G, nL, cps);
             if (min(sr.b, sr.x) > sr.a && sr.seg < g) pr[np] = r, pb[np++] = 0;
