@@ -221,14 +221,19 @@ def engine_main(args):
     do = torch.empty_like(dq)
     raw = lambda: eng.forward_raw(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), do.data_ptr(), Be, Ne, De, 0.99)  # noqa: E731
     ms, clk = _device_timer(raw, reps, args.warmup)
+    from subq_audio import _capi, ops
+
+    raw()
+    torch.cuda.synchronize()
+    launches, path = _capi.last_launches(), ops.last_path()
     line = {"metric": "engine forward tokens/sec (B=1,N=1024,D=256 fp32)", "value": Be * Ne / (ms / 1e3),
             "unit": "tokens/s", "n_gpus": 1, "steps": reps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "SubQEngine.forward_raw B=1 N=1024 D=256 decay 0.99 (exact recurrent kernel)",
+            "config": {"workload": f"SubQEngine.forward_raw B=1 N=1024 D=256 decay 0.99 ({path} kernels)",
                        "l2": "3 MB of inputs fit in L2: a latency-bound single-sequence scan"},
             "e2e": {"value": Be * Ne / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 3 * q.nbytes,
                     "d2h_bytes_per_step": q.nbytes},
-            "gpu_launches": reps, "clocks": clk}
+            "gpu_launches": reps * launches, "clocks": clk}
     print(json.dumps(line))
     return 0
 

@@ -77,13 +77,16 @@ typedef enum subq_decay_mode {
 
 /* Which kernel family a call may use. AUTO picks the tensor-core path when
  * the shape allows it (bf16/fp16, d = e = 64; with per-token decay bf16
- * only) and the exact float32 path otherwise; calls of at most 16 tokens
- * (streaming decode steps) take the exact, token-recurrent path, which is
- * faster there. */
+ * only); otherwise the chunk-parallel float32 forward for calls of at least
+ * 64 tokens (d <= 256, forward time, scalar gamma <= 1), and the exact
+ * float32 path for the rest. Calls of at most 16 tokens (streaming decode
+ * steps) take the exact, token-recurrent path, which is faster there. The
+ * backward has no chunked variant: CHUNKED runs it on the exact path. */
 typedef enum subq_kernel_path {
     SUBQ_PATH_AUTO = 0,
-    SUBQ_PATH_EXACT = 1,      /* SIMT float32 sequential scan, any d, e <= 256 */
-    SUBQ_PATH_TENSORCORE = 2  /* tcgen05 chunked scan, bf16/fp16, d = e = 64   */
+    SUBQ_PATH_EXACT = 1,       /* SIMT float32 sequential scan, any d, e <= 256          */
+    SUBQ_PATH_TENSORCORE = 2,  /* tcgen05 chunked scan, bf16/fp16, d = e = 64            */
+    SUBQ_PATH_CHUNKED = 3      /* SIMT float32 chunk-parallel forward, d <= 256, no reverse */
 } subq_kernel_path;
 
 typedef struct subq_tensor4 {

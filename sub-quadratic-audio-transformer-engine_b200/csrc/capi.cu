@@ -47,7 +47,7 @@ int check_desc(const subq_scan_desc& d, subq::ScanParams& p) {
         return fail(SUBQ_ERR_INVALID_ARGUMENT, "unknown decay_mode");
     if ((d.decay_mode == SUBQ_DECAY_PER_HEAD || d.decay_mode == SUBQ_DECAY_PER_TOKEN) && !d.log_gamma)
         return fail(SUBQ_ERR_INVALID_ARGUMENT, "log_gamma pointer required by decay_mode");
-    if (d.path < SUBQ_PATH_AUTO || d.path > SUBQ_PATH_TENSORCORE)
+    if (d.path < SUBQ_PATH_AUTO || d.path > SUBQ_PATH_CHUNKED)
         return fail(SUBQ_ERR_INVALID_ARGUMENT, "unknown kernel path");
     if (!(d.clamp_min >= 0.f))
         return fail(SUBQ_ERR_INVALID_ARGUMENT, "clamp_min must be >= 0");
@@ -89,13 +89,21 @@ int check_tensor(const subq_tensor4& t, const char* name, int dtype, bool empty)
 constexpr int kRecurrentMaxTokens = 16;
 
 bool use_tc(const subq::ScanParams& p, int dtype, int path) {
-    if (path == SUBQ_PATH_EXACT || dtype == SUBQ_FP64) return false;
+    if (path == SUBQ_PATH_EXACT || path == SUBQ_PATH_CHUNKED || dtype == SUBQ_FP64) return false;
     if (path == SUBQ_PATH_AUTO && p.N <= kRecurrentMaxTokens) return false;
     return subq::tc_supported(p, dtype);
 }
 
 bool use_tc_bwd(const subq::ScanParams& p, int dtype, int path) {
     return use_tc(p, dtype, path) && subq::tc_bwd_supported(p, dtype);
+}
+
+// The forward's kernel family when the tensor cores do not take the call.
+int fwd_simt_path(const subq::ScanParams& p, int dtype, int path) {
+    if (path == SUBQ_PATH_CHUNKED) return subq::chunk_fwd_usable(p, dtype) ? SUBQ_PATH_CHUNKED : -1;
+    if (path == SUBQ_PATH_AUTO && p.N >= subq::kChunkMinTokens && subq::chunk_fwd_usable(p, dtype))
+        return SUBQ_PATH_CHUNKED;
+    return SUBQ_PATH_EXACT;
 }
 
 int fill_fwd(const subq_fwd_args* a, subq::ScanParams& p) {
@@ -219,6 +227,7 @@ size_t subq_fwd_workspace_bytes(const subq_fwd_args* a) {
     subq::ScanParams p;
     if (fill_fwd(a, p) != SUBQ_OK) return 0;
     if (use_tc(p, a->desc.dtype, a->desc.path)) return subq::tc_fwd_workspace_bytes(p);
+    if (fwd_simt_path(p, a->desc.dtype, a->desc.path) == SUBQ_PATH_CHUNKED) return subq::chunk_fwd_workspace_bytes(p);
     return 0;
 }
 
@@ -241,8 +250,13 @@ int subq_fwd(const subq_fwd_args* a) {
     const bool tc = use_tc(p, a->desc.dtype, a->desc.path);
     if (a->desc.path == SUBQ_PATH_TENSORCORE && !tc)
         return fail(SUBQ_ERR_UNSUPPORTED, "tensor-core path needs bf16/fp16 with head_dim = value_dim = 64");
+    const int simt = tc ? SUBQ_PATH_TENSORCORE : fwd_simt_path(p, a->desc.dtype, a->desc.path);
+    if (simt < 0)
+        return fail(SUBQ_ERR_UNSUPPORTED,
+                    "chunked path needs fp32/fp16/bf16, head_dim <= 256, forward time and no decay fallback");
+    const int used = tc ? SUBQ_PATH_TENSORCORE : simt;
     if (p.B == 0 || p.H == 0) {
-        g_last_path = tc ? SUBQ_PATH_TENSORCORE : SUBQ_PATH_EXACT;
+        g_last_path = used;
         g_last_launches = 0;
         return SUBQ_OK;
     }
@@ -259,12 +273,18 @@ int subq_fwd(const subq_fwd_args* a) {
         if ((rc = check_workspace(a->workspace, a->workspace_bytes, need))) return rc;
         p.ws = static_cast<float*>(a->workspace);
         err = subq::launch_fwd_tc(p, a->desc.dtype, st, &launches);
+    } else if (used == SUBQ_PATH_CHUNKED) {
+        const size_t need = subq::chunk_fwd_workspace_bytes(p);
+        if ((rc = check_workspace(a->workspace, a->workspace_bytes, need))) return rc;
+        p.ws = static_cast<float*>(a->workspace);
+        err = subq::launch_fwd_chunk(p, a->desc.dtype, st);
+        launches = 2;
     } else {
         err = subq::launch_fwd_exact(p, a->desc.dtype, st);
         launches = 1;
     }
     if (err != cudaSuccess) return fail_cuda(err, "subq_fwd launch");
-    g_last_path = tc ? SUBQ_PATH_TENSORCORE : SUBQ_PATH_EXACT;
+    g_last_path = used;
     g_last_launches = launches;
     return SUBQ_OK;
 }

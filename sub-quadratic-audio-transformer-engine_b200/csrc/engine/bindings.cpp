@@ -107,10 +107,15 @@ public:
                 prepare_state(B, D, normalize, carry_state);
                 const size_t saved = arena_.get_offset();
                 const size_t avail = arena_.get_total_bytes() > saved ? arena_.get_total_bytes() - saved : 0;
-                // four chunk buffers, each rounded up to the arena's 256-byte alignment
-                const size_t denom = 4 * B * D * sizeof(float);
-                const size_t usable = avail > 4 * 255 ? avail - 4 * 255 : 0;
-                const size_t max_chunk = denom ? usable / denom : 1024;
+                // four piece buffers, each rounded up to the arena's 256-byte alignment, and
+                // the kernels' workspace: at most (64-token pieces + 1) x that of 64 tokens
+                const size_t buf_tok = 4 * B * D * sizeof(float);
+                const size_t ws64 = N >= 64 ? forward_workspace(B, 64, D, decay_factor, normalize) : 0;
+                size_t max_chunk = 0;
+                if (buf_tok && ws64 && avail > 5 * 255 + ws64)
+                    max_chunk = (avail - 5 * 255 - ws64) / (buf_tok + (ws64 + 63) / 64);
+                if (max_chunk < 64)  // too little room for it: pieces without (the exact path)
+                    max_chunk = !buf_tok ? 1024 : avail > 4 * 255 ? (avail - 4 * 255) / buf_tok : 0;
                 const size_t chunk = std::max<size_t>(1, std::min<size_t>(max_chunk, 16384));
                 for (size_t t = 0; t < N; t += chunk) {
                     const size_t cur = std::min(chunk, N - t);
@@ -267,6 +272,18 @@ private:
     void run_forward(void* q, void* k, void* v, void* o, size_t B, size_t N, size_t D, float decay_factor,
                      bool normalize) {
         if (!(decay_factor >= 0.f)) throw std::invalid_argument("decay_factor must be a number >= 0");
+        engine_.forward(forward_args(q, k, v, o, B, N, D, decay_factor, normalize));
+    }
+
+    // Device workspace of a forward over N tokens (0 on the exact path).
+    size_t forward_workspace(size_t B, size_t N, size_t D, float decay_factor, bool normalize) {
+        void* any = reinterpret_cast<void*>(256);  // the query reads shapes, not data
+        subq_fwd_args a = forward_args(any, any, any, any, B, N, D, decay_factor, normalize);
+        return subq_fwd_workspace_bytes(&a);
+    }
+
+    subq_fwd_args forward_args(void* q, void* k, void* v, void* o, size_t B, size_t N, size_t D,
+                               float decay_factor, bool normalize) {
         subq_fwd_args a{};
         a.desc.batch = (int64_t)B;
         a.desc.heads = 1;
@@ -299,7 +316,7 @@ private:
             a.norm_in = z_;
             a.norm_out = z_;
         }
-        engine_.forward(a);
+        return a;
     }
 
     int device_id_{0};

@@ -92,7 +92,15 @@ void Engine::forward(AttentionContext& ctx, void* stream) {
 
 void Engine::forward(subq_fwd_args a) {
     ArenaMark mark(arena_);
-    const size_t need = subq_fwd_workspace_bytes(&a);
+    size_t need = subq_fwd_workspace_bytes(&a);
+    // The automatic path's chunked kernels need a workspace of about 0.8 KB
+    // per token at head_dim 64 (34 KB at 256); when the arena cannot hold it,
+    // the call runs on the exact path, which needs none.
+    const size_t room = arena_.get_total_bytes() - arena_.get_offset();
+    if (a.desc.path == SUBQ_PATH_AUTO && need + 256 > room) {
+        a.desc.path = SUBQ_PATH_EXACT;
+        need = subq_fwd_workspace_bytes(&a);
+    }
     if (need) {
         a.workspace = arena_.allocate(need);
         a.workspace_bytes = need;

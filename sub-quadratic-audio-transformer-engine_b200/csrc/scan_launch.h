@@ -19,6 +19,14 @@ cudaError_t launch_feature_map(void* x, int64_t n, int dtype, cudaStream_t st);
 cudaError_t launch_group_sum(const void* src, void* dst, int dtype, int B, int Hkv, int G, int N, int e,
                              int64_t dsb, int64_t dsh, int64_t dsn, cudaStream_t st);
 
+// Chunk-parallel float32 forward on the CUDA cores (scan_chunk.cu): the
+// automatic path's choice for calls of at least kChunkMinTokens tokens that
+// the tensor-core kernels do not take (float32, or d, e other than 64).
+constexpr int kChunkMinTokens = 64;
+bool chunk_fwd_usable(const ScanParams& p, int dtype);
+size_t chunk_fwd_workspace_bytes(const ScanParams& p);
+cudaError_t launch_fwd_chunk(const ScanParams& p, int dtype, cudaStream_t st);  // 2 launches
+
 // Tensor-core path (scan_tc.cu).
 bool tc_supported(const ScanParams& p, int dtype);
 bool tc_bwd_supported(const ScanParams& p, int dtype);

@@ -24,7 +24,7 @@ SUBQ_ERR_STATE = 7
 
 SUBQ_FP32, SUBQ_FP16, SUBQ_BF16, SUBQ_FP64 = 0, 1, 2, 3
 SUBQ_DECAY_NONE, SUBQ_DECAY_SCALAR, SUBQ_DECAY_PER_HEAD, SUBQ_DECAY_PER_TOKEN = 0, 1, 2, 3
-SUBQ_PATH_AUTO, SUBQ_PATH_EXACT, SUBQ_PATH_TENSORCORE = 0, 1, 2
+SUBQ_PATH_AUTO, SUBQ_PATH_EXACT, SUBQ_PATH_TENSORCORE, SUBQ_PATH_CHUNKED = 0, 1, 2, 3
 
 # Every symbol include/kernels.hpp declares.
 EXPORTED = (

@@ -15,7 +15,8 @@ from . import _capi
 
 _DTYPES = {torch.float32: _capi.SUBQ_FP32, torch.float16: _capi.SUBQ_FP16, torch.bfloat16: _capi.SUBQ_BF16,
            torch.float64: _capi.SUBQ_FP64}
-_PATHS = {"auto": _capi.SUBQ_PATH_AUTO, "exact": _capi.SUBQ_PATH_EXACT, "tensorcore": _capi.SUBQ_PATH_TENSORCORE}
+_PATHS = {"auto": _capi.SUBQ_PATH_AUTO, "exact": _capi.SUBQ_PATH_EXACT, "tensorcore": _capi.SUBQ_PATH_TENSORCORE,
+          "chunked": _capi.SUBQ_PATH_CHUNKED}
 
 LogGamma = Union[None, float, torch.Tensor]
 
@@ -339,7 +340,7 @@ def check_device_status(device: Optional[torch.device] = None) -> None:
 
 
 def last_path() -> str:
-    return {0: "auto", 1: "exact", 2: "tensorcore"}.get(_capi.last_path(), "?")
+    return {0: "auto", 1: "exact", 2: "tensorcore", 3: "chunked"}.get(_capi.last_path(), "?")
 
 
 def last_launches() -> int:

@@ -205,9 +205,9 @@ def test_gated_module_runs_on_tensor_cores_and_matches_exact():
     y.float().square().mean().backward()
     g_tc = {n: p.grad.detach().clone() for n, p in mod.named_parameters()}
     mod.zero_grad()
-    y32, _ = mod(x)  # float32 inputs: the exact kernels
+    y32, _ = mod(x)  # float32 inputs: the CUDA-core kernels (chunked forward, exact backward)
     y32.square().mean().backward()
-    assert ops.last_path() == "exact"
+    assert ops.last_path() in ("exact", "chunked")
     assert rel_err(y, y32.detach().double().cpu().numpy()) < 3e-2
     for n, p in mod.named_parameters():
         assert rel_err(g_tc[n], p.grad.double().cpu().numpy()) < 5e-2, n
