@@ -326,7 +326,7 @@ def encoder_main(args, rank, world, local_rank):
                            "l2": "activations far above the 126 MB L2"},
                 "e2e": {"value": tokens / (ms / 1e3), "unit": "tokens/s",
                         "h2d_bytes_per_step": x_h.numel() * 4, "d2h_bytes_per_step": 4},
-                "gpu_launches": 4 * 12 * args.steps, "clocks": clk}
+                "gpu_launches": 7 * 12 * args.steps, "clocks": clk}
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

@@ -14,6 +14,9 @@
  *                       run_attention_backward_ex(...)                   include/attention.hpp:26-32
  *                       _single_direction_causal_backward                python/subq_audio/autograd.py:441-544
  *   subq_feature_map    run_feature_map(TensorDescriptor&)               include/attention.hpp:22
+ *   subq_head_rmsnorm_fwd / _bwd
+ *                       SubQLinearAttention's per-head nn.RMSNorm and the
+ *                       transpose copy after it                          python/subq_audio/autograd.py:706-710,763-769
  *   subq_*_workspace_bytes, subq_last_error, subq_abi_version, subq_device_info:
  *                       no single counterpart; they carry the reference's
  *                       scratch allocation (attention_backward.cpp:305-361 allocated
@@ -49,7 +52,7 @@
 extern "C" {
 #endif
 
-#define SUBQ_ABI_VERSION 4
+#define SUBQ_ABI_VERSION 5
 
 typedef enum subq_status {
     SUBQ_OK = 0,
@@ -179,6 +182,36 @@ size_t subq_segment_states_bytes(const subq_fwd_args* args);
 
 /* In-place phi(x) = ELU(x) + 1 over n contiguous elements (run_feature_map). */
 int subq_feature_map(void* x, int64_t n, int32_t dtype, void* stream);
+
+/* Per-head RMSNorm of the scan's output, y = x * rsqrt(mean_D(x^2) + eps) * w
+ * over each row of D values (one token of one head): SubQLinearAttention's
+ * nn.RMSNorm(head_dim, eps=1e-5) and the [B, H, L, D] -> [B, L, H*D] copy
+ * after it (reference python/subq_audio/autograd.py:706-710, 763-769); y is
+ * written through its own strides, so giving it the [B, L, H, D] layout
+ * replaces the copy. Math in float32 whatever the dtype (fp32, fp16 or bf16).
+ * x, y, dy and dx are [B, H, N, D] views with element strides; D is 8, 16,
+ * 32, 64, 128 or 256 (SUBQ_ERR_UNSUPPORTED otherwise); every row starts on a
+ * 16-byte boundary (data and strides). The backward reads x and dy and writes
+ *   dx = r (dy w - xh mean_D(dy w xh)),  xh = x r,  r = rsqrt(mean_D(x^2) + eps)
+ * and, when `dweight` is given, dweight = sum over rows of dy xh (written,
+ * not accumulated; bitwise reproducible), which needs `workspace` of
+ * subq_head_rmsnorm_bwd_workspace_bytes. dx may be x or dy (in place). */
+typedef struct subq_rmsnorm_args {
+    int64_t batch, heads, seq_len, head_dim;
+    int32_t dtype;
+    float eps;
+    subq_tensor4 x, y;      /* forward: input and output (the backward reads x) */
+    subq_tensor4 dy, dx;    /* backward: upstream gradient and input gradient */
+    const float* weight;    /* [D] float32, or NULL for a weight of 1 */
+    float* dweight;         /* backward: [D] float32, or NULL */
+    void* workspace;
+    size_t workspace_bytes;
+    void* stream;
+} subq_rmsnorm_args;
+
+int subq_head_rmsnorm_fwd(const subq_rmsnorm_args* args);
+int subq_head_rmsnorm_bwd(const subq_rmsnorm_args* args);
+size_t subq_head_rmsnorm_bwd_workspace_bytes(const subq_rmsnorm_args* args);
 
 /* Backward scan with no allocation and no caller workspace (no counterpart in
  * the reference, whose backward allocates its scratch on every call). For

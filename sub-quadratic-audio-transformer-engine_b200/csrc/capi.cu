@@ -351,6 +351,90 @@ int subq_feature_map(void* x, int64_t n, int32_t dtype, void* stream) {
     return SUBQ_OK;
 }
 
+// Checks of a per-head RMSNorm call; fills p. Rows must be 16-byte aligned
+// (the kernels move 8 elements per thread).
+static int fill_rms(const subq_rmsnorm_args* a, subq::RmsParams& p, bool bwd) {
+    if (!a) return fail(SUBQ_ERR_INVALID_ARGUMENT, "null argument block");
+    if (a->batch < 0 || a->heads < 0 || a->seq_len < 0 || a->head_dim <= 0)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "negative batch, heads or seq_len, or head_dim <= 0");
+    if (a->batch > 65535 || a->heads > 65535 || a->seq_len > (int64_t)1 << 30)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "batch/heads above 65535 or seq_len above 2^30");
+    if (a->dtype != SUBQ_FP32 && a->dtype != SUBQ_FP16 && a->dtype != SUBQ_BF16)
+        return fail(SUBQ_ERR_INVALID_ARGUMENT, "head RMSNorm supports float32, float16 and bfloat16");
+    if (!subq::rms_supported_dim((int)a->head_dim))
+        return fail(SUBQ_ERR_UNSUPPORTED, "head RMSNorm needs head_dim 8, 16, 32, 64, 128 or 256");
+    if (!(a->eps >= 0.f) || a->eps > 1e30f) return fail(SUBQ_ERR_INVALID_ARGUMENT, "eps must be >= 0 and finite");
+    p = subq::RmsParams{};
+    p.B = (int)a->batch; p.H = (int)a->heads; p.N = (int)a->seq_len; p.D = (int)a->head_dim;
+    p.eps = a->eps;
+    p.w = a->weight;
+    const bool empty = p.B == 0 || p.H == 0 || p.N == 0;
+    const size_t es = elem_size(a->dtype);
+    auto rows_aligned = [&](const subq_tensor4& t, const char* name) {
+        int rc = check_tensor(t, name, a->dtype, empty);
+        if (rc) return rc;
+        if (reinterpret_cast<uintptr_t>(t.data) % 16 != 0 || (t.stride_b * es) % 16 != 0 ||
+            (t.stride_h * es) % 16 != 0 || (t.stride_n * es) % 16 != 0)
+            return fail(SUBQ_ERR_INVALID_ARGUMENT, std::string(name) + ": rows must start on 16-byte boundaries");
+        return (int)SUBQ_OK;
+    };
+    int rc = rows_aligned(a->x, "x");
+    if (rc) return rc;
+    p.x = a->x.data; p.x_sb = a->x.stride_b; p.x_sh = a->x.stride_h; p.x_sn = a->x.stride_n;
+    if (!bwd) {
+        if ((rc = rows_aligned(a->y, "y"))) return rc;
+        p.y = a->y.data; p.y_sb = a->y.stride_b; p.y_sh = a->y.stride_h; p.y_sn = a->y.stride_n;
+    } else {
+        if ((rc = rows_aligned(a->dy, "dy")) || (rc = rows_aligned(a->dx, "dx"))) return rc;
+        p.dy = a->dy.data; p.dy_sb = a->dy.stride_b; p.dy_sh = a->dy.stride_h; p.dy_sn = a->dy.stride_n;
+        p.dx = a->dx.data; p.dx_sb = a->dx.stride_b; p.dx_sh = a->dx.stride_h; p.dx_sn = a->dx.stride_n;
+        p.dw = a->dweight;
+    }
+    return SUBQ_OK;
+}
+
+size_t subq_head_rmsnorm_bwd_workspace_bytes(const subq_rmsnorm_args* a) {
+    subq::RmsParams p;
+    if (fill_rms(a, p, true) != SUBQ_OK || !a->dweight) return 0;
+    return align_up((size_t)subq::rms_blocks(p) * p.D * sizeof(float));
+}
+
+int subq_head_rmsnorm_fwd(const subq_rmsnorm_args* a) {
+    subq::RmsParams p;
+    int rc = fill_rms(a, p, false);
+    if (rc) return rc;
+    g_last_launches = 0;
+    if (p.B == 0 || p.H == 0 || p.N == 0) return SUBQ_OK;
+    cudaError_t err = subq::launch_rms_fwd(p, a->dtype, static_cast<cudaStream_t>(a->stream));
+    if (err != cudaSuccess) return fail_cuda(err, "subq_head_rmsnorm_fwd launch");
+    g_last_launches = 1;
+    return SUBQ_OK;
+}
+
+int subq_head_rmsnorm_bwd(const subq_rmsnorm_args* a) {
+    subq::RmsParams p;
+    int rc = fill_rms(a, p, true);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(a->stream);
+    g_last_launches = 0;
+    if (p.B == 0 || p.H == 0 || p.N == 0) {  // no rows: dweight is 0
+        if (p.dw) {
+            cudaError_t err = cudaMemsetAsync(p.dw, 0, sizeof(float) * p.D, st);
+            if (err != cudaSuccess) return fail_cuda(err, "subq_head_rmsnorm_bwd dweight");
+        }
+        return SUBQ_OK;
+    }
+    if (p.dw) {
+        const size_t need = (size_t)subq::rms_blocks(p) * p.D * sizeof(float);
+        if ((rc = check_workspace(a->workspace, a->workspace_bytes, need))) return rc;
+        p.part = static_cast<float*>(a->workspace);
+    }
+    cudaError_t err = subq::launch_rms_bwd(p, a->dtype, st);
+    if (err != cudaSuccess) return fail_cuda(err, "subq_head_rmsnorm_bwd launch");
+    g_last_launches = p.dw ? 2 : 1;
+    return SUBQ_OK;
+}
+
 int subq_device_info(int device, char* arch, size_t arch_len, size_t* memory_bytes, int* bf16_supported) {
     cudaDeviceProp prop;
     cudaError_t err = cudaGetDeviceProperties(&prop, device);

@@ -27,6 +27,25 @@ bool chunk_fwd_usable(const ScanParams& p, int dtype);
 size_t chunk_fwd_workspace_bytes(const ScanParams& p);
 cudaError_t launch_fwd_chunk(const ScanParams& p, int dtype, cudaStream_t st);  // 2 launches
 
+// Per-head RMSNorm of the scan's output (head_norm.cu). Rows are the
+// (b, n, h) of [B, H, N, D] views with element strides; D contiguous.
+struct RmsParams {
+    int B, H, N, D;
+    float eps;
+    const void* x; int64_t x_sb, x_sh, x_sn;     // input (the scan's output)
+    void* y; int64_t y_sb, y_sh, y_sn;           // forward output
+    const void* dy; int64_t dy_sb, dy_sh, dy_sn; // backward: upstream gradient
+    void* dx; int64_t dx_sb, dx_sh, dx_sn;       // backward: input gradient
+    const float* w;                              // [D] or null (weight 1)
+    float* dw;                                   // backward: [D] or null
+    float* part;                                 // backward: [rms_blocks][D] CTA partials of dw
+};
+constexpr int kRmsMaxBlocks = 148 * 8;
+bool rms_supported_dim(int D);
+int rms_blocks(const RmsParams& p);
+cudaError_t launch_rms_fwd(const RmsParams& p, int dtype, cudaStream_t st);  // 1 launch
+cudaError_t launch_rms_bwd(const RmsParams& p, int dtype, cudaStream_t st);  // 2 launches with dw, else 1
+
 // Tensor-core path (scan_tc.cu).
 bool tc_supported(const ScanParams& p, int dtype);
 bool tc_bwd_supported(const ScanParams& p, int dtype);

@@ -32,6 +32,7 @@ EXPORTED = (
     "subq_feature_map", "subq_last_path", "subq_last_launches", "subq_last_error",
     "subq_abi_version", "subq_device_info", "subq_device_status", "subq_bwd_noalloc",
     "subq_segment_states_bytes", "subq_selftest_wait_timeout",
+    "subq_head_rmsnorm_fwd", "subq_head_rmsnorm_bwd", "subq_head_rmsnorm_bwd_workspace_bytes",
 )
 
 
@@ -72,6 +73,17 @@ class BwdArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("stream", ctypes.c_void_p), ("segment_states", ctypes.c_void_p),
         ("out", Tensor4),
+    ]
+
+
+class RmsArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("seq_len", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64), ("dtype", ctypes.c_int32), ("eps", ctypes.c_float),
+        ("x", Tensor4), ("y", Tensor4), ("dy", Tensor4), ("dx", Tensor4),
+        ("weight", ctypes.c_void_p), ("dweight", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+        ("stream", ctypes.c_void_p),
     ]
 
 
@@ -124,6 +136,11 @@ def load() -> ctypes.CDLL:
             lib.subq_device_status.restype = ctypes.c_int
             lib.subq_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_void_p]
             lib.subq_selftest_wait_timeout.restype = ctypes.c_int
+            for name in ("subq_head_rmsnorm_fwd", "subq_head_rmsnorm_bwd"):
+                getattr(lib, name).argtypes = [ctypes.POINTER(RmsArgs)]
+                getattr(lib, name).restype = ctypes.c_int
+            lib.subq_head_rmsnorm_bwd_workspace_bytes.argtypes = [ctypes.POINTER(RmsArgs)]
+            lib.subq_head_rmsnorm_bwd_workspace_bytes.restype = ctypes.c_size_t
             _lib = lib
     return _lib
 
@@ -147,6 +164,18 @@ def bwd(args: BwdArgs) -> None:
 def bwd_noalloc(args: BwdArgs) -> None:
     """subq_bwd_noalloc: the backward with the library's static scratch."""
     check(load().subq_bwd_noalloc(ctypes.byref(args)))
+
+
+def head_rmsnorm_fwd(args: RmsArgs) -> None:
+    check(load().subq_head_rmsnorm_fwd(ctypes.byref(args)))
+
+
+def head_rmsnorm_bwd(args: RmsArgs) -> None:
+    check(load().subq_head_rmsnorm_bwd(ctypes.byref(args)))
+
+
+def head_rmsnorm_bwd_workspace_bytes(args: RmsArgs) -> int:
+    return int(load().subq_head_rmsnorm_bwd_workspace_bytes(ctypes.byref(args)))
 
 
 def fwd_workspace_bytes(args: FwdArgs) -> int:

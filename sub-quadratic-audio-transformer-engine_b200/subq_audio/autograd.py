@@ -181,6 +181,29 @@ class _CausalScan(torch.autograd.Function):
         return dq, dk, dv, glg, None, None, None, None, None
 
 
+class _HeadRMSNorm(torch.autograd.Function):
+    """Per-head RMSNorm of the scan's output on the library's kernels
+    (``subq_audio::head_rmsnorm_fwd`` / ``_bwd``): the reference's
+    ``nn.RMSNorm(head_dim)`` and the transpose copy after it
+    (python/subq_audio/autograd.py:763-769). The output is a [B, H, N, D] view
+    of a [B, N, H, D] buffer, so the transpose back for the output projection
+    is a view; the backward recomputes the row scale from x."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        y = torch.ops.subq_audio.head_rmsnorm_fwd(x, weight, eps)
+        ctx.eps = eps
+        ctx.save_for_backward(x, weight)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dx, dw = torch.ops.subq_audio.head_rmsnorm_bwd(dy, x, w, ctx.eps)
+        gw = dw.to(w.dtype) if (w is not None and ctx.needs_input_grad[1]) else None
+        return dx, gw, None
+
+
 def _to_device_inputs(q, k, v):
     if q.is_cuda:
         return q, k, v, None
@@ -396,16 +419,19 @@ class SubQLinearAttention(nn.Module):
         # view), so the transpose back below needs no copy
         out, next_state = _chunkwise(Q, K, V, decay_w, past_state, attention_mask, self.is_causal,
                                      want_state=use_cache)
-        if self.head_norm is not None:
-            # with the weight in the activations' dtype torch runs its fused RMSNorm
-            # kernel (an fp32 weight on bf16 activations takes an unfused path)
-            w = self.head_norm.weight
-            if w is not None and w.dtype != out.dtype:
-                w = w.to(out.dtype)
-            out = F.rms_norm(out, self.head_norm.normalized_shape, w, self.head_norm.eps)
+        if ops.head_rmsnorm_supported(out):
+            # the library's per-head RMSNorm (float32 math with the float32 weight);
+            # it writes [B, L, H, D] memory, so the transpose back is a view
+            w = self.head_norm.weight if self.head_norm is not None else None
+            eps = self.head_norm.eps if (self.head_norm is not None and self.head_norm.eps is not None) else 1e-5
+            out = _HeadRMSNorm.apply(out, w, eps)
+            out = out.transpose(1, 2).reshape(B, L, self.hidden_size)
         else:
-            out = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + 1e-5)
-        out = out.transpose(1, 2).contiguous().view(B, L, self.hidden_size)
+            if self.head_norm is not None:
+                out = self.head_norm(out)
+            else:
+                out = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + 1e-5)
+            out = out.transpose(1, 2).contiguous().view(B, L, self.hidden_size)
         return self.out_proj(out), (next_state if use_cache else None)
 
 

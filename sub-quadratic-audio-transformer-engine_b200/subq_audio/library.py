@@ -118,3 +118,31 @@ def _scan_bwd_fake(q, k, v, dout, log_gamma, mask, S0, z0, o, handover, reverse,
     dv = ops._empty_in_order(v, tuple(v.shape), q.dtype)
     dlg = _empty_f32(q, (B, H, N) if need_dlog_gamma else (0,))
     return dq, dk, dv, dlg
+
+
+# Per-head RMSNorm of the scan's output (the module epilogue):
+#     y = torch.ops.subq_audio.head_rmsnorm_fwd(x, weight, eps)
+#     dx, dweight = torch.ops.subq_audio.head_rmsnorm_bwd(dy, x, weight, eps)
+# y is a [B, H, N, D] view of a [B, N, H, D] buffer; dweight is float32 [D]
+# (empty without a weight).
+@torch.library.custom_op("subq_audio::head_rmsnorm_fwd", mutates_args=(), device_types="cuda")
+def head_rmsnorm_fwd(x: Tensor, weight: Optional[Tensor], eps: float) -> Tensor:
+    return ops.head_rmsnorm(x, weight, eps)
+
+
+@head_rmsnorm_fwd.register_fake
+def _head_rmsnorm_fwd_fake(x, weight, eps):
+    B, H, N, D = x.shape
+    return x.new_empty((B, N, H, D)).transpose(1, 2)
+
+
+@torch.library.custom_op("subq_audio::head_rmsnorm_bwd", mutates_args=(), device_types="cuda")
+def head_rmsnorm_bwd(dy: Tensor, x: Tensor, weight: Optional[Tensor], eps: float) -> Tuple[Tensor, Tensor]:
+    dx, dw = ops.head_rmsnorm_backward(dy, x, weight, eps, need_dweight=weight is not None)
+    return dx, (dw if dw is not None else _empty_f32(x, (0,)))
+
+
+@head_rmsnorm_bwd.register_fake
+def _head_rmsnorm_bwd_fake(dy, x, weight, eps):
+    dx = ops._empty_in_order(x, tuple(x.shape), x.dtype)
+    return dx, _empty_f32(x, (x.shape[-1],) if weight is not None else (0,))

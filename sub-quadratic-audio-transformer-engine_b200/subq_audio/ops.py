@@ -339,6 +339,87 @@ def check_device_status(device: Optional[torch.device] = None) -> None:
                                   "call; its gradients are not valid")
 
 
+_RMS_DIMS = (8, 16, 32, 64, 128, 256)
+
+
+def head_rmsnorm_supported(x: torch.Tensor) -> bool:
+    """True when the per-head RMSNorm kernels take x ([B, H, N, D] CUDA,
+    float32/float16/bfloat16, D in 8..256 a power of two)."""
+    return (x.is_cuda and x.dim() == 4 and x.shape[-1] in _RMS_DIMS
+            and x.dtype in (torch.float32, torch.float16, torch.bfloat16))
+
+
+def _rows16(t: torch.Tensor) -> torch.Tensor:
+    """t itself when its rows start on 16-byte boundaries, else a contiguous copy."""
+    es = t.element_size()
+    if (t.stride(-1) == 1 and t.data_ptr() % 16 == 0
+            and all((s * es) % 16 == 0 for s in t.stride()[:3])):
+        return t
+    return t.contiguous()
+
+
+def _rms_args(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float, keep: list) -> _capi.RmsArgs:
+    B, H, N, D = x.shape
+    a = _capi.RmsArgs()
+    a.batch, a.heads, a.seq_len, a.head_dim = B, H, N, D
+    a.dtype = _DTYPES[x.dtype]
+    a.eps = float(eps)
+    a.x = _t4(x)
+    if weight is not None:
+        w = weight.detach().to(device=x.device, dtype=torch.float32).contiguous()
+        if w.shape != (D,):
+            raise ValueError(f"weight must have shape ({D},), got {tuple(weight.shape)}")
+        keep.append(w)
+        a.weight = w.data_ptr()
+    a.stream = torch.cuda.current_stream(x.device).cuda_stream
+    return a
+
+
+def head_rmsnorm(x: torch.Tensor, weight: Optional[torch.Tensor] = None, eps: float = 1e-5) -> torch.Tensor:
+    """Per-head RMSNorm y = x * rsqrt(mean(x^2, -1) + eps) * weight of a
+    [B, H, N, D] scan output (float32 math). y is a [B, H, N, D] view of a
+    [B, N, H, D] buffer, so ``y.transpose(1, 2).reshape(B, N, H * D)`` -- the
+    output projection's input -- is a view, not a copy."""
+    _require_cuda(x)
+    if not head_rmsnorm_supported(x):
+        raise ValueError(f"head_rmsnorm needs a [B, H, N, D] float32/float16/bfloat16 tensor with D in {_RMS_DIMS}")
+    x = _rows16(x)
+    B, H, N, D = x.shape
+    y = torch.empty(B, N, H, D, dtype=x.dtype, device=x.device).transpose(1, 2)
+    keep: list = []
+    with torch.cuda.device(x.device):
+        a = _rms_args(x, weight, eps, keep)
+        a.y = _t4(y)
+        _capi.head_rmsnorm_fwd(a)
+    return y
+
+
+def head_rmsnorm_backward(dy: torch.Tensor, x: torch.Tensor, weight: Optional[torch.Tensor] = None,
+                          eps: float = 1e-5, need_dweight: bool = True
+                          ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Gradients of ``head_rmsnorm``: dx (in x's memory order, x's dtype) and,
+    with a weight and ``need_dweight``, d weight (float32 [D])."""
+    _require_cuda(dy, x)
+    if not head_rmsnorm_supported(x) or dy.shape != x.shape or dy.dtype != x.dtype:
+        raise ValueError("head_rmsnorm_backward needs dy and x of one supported shape and dtype")
+    x, dy = _rows16(x), _rows16(dy)
+    D = x.shape[-1]
+    dx = _empty_in_order(x, tuple(x.shape), x.dtype)
+    dw = torch.empty(D, dtype=torch.float32, device=x.device) if (need_dweight and weight is not None) else None
+    keep: list = []
+    with torch.cuda.device(x.device):
+        a = _rms_args(x, weight, eps, keep)
+        a.dy, a.dx = _t4(dy), _t4(dx)
+        if dw is not None:
+            a.dweight = dw.data_ptr()
+            nbytes = _capi.head_rmsnorm_bwd_workspace_bytes(a)
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+            a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
+            keep.append(ws)
+        _capi.head_rmsnorm_bwd(a)
+    return dx, dw
+
+
 def last_path() -> str:
     return {0: "auto", 1: "exact", 2: "tensorcore", 3: "chunked"}.get(_capi.last_path(), "?")
 

@@ -65,7 +65,7 @@ def _fwd_args(B=1, H=1, N=8, d=4, e=4, dtype=_capi.SUBQ_FP32):
 
 def test_abi_version_and_error_text():
     lib = _capi.load()
-    assert lib.subq_abi_version() == 4
+    assert lib.subq_abi_version() == 5
     a = _fwd_args()
     a.desc.head_dim = 0
     assert lib.subq_fwd(ctypes.byref(a)) == _capi.SUBQ_ERR_INVALID_ARGUMENT
