@@ -397,13 +397,57 @@ class SubQLinearAttention(nn.Module):
     def decay_factor(self) -> torch.Tensor:
         return torch.sigmoid(self.raw_decay)
 
+    def _fused_projections(self, x: torch.Tensor):
+        """q, k, v and the gate from ONE GEMM over the concatenated weights
+        (rows padded to a multiple of 8, so every output row starts on a 16-byte
+        boundary), returned as strided views of its [B, L, R] output. Against
+        four nn.Linear calls this casts x once under autocast, and its backward
+        forms dx in one GEMM instead of four GEMMs and three adds. The
+        parameters stay the four Linear modules (the reference's state-dict
+        names); their gradients come back through the concatenation. None when
+        a projection is not a plain nn.Linear or the sizes do not align."""
+        mods = [self.q_proj, self.k_proj, self.v_proj]
+        if self.use_data_dependent_gating and self.gate_proj is not None:
+            mods.append(self.gate_proj)
+        if not x.is_cuda or any(type(m) is not nn.Linear for m in mods):
+            return None
+        outs = [m.out_features for m in mods]
+        if any(o % 8 for o in outs[:3]):
+            return None
+        rows = sum(outs)
+        pad = -rows % 8
+        ws = [m.weight for m in mods]
+        if len({(w.dtype, w.device) for w in ws}) != 1:
+            return None
+        if pad:
+            ws.append(ws[0].new_zeros(pad, ws[0].shape[1]))
+        has_bias = [m.bias is not None for m in mods]
+        bias = None
+        if any(has_bias):
+            bs = [m.bias if m.bias is not None else ws[0].new_zeros(o) for m, o in zip(mods, outs)]
+            if pad:
+                bs.append(ws[0].new_zeros(pad))
+            bias = torch.cat(bs)
+        y = F.linear(x, torch.cat(ws), bias)
+        # split, not slicing: its backward writes the one [B, L, R] gradient with a
+        # single concatenation (a slice's backward zero-fills a full-size gradient
+        # per slice and then sums them)
+        return list(torch.split(y, outs + ([pad] if pad else []), dim=-1))[:len(outs)]
+
     def forward(self, hidden_states: torch.Tensor, past_state: StateLike = None,
                 attention_mask: Optional[torch.Tensor] = None, use_cache: bool = False,
                 position_embeddings: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, **kwargs: Any):
         B, L, _ = hidden_states.shape
-        Q = self.q_proj(hidden_states).view(B, L, self.num_heads, self.head_dim).transpose(1, 2)
-        K = self.k_proj(hidden_states).view(B, L, self.num_key_value_heads, self.head_dim).transpose(1, 2)
-        V = self.v_proj(hidden_states).view(B, L, self.num_key_value_heads, self.head_dim).transpose(1, 2)
+        fused = self._fused_projections(hidden_states)
+        if fused is not None:
+            q, k, v = fused[:3]
+            gate_lin = fused[3] if len(fused) > 3 else None
+        else:
+            q, k, v = self.q_proj(hidden_states), self.k_proj(hidden_states), self.v_proj(hidden_states)
+            gate_lin = None
+        Q = q.view(B, L, self.num_heads, self.head_dim).transpose(1, 2)
+        K = k.view(B, L, self.num_key_value_heads, self.head_dim).transpose(1, 2)
+        V = v.view(B, L, self.num_key_value_heads, self.head_dim).transpose(1, 2)
         if position_embeddings is not None:
             cos, sin = position_embeddings
             Q, K = apply_rotary_pos_emb(Q, K, cos, sin)
@@ -411,7 +455,7 @@ class SubQLinearAttention(nn.Module):
         # query head h reads K/V head h // groups, and the backward sums dK, dV
         # over each group (the reference's repeat_interleave, autograd.py:746-748)
         if self.use_data_dependent_gating and self.gate_proj is not None:
-            gate = self.gate_proj(hidden_states).transpose(1, 2)
+            gate = (gate_lin if gate_lin is not None else self.gate_proj(hidden_states)).transpose(1, 2)
             decay_w = self.raw_decay.view(1, self.num_heads, 1) + gate
         else:
             decay_w = self.raw_decay

@@ -1,10 +1,16 @@
-"""The per-head RMSNorm kernels (csrc/head_norm.cu, subq_head_rmsnorm_fwd /
-_bwd) against torch's float32 RMSNorm and its autograd: the reference's
-SubQLinearAttention epilogue, nn.RMSNorm(head_dim, eps=1e-5) then the
-transpose copy to [B, L, H*D] (reference python/subq_audio/autograd.py:706-710,
-763-769). Tolerances: 1e-5 of max |ref| for float32, 1e-2 for 16-bit outputs
-(one rounding of the output); dweight in float32 at 1e-4 (sums over up to
-10^5 rows in another order).
+"""The module's prologue and epilogue around the scan.
+
+Epilogue: the per-head RMSNorm kernels (csrc/head_norm.cu,
+subq_head_rmsnorm_fwd / _bwd) against torch's float32 RMSNorm and its
+autograd: the reference's SubQLinearAttention epilogue, nn.RMSNorm(head_dim,
+eps=1e-5) then the transpose copy to [B, L, H*D] (reference
+python/subq_audio/autograd.py:706-710, 763-769). Tolerances: 1e-5 of max |ref|
+for float32, 1e-2 for 16-bit outputs (one rounding of the output); dweight in
+float32 at 1e-4 (sums over up to 10^5 rows in another order).
+
+Prologue: q, k, v and the gate from one GEMM over the concatenated weights
+against the four nn.Linear calls of the reference (autograd.py:735-751):
+outputs and every gradient, with bias, GQA and without gating.
 """
 import ctypes
 
@@ -147,3 +153,34 @@ def test_module_epilogue_equals_torch_epilogue(dtype, monkeypatch):
     assert rel(y_k, y_t) < tol
     for a, b in zip(g_k, g_t):
         assert rel(a, b) < tol
+
+
+@pytest.mark.parametrize("bias,kv_heads,gating,dtype", [(False, 4, True, torch.bfloat16),
+                                                        (True, 2, True, torch.float32),
+                                                        (True, 4, False, torch.bfloat16),
+                                                        (False, 1, True, torch.float32)])
+def test_fused_projections_equal_separate_linears(bias, kv_heads, gating, dtype, monkeypatch):
+    torch.manual_seed(4)
+    mod = SubQLinearAttention(256, num_heads=4, num_key_value_heads=kv_heads, bias=bias,
+                              use_data_dependent_gating=gating).cuda()
+    x = torch.randn(2, 500, 256, device="cuda", requires_grad=True)
+    assert mod._fused_projections(x) is not None
+
+    def run():
+        for p in mod.parameters():
+            p.grad = None
+        x.grad = None
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=dtype == torch.bfloat16):
+            y, _ = mod(x)
+        y.float().square().mean().backward()
+        return y.detach().float(), {n: p.grad.clone() for n, p in mod.named_parameters()}, x.grad.clone()
+
+    y_f, g_f, dx_f = run()
+    monkeypatch.setattr(SubQLinearAttention, "_fused_projections", lambda self, h: None)
+    y_s, g_s, dx_s = run()
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert rel(y_f, y_s) < tol
+    assert rel(dx_f, dx_s) < tol
+    assert g_f.keys() == g_s.keys()
+    for n in g_f:
+        assert rel(g_f[n], g_s[n]) < tol, n
