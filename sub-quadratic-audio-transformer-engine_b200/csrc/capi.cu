@@ -277,8 +277,7 @@ int subq_fwd(const subq_fwd_args* a) {
         const size_t need = subq::chunk_fwd_workspace_bytes(p);
         if ((rc = check_workspace(a->workspace, a->workspace_bytes, need))) return rc;
         p.ws = static_cast<float*>(a->workspace);
-        err = subq::launch_fwd_chunk(p, a->desc.dtype, st);
-        launches = 2;
+        err = subq::launch_fwd_chunk(p, a->desc.dtype, st, &launches);
     } else {
         err = subq::launch_fwd_exact(p, a->desc.dtype, st);
         launches = 1;

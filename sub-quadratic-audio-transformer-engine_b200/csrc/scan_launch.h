@@ -25,7 +25,9 @@ cudaError_t launch_group_sum(const void* src, void* dst, int dtype, int B, int H
 constexpr int kChunkMinTokens = 64;
 bool chunk_fwd_usable(const ScanParams& p, int dtype);
 size_t chunk_fwd_workspace_bytes(const ScanParams& p);
-cudaError_t launch_fwd_chunk(const ScanParams& p, int dtype, cudaStream_t st);  // 2 launches
+// Returns the number of kernel launches issued through *launches (2, or 4 in
+// the chunk-parallel form for calls with few sequences).
+cudaError_t launch_fwd_chunk(const ScanParams& p, int dtype, cudaStream_t st, int* launches);
 
 // Per-head RMSNorm of the scan's output (head_norm.cu). Rows are the
 // (b, n, h) of [B, H, N, D] views with element strides; D contiguous.

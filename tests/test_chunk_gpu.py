@@ -33,6 +33,10 @@ CASES = [
     (1, 2, 190, 200, 3, torch.float32, "none", True, False, True),
     (2, 2, 333, 32, 32, torch.bfloat16, "token", True, True, True),
     (1, 2, 150, 96, 80, torch.float16, "head", False, True, False),
+    # enough sequences x columns for the sequential chunk walk (the rows above take
+    # the chunk-parallel form: scores, state, prefix, outputs)
+    (4, 8, 200, 64, 64, torch.float32, "token", True, True, True),
+    (2, 20, 130, 32, 48, torch.float32, "scalar", False, True, False),
 ]
 
 
@@ -70,6 +74,17 @@ def test_chunked_forward_matches_exact_kernel(case):
     torch.testing.assert_close(S_c, S_x, rtol=1e-4, atol=1e-4 * S_x.abs().max().item())
     if z_x is not None:
         torch.testing.assert_close(z_c, z_x, rtol=1e-5, atol=1e-5 * z_x.abs().max().item())
+
+
+def test_both_forms_launch_counts():
+    from subq_audio import _capi
+
+    q = torch.randn(1, 2, 300, 32, device="cuda")
+    ops.scan_forward(q, q, q, path="chunked")
+    assert _capi.last_launches() == 4  # scores, state, prefix, outputs
+    q = torch.randn(4, 8, 300, 64, device="cuda")
+    ops.scan_forward(q, q, q, path="chunked")
+    assert _capi.last_launches() == 2  # scores, sequential walk
 
 
 def test_automatic_path_choice():
