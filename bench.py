@@ -40,6 +40,9 @@ init and seeded N(0,1) frames; under torchrun the model is wrapped in DDP
       N=1024, D=256 float32 U[0,1), decay 0.99, through the numpy API (host
       buffers) and forward_raw (device buffers); --impl reference times the
       reference's own C++ engine (CPU build) on the same call
+  python bench.py --workload headnorm the module's per-head RMSNorm epilogue
+      (subq_head_rmsnorm_fwd + _bwd with dweight) at the encoder layer's shape:
+      [B=4, H=12, N=16384, D=64] bf16 in the projections' [B, N, H, D] memory
 """
 from __future__ import annotations
 
@@ -72,7 +75,7 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--path", default="auto", choices=["auto", "exact", "tensorcore"])
-    p.add_argument("--workload", default="scan", choices=["scan", "encoder", "stream", "engine"])
+    p.add_argument("--workload", default="scan", choices=["scan", "encoder", "stream", "engine", "headnorm"])
     p.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                    help="scan workload: weak = the full batch on every rank; strong = the B=8 batch split "
                         "over the ranks (one slice each)")
@@ -99,6 +102,41 @@ def _device_timer(fn, steps, warmup):
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps, clocks_summary(sampler)
+
+
+def headnorm_main(args):
+    """The per-head RMSNorm kernels at the encoder layer's shape; one step =
+    forward + backward (with dweight). Algorithmic bytes: the forward reads x
+    and writes y, the backward reads x and dy and writes dx (5 x 100.7 MB)."""
+    import torch
+
+    from subq_audio import ops
+
+    B, H, N, D = 4, 12, 16384, 64
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(B, N, H, D, device="cuda", dtype=torch.bfloat16, generator=g).transpose(1, 2)
+    dy = torch.randn(B, N, H, D, device="cuda", dtype=torch.bfloat16, generator=g).transpose(1, 2)
+    w = torch.rand(D, device="cuda", generator=g) + 0.5
+
+    def step():
+        ops.head_rmsnorm(x, w)
+        ops.head_rmsnorm_backward(dy, x, w)
+
+    ms, clk = _device_timer(step, max(3, args.steps), max(3, args.warmup))
+    nbytes = 5 * x.numel() * x.element_size()
+    peak, _, peak_kind = peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "head RMSNorm fwd+bwd rows/s (B=4,H=12,N=16384,D=64 bf16)", "value": B * H * N / (ms / 1e3),
+        "unit": "rows/s", "n_gpus": 1, "steps": max(3, args.steps), "warmup": max(3, args.warmup),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "subq_head_rmsnorm_fwd + _bwd (dweight), [4, 12, 16384, 64] bf16, [B, N, H, D] memory",
+                   "l2": "503 MB moved per step, above the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": gbs / peak},
+        "gpu_launches": 3 * max(3, args.steps), "clocks": clk}))
+    return 0
 
 
 def stream_main(args):
@@ -493,6 +531,13 @@ def main():
 
     if args.workload == "engine":
         return engine_main(args) if rank == 0 else 0
+    if args.workload == "headnorm":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the RMSNorm epilogue is timed on the GPU "
+                                  "path only; the reference arm times the scan and engine workloads"}))
+            return 0
+        return headnorm_main(args) if rank == 0 else 0
     if args.workload == "stream":
         if args.impl == "reference":
             if rank == 0:

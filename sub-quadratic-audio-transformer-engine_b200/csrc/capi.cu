@@ -389,6 +389,13 @@ static int fill_rms(const subq_rmsnorm_args* a, subq::RmsParams& p, bool bwd) {
         p.dx = a->dx.data; p.dx_sb = a->dx.stride_b; p.dx_sh = a->dx.stride_h; p.dx_sn = a->dx.stride_n;
         p.dw = a->dweight;
     }
+    // dense (b, n, h) row order: row r at element r * D
+    const int64_t D = p.D, H = p.H, N = p.N;
+    auto dense = [&](const subq_tensor4& t) {
+        return t.stride_h == D && t.stride_n == H * D && (t.stride_b == N * H * D || p.B == 1);
+    };
+    p.dense = (dense(a->x) ? 1 : 0) | (!bwd && dense(a->y) ? 2 : 0) | (bwd && dense(a->dy) ? 4 : 0) |
+              (bwd && dense(a->dx) ? 8 : 0);
     return SUBQ_OK;
 }
 

@@ -87,8 +87,11 @@ __device__ __forceinline__ float row_sum(float v) {
     return v;
 }
 
-// Row r of the (b, n, h) walk -> element offset under strides (sb, sh, sn).
-__device__ __forceinline__ int64_t row_off(const RmsParams& p, int64_t r, int64_t sb, int64_t sh, int64_t sn) {
+// Row r of the (b, n, h) walk -> element offset under strides (sb, sh, sn);
+// r * D for a tensor dense in that order (bit `t` of p.dense).
+__device__ __forceinline__ int64_t row_off(const RmsParams& p, int64_t r, int64_t sb, int64_t sh, int64_t sn,
+                                           int t) {
+    if (p.dense & (1 << t)) return r * p.D;
     const int h = (int)(r % p.H);
     const int64_t bn = r / p.H;
     const int n = (int)(bn % p.N);
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(kThreads) rms_fwd_kernel(RmsParams p) {
         const int64_t r = r0 + (threadIdx.x & 31) / TPR;
         const bool live = r < rows;
         float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (live) Vec8<T>::load(x + row_off(p, r, p.x_sb, p.x_sh, p.x_sn) + li * 8, f);
+        if (live) Vec8<T>::load(x + row_off(p, r, p.x_sb, p.x_sh, p.x_sn, 0) + li * 8, f);
         float ss = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
@@ -120,7 +123,7 @@ __global__ void __launch_bounds__(kThreads) rms_fwd_kernel(RmsParams p) {
         const float rs = rsqrtf(ss * (1.f / D) + p.eps);
 #pragma unroll
         for (int i = 0; i < 8; ++i) f[i] = f[i] * rs * w[i];
-        if (live) Vec8<T>::store(y + row_off(p, r, p.y_sb, p.y_sh, p.y_sn) + li * 8, f);
+        if (live) Vec8<T>::store(y + row_off(p, r, p.y_sb, p.y_sh, p.y_sn, 1) + li * 8, f);
     }
 }
 
@@ -146,8 +149,8 @@ __global__ void __launch_bounds__(kThreads) rms_bwd_kernel(RmsParams p) {
         float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (live) {
-            Vec8<T>::load(x + row_off(p, r, p.x_sb, p.x_sh, p.x_sn) + li * 8, f);
-            Vec8<T>::load(dy + row_off(p, r, p.dy_sb, p.dy_sh, p.dy_sn) + li * 8, g);
+            Vec8<T>::load(x + row_off(p, r, p.x_sb, p.x_sh, p.x_sn, 0) + li * 8, f);
+            Vec8<T>::load(dy + row_off(p, r, p.dy_sb, p.dy_sh, p.dy_sn, 2) + li * 8, g);
         }
         float ss = 0.f;
 #pragma unroll
@@ -166,7 +169,7 @@ __global__ void __launch_bounds__(kThreads) rms_bwd_kernel(RmsParams p) {
         dot = row_sum<TPR>(dot) * (1.f / D);
 #pragma unroll
         for (int i = 0; i < 8; ++i) g[i] = rs * (g[i] - f[i] * dot);
-        if (live) Vec8<T>::store(dx + row_off(p, r, p.dx_sb, p.dx_sh, p.dx_sn) + li * 8, g);
+        if (live) Vec8<T>::store(dx + row_off(p, r, p.dx_sb, p.dx_sh, p.dx_sn, 3) + li * 8, g);
     }
     // dw over the CTA: thread group li of each row slot, summed in slot order
     __shared__ float red[kThreads * 8];
@@ -187,6 +190,7 @@ __global__ void __launch_bounds__(1024) rms_dw_kernel(const float* part, int nb,
     __shared__ float red[1024];
     const int c = threadIdx.x % D, k = threadIdx.x / D, K = blockDim.x / D;
     float s = 0.f;
+#pragma unroll 8
     for (int b = k; b < nb; b += K) s += part[(int64_t)b * D + c];
     red[threadIdx.x] = s;
     __syncthreads();

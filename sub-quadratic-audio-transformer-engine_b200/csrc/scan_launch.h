@@ -41,6 +41,9 @@ struct RmsParams {
     const float* w;                              // [D] or null (weight 1)
     float* dw;                                   // backward: [D] or null
     float* part;                                 // backward: [rms_blocks][D] CTA partials of dw
+    // bit t set: tensor t (x, y, dy, dx) is dense in (b, n, h) row order
+    // (strides N*H*D, D, H*D), so row r starts at element r * D
+    int dense;
 };
 constexpr int kRmsMaxBlocks = 148 * 8;
 bool rms_supported_dim(int D);
