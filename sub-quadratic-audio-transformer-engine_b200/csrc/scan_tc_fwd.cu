@@ -45,6 +45,7 @@ constexpr int kStages = 3;
 constexpr int kFwdThreads = 448;
 constexpr int kComputeThreads = 256, kTransformThreads = 128;
 constexpr int kBarCompute = 1, kBarTransform = 2;  // named barrier ids
+constexpr int kBarQuad = 3;  // 3..6: the two compute warps of TMEM lane quadrant q (64 threads)
 constexpr int kWarpProducer = 12, kWarpMma = 13;
 constexpr int kNX = 80;  // state / output MMA width: 64 value columns + 16 normaliser columns
 
@@ -135,8 +136,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
     if (tid == 0) {
         // with decay a stage is released by the tensor core (its operands read)
         // and by the compute warps (its decay scalars read)
-        for (int i = 0; i < B_COUNT; ++i)
-            tc::mbar_init(&bars[i], (kDecay && i >= B_EMPTY && i < B_EMPTY + kStages) ? 2 : 1);
+        // the compute warps signal P, O' and the state operand consumed one arrival
+        // per warp (8), each after its own TMEM or shared-memory work
+        for (int i = 0; i < B_COUNT; ++i) {
+            const bool per_warp = (i >= B_PSDONE && i < B_PSDONE + 2) || (i >= B_ODONE && i < B_ODONE + 2) ||
+                                  i == B_SBDONE;
+            tc::mbar_init(&bars[i], per_warp ? 8 : (kDecay && i >= B_EMPTY && i < B_EMPTY + kStages) ? 2 : 1);
+        }
         tc::fence_mbar_init();
     }
     if (warp == kWarpMma) tc::tmem_alloc(tslot, kTmemCols);
@@ -601,13 +607,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                     packed[x] = *reinterpret_cast<uint32_t*>(&h2);
                 }
             }
+            // the packed half of warp (quad, 1) lands in columns that warp (quad, 0)
+            // reads as fp32: the two warps of a lane quadrant meet first
             tc::tc_fence_before();
-            tc::bar_sync(kBarCompute, kComputeThreads);  // every fp32 read of P[b] is done
+            tc::bar_sync(kBarQuad + quad, 64);
             tc::tc_fence_after();
             tc::tmem_st32_raw(tmem + cP + bf * 128 + loff + hf * 32, packed);
             tc::tc_fence_before();
-            tc::bar_sync(kBarCompute, kComputeThreads);
-            if (tid == 0) tc::mbar_arrive(&bars[B_PSDONE + bf]);
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars[B_PSDONE + bf]);
             return true;
         };
         // decay: bf16 f [S | z] (registers v, z) into the operand buffer `dst`
@@ -667,11 +675,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
                 if (i + 1 < n) write_operand(sm + L::sb + ((i + 1) & 1) * L::sbuf, exp2_fast(dec[2 * s1]));
                 tc::fence_proxy_async();
                 tc::tc_fence_before();
-                tc::bar_sync(kBarCompute, kComputeThreads);
-                if (tid == 0) {
-                    tc::mbar_arrive(&bars[B_SBDONE]);
-                    tc::mbar_arrive(&bars[B_EMPTY + s]);
-                }
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&bars[B_SBDONE]);
+                tc::bar_sync(kBarCompute, kComputeThreads);  // every read of the stage's decay scalars
+                if (tid == 0) tc::mbar_arrive(&bars[B_EMPTY + s]);
             } else {
             {
                 uint8_t* sbn = sm + L::sb + ((i + 1) & 1) * L::sbuf;
@@ -692,10 +699,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             }
             tc::fence_proxy_async();
             tc::tc_fence_before();
-            tc::bar_sync(kBarCompute, kComputeThreads);
-            if (tid == 0) {
-                tc::mbar_arrive(&bars[B_SBDONE]);
-                if (P.chunks && i + 1 < n) {  // the next chunk's state operand to the handover
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars[B_SBDONE]);
+            if (P.chunks && i + 1 < n) {  // the next chunk's state operand to the handover
+                tc::bar_sync(kBarCompute, kComputeThreads);
+                if (tid == 0) {
                     tc::bulk_store(chunk_slot(c + 1), sm + L::sb + ((i + 1) & 1) * L::sbuf, kSAtom);
                     tc::bulk_commit();
                 }
@@ -714,9 +722,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fwd_kernel(const __grid_consta
             float zi = 0.f;
             if (kNorm) zi = tmem_ld1(tmem + cO + bf * kNX + loff + 64);
             tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars[B_ODONE + bf]);  // this warp has read O'[bf]
             if (tid == 0) tc::bulk_wait_read0();  // the previous chunk's output has left the staging tile
             tc::bar_sync(kBarCompute, kComputeThreads);
-            if (tid == 0) tc::mbar_arrive(&bars[B_ODONE + bf]);  // every thread has read O'[bf]
             {
                 // O' and its normaliser column carry phi(q) unscaled: o = s O' / max(s Z', clamp)
                 float inv = (mr_row != 0 ? 1.f : 0.f) * p.scale;
