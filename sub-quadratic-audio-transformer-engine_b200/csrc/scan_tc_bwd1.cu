@@ -161,7 +161,13 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
     const uint32_t sbase = tc::smem_u32(sm);
 
     if (tid == 0) {
-        for (int i = 0; i < F_COUNT; ++i) tc::mbar_init(&bars[i], 1);
+        // the compute warps' signals take one arrival per warp (8), each after that
+        // warp's own shared-memory or TMEM work
+        for (int i = 0; i < F_COUNT; ++i) {
+            const bool per_warp = i == F_OC || i == F_OC + 1 || i == F_OUT || i == F_OUT + 1 || i == F_MDONEA ||
+                                  i == F_DSB || i == F_EPI;
+            tc::mbar_init(&bars[i], per_warp ? 8 : 1);
+        }
         tc::fence_mbar_init();
     }
     if (warp == kWarpMma) tc::tmem_alloc(tslot, kTmemCols);
@@ -409,11 +415,13 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
         const int quad = warp & 3, hf = warp >> 2;
         const int row = quad * 32 + lane, srow = quad * 16 + lane;
         const uint32_t loff = (uint32_t)(quad * 32) << 16;
+        // this warp's shared-memory writes (to the async proxy) and TMEM accesses
+        // are complete: one arrival of the 8 the barrier counts
         auto publish = [&](uint64_t* bar) {
             tc::fence_proxy_async();
             tc::tc_fence_before();
-            tc::bar_sync(kBarCompute, kComputeThreads);
-            if (tid == 0) tc::mbar_arrive(bar);
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(bar);
         };
         auto cwait = [&](uint64_t* bar, uint32_t parity) -> bool {
             ok = tc::bar_and(kBarCompute, kComputeThreads, wait_bar(bar, parity, P.status)) && ok;
@@ -600,8 +608,8 @@ __global__ void __launch_bounds__(kThreads1, 1) bwd1_kernel(const __grid_constan
                 tc::tmem_regs_ready<32>(rk);
                 tc::tmem_regs_ready<32>(rq);
                 tc::tc_fence_before();
-                tc::bar_sync(kBarCompute, kComputeThreads);
-                if (tid == 0) tc::mbar_arrive(&bars[F_EPI]);  // the accumulators' columns are free
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&bars[F_EPI]);  // this warp's accumulator rows are read
                 // dv = s m dV over the v tile; dk = s m dK~ phi'(k) over the k^ tile; dq =
                 // s dQ~ phi'(q) over the o^ tile (phi' = min(phi, 1)), 8 columns at a time
 #pragma unroll
