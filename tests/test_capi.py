@@ -168,3 +168,84 @@ def test_product_has_no_cpu_path():
     q = torch.randn(1, 1, 8, 4)
     with pytest.raises(RuntimeError, match="CUDA"):
         subq_audio.ops.scan_forward(q, q, q)
+
+
+def _rms_args(B=2, H=3, N=5, D=64, dtype=_capi.SUBQ_BF16):
+    a = _capi.RmsArgs()
+    a.batch, a.heads, a.seq_len, a.head_dim, a.dtype, a.eps = B, H, N, D, dtype, 1e-5
+    for i, name in enumerate(("x", "y", "dy", "dx")):
+        t = getattr(a, name)
+        t.data = 0x100000 * (i + 1)
+        t.stride_b, t.stride_h, t.stride_n = N * H * D, D, H * D  # [B, N, H, D] memory
+    return a
+
+
+def test_rmsnorm_struct_layout_matches_header(tmp_path):
+    src = tmp_path / "rms.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "kernels.hpp"\n'
+        "int main(void){printf(\"%zu %zu %zu %zu %zu\\n\", sizeof(subq_rmsnorm_args),"
+        " offsetof(subq_rmsnorm_args, x), offsetof(subq_rmsnorm_args, weight),"
+        " offsetof(subq_rmsnorm_args, workspace_bytes), offsetof(subq_rmsnorm_args, stream));return 0;}\n")
+    exe = tmp_path / "rms"
+    subprocess.run(["gcc", "-x", "c", "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe)], check=True)
+    got = list(map(int, subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()))
+    R = _capi.RmsArgs
+    assert got == [ctypes.sizeof(R), R.x.offset, R.weight.offset, R.workspace_bytes.offset, R.stream.offset]
+
+
+@pytest.mark.parametrize("change,code,text", [
+    (lambda a: setattr(a, "head_dim", 48), _capi.SUBQ_ERR_UNSUPPORTED, b"head_dim"),
+    (lambda a: setattr(a, "dtype", _capi.SUBQ_FP64), _capi.SUBQ_ERR_INVALID_ARGUMENT, b"float32"),
+    (lambda a: setattr(a, "eps", -1.0), _capi.SUBQ_ERR_INVALID_ARGUMENT, b"eps"),
+    (lambda a: setattr(a.x, "stride_n", 3 * 64 + 4), _capi.SUBQ_ERR_INVALID_ARGUMENT, b"16-byte"),
+    (lambda a: setattr(a.y, "data", 0x100008), _capi.SUBQ_ERR_INVALID_ARGUMENT, b"16-byte"),
+    (lambda a: setattr(a.x, "data", 0), _capi.SUBQ_ERR_INVALID_ARGUMENT, b"null"),
+    (lambda a: setattr(a, "seq_len", -1), _capi.SUBQ_ERR_INVALID_ARGUMENT, b"negative"),
+])
+def test_rmsnorm_rejects_bad_arguments_before_the_gpu(change, code, text):
+    lib = _capi.load()
+    a = _rms_args()
+    change(a)
+    assert lib.subq_head_rmsnorm_fwd(ctypes.byref(a)) == code
+    assert text in lib.subq_last_error()
+    assert lib.subq_head_rmsnorm_fwd(None) == _capi.SUBQ_ERR_INVALID_ARGUMENT
+
+
+def test_rmsnorm_backward_workspace_is_the_cta_partials():
+    """dweight needs one D-float partial per CTA: min(ceil(rows / (256 / (D / 8))), 1184) of them,
+    rounded up to 256 bytes; no workspace without dweight."""
+    lib = _capi.load()
+    for B, H, N, D in [(2, 3, 5, 64), (4, 12, 16384, 64), (1, 1, 1, 8), (1, 2, 700, 256)]:
+        a = _rms_args(B, H, N, D)
+        assert lib.subq_head_rmsnorm_bwd_workspace_bytes(ctypes.byref(a)) == 0
+        a.dweight = 0x900000
+        rows, rpb = B * H * N, 256 // (D // 8)
+        blocks = min(-(-rows // rpb), 148 * 8)
+        want = -(-blocks * D * 4 // 256) * 256
+        assert lib.subq_head_rmsnorm_bwd_workspace_bytes(ctypes.byref(a)) == want
+
+
+def test_chunked_forward_workspace_and_path_choice():
+    """float32 calls of 64 tokens or more take the chunked forward under AUTO:
+    per 64-token chunk and sequence a block of 17,152 + 512 (round32(d) + 4)
+    bytes, the normaliser copy, and in the chunk-parallel form (few sequences)
+    d (e + 1) floats of chunk states; shorter calls run on the exact path with
+    no workspace; an explicit CHUNKED request the path cannot take is refused."""
+    lib = _capi.load()
+
+    def ws(B, H, N, d, e, path=_capi.SUBQ_PATH_AUTO, dtype=_capi.SUBQ_FP32):
+        a = _fwd_args(B, H, N, d, e, dtype)
+        a.desc.path = path
+        return lib.subq_fwd_workspace_bytes(ctypes.byref(a))
+
+    block = lambda d: 17152 + 512 * ((d + 31) // 32 * 32 + 4)  # noqa: E731
+    zcopy = lambda B, H, d: -(-B * H * d * 4 // 16) * 16  # noqa: E731
+    assert ws(1, 1, 640, 64, 64) == 10 * block(64) + zcopy(1, 1, 64) + 10 * 64 * 65 * 4   # chunk-parallel
+    assert ws(4, 8, 640, 64, 64) == 32 * 10 * block(64) + zcopy(4, 8, 64)                 # sequential walk
+    assert ws(1, 1, 63, 64, 64) == 0                                                      # exact path
+    assert ws(1, 1, 63, 64, 64, path=_capi.SUBQ_PATH_CHUNKED) == block(64) + zcopy(1, 1, 64) + 64 * 65 * 4
+    a = _fwd_args(1, 1, 100, 8, 8, _capi.SUBQ_FP64)
+    a.desc.path = _capi.SUBQ_PATH_CHUNKED
+    assert lib.subq_fwd(ctypes.byref(a)) == _capi.SUBQ_ERR_UNSUPPORTED
+    assert b"chunked" in lib.subq_last_error()
