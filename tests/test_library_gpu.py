@@ -91,3 +91,16 @@ def test_layer_traces_with_fullgraph(causal):
     torch.testing.assert_close(out, ref)
     for a, b in zip([p.grad for p in layer.parameters()] + [x.grad], ref_grads):
         torch.testing.assert_close(a, b)
+
+
+@pytest.mark.parametrize("with_weight", [True, False])
+def test_head_rmsnorm_operators_opcheck(with_weight):
+    """The epilogue operators' schemas and fake kernels: output shapes, dtypes
+    and strides ([B, N, H, D] memory for y, x's order for dx) as the real ones."""
+    x = torch.randn(2, 300, 4, 64, device="cuda", dtype=torch.bfloat16).transpose(1, 2)
+    dy = torch.randn(2, 300, 4, 64, device="cuda", dtype=torch.bfloat16).transpose(1, 2)
+    w = (torch.rand(64, device="cuda") + 0.5) if with_weight else None
+    torch.library.opcheck(torch.ops.subq_audio.head_rmsnorm_fwd.default, (x, w, 1e-5),
+                          test_utils=("test_schema", "test_faketensor"))
+    torch.library.opcheck(torch.ops.subq_audio.head_rmsnorm_bwd.default, (dy, x, w, 1e-5),
+                          test_utils=("test_schema", "test_faketensor"))
