@@ -14,7 +14,7 @@
 // which is the recurrence of the reference (src/kernels/attention_forward.cpp:42-58,
 // python/subq_audio/autograd.py:108-169 and :292-376) regrouped by chunk.
 //
-// chunk_scores_kernel (one CTA per chunk, every chunk at once) writes a block
+// chunk_scores_kernel (three CTAs per chunk, every chunk at once) writes a block
 // per chunk into the workspace: A (row stride 65), L (float64: differences of
 // two prefix sums keep their precision), and q~, k~ in padded rows.
 // chunk_scan_kernel then walks the chunks of one sequence for kET value
@@ -66,52 +66,63 @@ __device__ __forceinline__ double chunk_lg(const ScanParams& p, int b, int h, in
     return lg < -1e4f ? -1e4 : (double)lg;
 }
 
-// One CTA per chunk: q~, k~ staged (and written out), L by a warp scan, then
-// A with thread (ty, tx) forming A[ty + 16 a][tx + 16 c] for a, c < 4.
+// Three CTAs per chunk (blockIdx.x = 3 chunk + quadrant; y = head, z = batch):
+// the causal 64 x 64 block A is
+// three 32 x 32 quadrants, (t, tau) in (lo, lo), (hi, lo) and (hi, hi); the
+// fourth, (lo, hi), is zero. A CTA stages the 32 rows of q~ and of k~ its
+// quadrant needs and forms its 32 x 32 outputs (thread (ty, tx) rows ty, ty + 16
+// and columns tx, tx + 16). Quadrant (lo, lo) writes L, the zero quadrant and
+// rows 0-31 of q~ and k~; quadrant (hi, hi) writes rows 32-63 of both.
+constexpr int kHalf = kCh / 2;
 template <typename T>
 __global__ void __launch_bounds__(kCThreads) chunk_scores_kernel(ScanParams p, int nCh) {
-    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int c = blockIdx.x / 3, quad = blockIdx.x - 3 * c, h = blockIdx.y, b = blockIdx.z;
+    const int64_t bh = (int64_t)b * p.H + h;
+    const int t_lo = quad == 0 ? 0 : kHalf, tau_lo = quad == 2 ? kHalf : 0;
+    const bool write_q = quad != 1, write_k = quad != 1;  // rows t_lo.. of q~, tau_lo.. of k~
     const int d = p.d, DP = row_stride(d);
     extern __shared__ __align__(16) float smc[];
-    float* qs = smc;
-    float* ks = qs + kCh * DP;
-    double* Ls = reinterpret_cast<double*>(ks + kCh * DP);
+    float* qs = smc;                 // [32][DP]: rows t_lo + r
+    float* ks = qs + kHalf * DP;     // [32][DP]: rows tau_lo + r
+    double* Ls = reinterpret_cast<double*>(ks + kHalf * DP);  // [64]
     const int t0 = c * kCh;
-    unsigned char* blk = reinterpret_cast<unsigned char*>(p.ws) + ((int64_t)(b * p.H + h) * nCh + c) * block_bytes(d);
+    unsigned char* blk = reinterpret_cast<unsigned char*>(p.ws) + (bh * nCh + c) * block_bytes(d);
     float* out_a = reinterpret_cast<float*>(blk);
     double* out_l = reinterpret_cast<double*>(blk + kABytes);
     float* out_q = reinterpret_cast<float*>(blk + kABytes + kLBytes);
     float* out_k = out_q + kCh * DP;
 
-    if (c == 0 && p.normalize) {
-        const int64_t bh = (int64_t)b * p.H + h;
+    if (c == 0 && quad == 0 && p.normalize) {
         float* zc = z_copy(p, nCh) + bh * d;
         for (int i = threadIdx.x; i < d; i += blockDim.x) zc[i] = p.z_in ? p.z_in[bh * d + i] : 0.f;
     }
     const T* qb = (const T*)p.q + b * p.q_sb + h * p.q_sh;
     const T* kb = (const T*)p.k + b * p.k_sb + (h / p.kvg) * p.k_sh;
     // four elements per thread and step, their loads issued before any use
-    for (int x0 = threadIdx.x; x0 < kCh * DP; x0 += 4 * kCThreads) {
+    for (int x0 = threadIdx.x; x0 < kHalf * DP; x0 += 4 * kCThreads) {
         float qr[4], kr[4], mr[4];
-        bool in[4];
+        bool inq[4], ink[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const int x = x0 + u * kCThreads, tt = x / DP, i = x - tt * DP, t = t0 + tt;
-            in[u] = x < kCh * DP && i < d && t < p.N;
-            qr[u] = in[u] ? to_f<T>(qb[(int64_t)t * p.q_sn + i]) : 0.f;
-            kr[u] = in[u] ? to_f<T>(kb[(int64_t)t * p.k_sn + i]) : 0.f;
-            mr[u] = in[u] ? token_mask(p, b, t) : 0.f;
+            const int x = x0 + u * kCThreads, rr = x / DP, i = x - rr * DP;
+            const int tq = t0 + t_lo + rr, tk = t0 + tau_lo + rr;
+            const bool inx = x < kHalf * DP && i < d;
+            inq[u] = inx && tq < p.N;
+            ink[u] = inx && tk < p.N;
+            qr[u] = inq[u] ? to_f<T>(qb[(int64_t)tq * p.q_sn + i]) : 0.f;
+            kr[u] = ink[u] ? to_f<T>(kb[(int64_t)tk * p.k_sn + i]) : 0.f;
+            mr[u] = ink[u] ? token_mask(p, b, tk) : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int x = x0 + u * kCThreads;
-            if (x >= kCh * DP) break;
-            const float qf = in[u] ? phi_f(qr[u]) * p.scale : 0.f;  // padding and tokens past N: 0
-            const float kf = in[u] ? phi_f(kr[u]) * mr[u] : 0.f;
+            if (x >= kHalf * DP) break;
+            const float qf = inq[u] ? phi_f(qr[u]) * p.scale : 0.f;  // padding and tokens past N: 0
+            const float kf = ink[u] ? phi_f(kr[u]) * mr[u] : 0.f;
             qs[x] = qf;
             ks[x] = kf;
-            out_q[x] = qf;
-            out_k[x] = kf;
+            if (write_q) out_q[t_lo * DP + x] = qf;
+            if (write_k) out_k[tau_lo * DP + x] = kf;
         }
     }
     if (threadIdx.x < 32) {  // inclusive prefix of log(gamma): lane l owns tokens 2l, 2l + 1
@@ -127,42 +138,46 @@ __global__ void __launch_bounds__(kCThreads) chunk_scores_kernel(ScanParams p, i
         if (l == 0) pre = 0.0;
         Ls[2 * l] = pre + a0;
         Ls[2 * l + 1] = s;
-        out_l[2 * l] = pre + a0;
-        out_l[2 * l + 1] = s;
+        if (quad == 0) {
+            out_l[2 * l] = pre + a0;
+            out_l[2 * l + 1] = s;
+        }
     }
     __syncthreads();
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    float acc[4][4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) acc[a][cc] = 0.f;
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
     const int dv = (d + 3) & ~3;
     for (int i = 0; i < dv; i += 4) {
-        float4 q4[4], k4[4];
+        float4 q4[2], k4[2];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) q4[a] = *reinterpret_cast<const float4*>(qs + (ty + 16 * a) * DP + i);
+        for (int a = 0; a < 2; ++a) q4[a] = *reinterpret_cast<const float4*>(qs + (ty + 16 * a) * DP + i);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) k4[cc] = *reinterpret_cast<const float4*>(ks + (tx + 16 * cc) * DP + i);
+        for (int cc = 0; cc < 2; ++cc) k4[cc] = *reinterpret_cast<const float4*>(ks + (tx + 16 * cc) * DP + i);
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < 2; ++a)
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
+            for (int cc = 0; cc < 2; ++cc)
                 acc[a][cc] = fmaf(q4[a].w, k4[cc].w, fmaf(q4[a].z, k4[cc].z,
                              fmaf(q4[a].y, k4[cc].y, fmaf(q4[a].x, k4[cc].x, acc[a][cc]))));
     }
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
-        const int t = ty + 16 * a;
+    for (int a = 0; a < 2; ++a) {
+        const int t = t_lo + ty + 16 * a;
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-            const int tau = tx + 16 * cc;
+        for (int cc = 0; cc < 2; ++cc) {
+            const int tau = tau_lo + tx + 16 * cc;
             float w = 0.f;
             if (tau <= t) w = acc[a][cc] * expf((float)(Ls[t] - Ls[tau]));
             out_a[t * kALd + tau] = w;
         }
     }
-    if (threadIdx.x < kCh) out_a[threadIdx.x * kALd + kCh] = 0.f;  // the pad column
+    if (quad == 0) {  // the zero quadrant (t < 32, tau >= 32) and the pad column of rows 0-31
+        for (int x = threadIdx.x; x < kHalf * kHalf; x += kCThreads)
+            out_a[(x / kHalf) * kALd + kHalf + (x % kHalf)] = 0.f;
+        if (threadIdx.x < kHalf) out_a[threadIdx.x * kALd + kCh] = 0.f;
+    } else if (quad == 2 && threadIdx.x < kHalf) {
+        out_a[(kHalf + threadIdx.x) * kALd + kCh] = 0.f;  // the pad column of rows 32-63
+    }
 }
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -515,7 +530,7 @@ size_t out_smem(int d) {
 // The parallel form when the sequential walk would fill less than two waves.
 bool chunk_parallel(const ScanParams& p) { return (int64_t)((p.e + kET - 1) / kET) * p.B * p.H < 2 * 148; }
 
-size_t scores_smem(int d) { return sizeof(float) * 2 * kCh * row_stride(d) + sizeof(double) * kCh; }
+size_t scores_smem(int d) { return sizeof(float) * 2 * kHalf * row_stride(d) + sizeof(double) * kCh; }
 size_t scan_smem(int d) { return block_bytes(d) + sizeof(float) * (kCh * kVW + kCh + kVW * row_stride(d)); }
 
 template <typename T>
@@ -524,7 +539,7 @@ cudaError_t launch_chunk_t(const ScanParams& p, cudaStream_t st, int* launches) 
     auto k1 = chunk_scores_kernel<T>;
     cudaError_t err = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scores_smem(p.d));
     if (err != cudaSuccess) return err;
-    k1<<<dim3(nCh, p.H, p.B), kCThreads, scores_smem(p.d), st>>>(p, nCh);
+    k1<<<dim3(3 * nCh, p.H, p.B), kCThreads, scores_smem(p.d), st>>>(p, nCh);
     if (!chunk_parallel(p)) {
         auto k2 = chunk_scan_kernel<T>;
         err = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scan_smem(p.d));
