@@ -1,6 +1,6 @@
 """Parity of the CUDA scan (through the C ABI) with the float64 oracle.
 
-Metric: max |x - ref| / max |ref| over the tensor (the north-star metric).
+Metric: max |x - ref| / max |ref| over the tensor (max relative error to max |ref|).
 Tolerances: 1e-4 for float32, 1e-10 for float64 (exact path), 2e-2 for
 bfloat16/float16 (tensor-core path and exact path on 16-bit inputs); the
 oracle runs on the 16-bit-rounded inputs in float64.
