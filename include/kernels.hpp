@@ -81,7 +81,8 @@ typedef enum subq_decay_mode {
 /* Which kernel family a call may use. AUTO picks the tensor-core path when
  * the shape allows it (bf16/fp16, d = e = 64; with per-token decay bf16
  * only); otherwise the chunk-parallel float32 forward for calls of at least
- * 64 tokens (d <= 256, forward time, scalar gamma <= 1), and the exact
+ * 64 tokens (d <= 256, forward time, scalar gamma <= 1, at most 4 GiB of
+ * workspace), and the exact
  * float32 path for the rest. Calls of at most 16 tokens (streaming decode
  * steps) take the exact, token-recurrent path, which is faster there. The
  * backward has no chunked variant: CHUNKED runs it on the exact path. */

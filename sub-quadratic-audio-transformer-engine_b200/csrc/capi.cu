@@ -98,10 +98,16 @@ bool use_tc_bwd(const subq::ScanParams& p, int dtype, int path) {
     return use_tc(p, dtype, path) && subq::tc_bwd_supported(p, dtype);
 }
 
+// The automatic path takes the chunked forward while its workspace (about
+// 0.8 KB per token-head at d = 64, 2.3 KB at d = 256) stays within this; larger
+// calls run on the exact path, which needs none.
+constexpr size_t kChunkMaxWorkspace = (size_t)4 << 30;
+
 // The forward's kernel family when the tensor cores do not take the call.
 int fwd_simt_path(const subq::ScanParams& p, int dtype, int path) {
     if (path == SUBQ_PATH_CHUNKED) return subq::chunk_fwd_usable(p, dtype) ? SUBQ_PATH_CHUNKED : -1;
-    if (path == SUBQ_PATH_AUTO && p.N >= subq::kChunkMinTokens && subq::chunk_fwd_usable(p, dtype))
+    if (path == SUBQ_PATH_AUTO && p.N >= subq::kChunkMinTokens && subq::chunk_fwd_usable(p, dtype) &&
+        subq::chunk_fwd_workspace_bytes(p) <= kChunkMaxWorkspace)
         return SUBQ_PATH_CHUNKED;
     return SUBQ_PATH_EXACT;
 }

@@ -244,6 +244,7 @@ def test_chunked_forward_workspace_and_path_choice():
     assert ws(1, 1, 640, 64, 64) == 10 * block(64) + zcopy(1, 1, 64) + 10 * 64 * 65 * 4   # chunk-parallel
     assert ws(4, 8, 640, 64, 64) == 32 * 10 * block(64) + zcopy(4, 8, 64)                 # sequential walk
     assert ws(1, 1, 63, 64, 64) == 0                                                      # exact path
+    assert ws(64, 64, 65536, 64, 64) == 0  # over 4 GiB of chunk workspace: the exact path, which needs none
     assert ws(1, 1, 63, 64, 64, path=_capi.SUBQ_PATH_CHUNKED) == block(64) + zcopy(1, 1, 64) + 64 * 65 * 4
     a = _fwd_args(1, 1, 100, 8, 8, _capi.SUBQ_FP64)
     a.desc.path = _capi.SUBQ_PATH_CHUNKED
